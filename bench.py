@@ -1,0 +1,388 @@
+"""CVMM fw+bw benchmark (B200, sm_100a).
+
+One step = the whole CVMM hot path over one batch of the workload:
+cvmm_prepare_sel2 (device radix sort) -> forward gather-GEMM (+ weighted
+combine) -> backward (grad-W, grad-x, sel-weight grad); with N > 1 GPUs each
+rank processes its own tokens (weak scaling) and the fp32 expert-weight
+gradients are summed with an NCCL all-reduce inside the step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Prints one JSON line (rank 0). Timing: CUDA events on the compute stream around
+each step, L2 flushed (256 MiB write) before every timed step and outside the
+events, max over ranks. `e2e` repeats the step through the public API with the
+step's inputs copied from pinned host memory and a scalar read back every
+step. `roofline` covers the kernel with the largest share of the step, timed
+with CUDA events around its launches inside the timed steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "CVMM fw+bw ms/iter & TFLOP/s (% B200 BF16 TC peak), σ-MoE shapes, 1–8 GPU"
+DEFAULT_WORKLOAD = "ff_up_1024"  # BASELINE configs[1]; its metric is quoted on ff_up_1024
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--workload", default=DEFAULT_WORKLOAD)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--also", default="ff_down_1024_weighted",
+                   help="comma-separated extra workloads reported under 'also' (N=1 only)")
+    return p.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            m = json.load(f)
+        return {"hbm_gbs": m["hbm_gbs"], "bf16_tflops": m["bf16_tflops"],
+                "bf16_tflops_sustained": m["bf16_tflops_sustained"], "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ our arm
+def build_step(w, d, world):
+    import torch.distributed as dist
+
+    from cvmm_codex_b200 import cvmm, cvmm_prepare_sel2
+
+    x = d["x"].requires_grad_(True)
+    keys = d["keys"].requires_grad_(True)
+    wt = None if d["weights"] is None else d["weights"].requires_grad_(True)
+
+    def step(sel, grad_out):
+        x.grad = None
+        keys.grad = None
+        if wt is not None:
+            wt.grad = None
+        sel2 = cvmm_prepare_sel2(sel, wt, route_input=w.route_input)
+        if w.amp:
+            with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+                out = cvmm(x, sel2, keys)
+        else:
+            out = cvmm(x, sel2, keys)
+        out.backward(grad_out)
+        if world > 1:
+            dist.all_reduce(keys.grad)
+        return out
+
+    return step
+
+
+def time_steps(step, d, steps, flush, recorder=None):
+    times = []
+    for _ in range(steps):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        if recorder is not None:
+            with recorder:
+                step(d["sel"], d["grad_out"])
+        else:
+            step(d["sel"], d["grad_out"])
+        b.record()
+        times.append((a, b))
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in times)
+
+
+def time_e2e(step, d, steps, flush):
+    """Public-API step with host inputs: H2D of x/sel/grad_out (and weights) from
+    pinned memory, the step, and a D2H read of a scalar result, every step."""
+    host = {k: (None if v is None else v.detach().cpu().pin_memory()) for k, v in d.items() if k != "keys"}
+    dev = {k: (None if v is None else torch.empty_like(v, device="cuda")) for k, v in host.items()}
+    res_h = torch.empty((), dtype=torch.float32).pin_memory()
+    x_param = d["x"]
+    h2d = sum(v.numel() * v.element_size() for v in host.values() if v is not None)
+    total = 0.0
+    for i in range(steps + 1):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for k, v in host.items():
+            if v is not None:
+                dev[k].copy_(v, non_blocking=True)
+        with torch.no_grad():
+            x_param.copy_(dev["x"])
+            if d["weights"] is not None:
+                d["weights"].copy_(dev["weights"])
+        out = step(dev["sel"], dev["grad_out"])
+        res_h.copy_(out.detach()[..., 0].float().sum(), non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        if i > 0:  # first pass warms the pinned buffers
+            total += a.elapsed_time(b)
+    return total / steps, h2d, 4
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch.distributed as dist
+
+    from cvmm_codex_b200 import ops
+    from cvmm_codex_b200.workloads import WORKLOADS, make_inputs
+
+    torch.cuda.set_device(local_rank)
+    pk = peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def measure(name, with_e2e, with_roofline):
+        w = WORKLOADS[name]
+        d = make_inputs(w, "cuda", seed=rank)
+        step = build_step(w, d, world)
+        for _ in range(max(args.warmup, 3)):
+            step(d["sel"], d["grad_out"])
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        rec = ops.Recorder()
+        with ClockSampler(local_rank) as clk:
+            total_ms = time_steps(step, d, args.steps, flush, rec)
+        if world > 1:
+            t = torch.tensor([total_ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            total_ms = t.item()
+        torch.cuda.synchronize()
+        ms = total_ms / args.steps
+        flops = w.flops() * world
+        res = {"w": w, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "clocks": clk.summary(),
+               "launches": rec.launches // args.steps, "per_call": rec.summary()}
+        if with_e2e:
+            e_ms, bi, bo = time_e2e(step, d, max(3, args.steps // 5), flush)
+            if world > 1:
+                t = torch.tensor([e_ms], device="cuda")
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                e_ms = t.item()
+            res["e2e"] = {"value": round(flops / (e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                          "ms_per_step": round(e_ms, 4), "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo}
+        if with_roofline:
+            res["roofline"] = roofline(w, res["per_call"], args.steps, pk)
+        return res
+
+    main = measure(args.workload, not args.no_e2e, True)
+    w = main["w"]
+    line = {
+        "metric": METRIC, "value": round(main["tflops"], 3), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(main["ms"], 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if w.amp else "f32",
+        "data": "synthetic (seeded; shapes of the BASELINE config, inputs generated on device)",
+        "config": {"workload": w.name, "tokens_per_gpu": w.T, "d_in": w.d_in, "d_out": w.d_out,
+                   "experts": w.E, "top_k": w.k, "weighted": w.weighted, "route_input": w.route_input,
+                   "global_tokens": w.T * world, "parallelism": f"token-sharded dp{world}",
+                   "l2": "flushed (256 MiB write) before every timed step",
+                   "flops_per_step_per_gpu": w.flops(),
+                   "pct_bf16_peak_sustained": round(100 * main["tflops"] / world / pk["bf16_tflops_sustained"], 2)},
+        "clocks": main["clocks"],
+        "gpu_launches": main["launches"] * args.steps,
+        "roofline": main["roofline"],
+        "per_call_ms": {k: round(v[1] / max(v[0], 1), 5) for k, v in main["per_call"].items()},
+    }
+    if "e2e" in main:
+        line["e2e"] = main["e2e"]
+    if world == 1 and args.also:
+        also = {}
+        for name in [s for s in args.also.split(",") if s and s != args.workload]:
+            r = measure(name, False, True)
+            also[name] = {"value": round(r["tflops"], 3), "unit": "TFLOP/s", "ms_per_step": round(r["ms"], 4),
+                          "pct_bf16_peak_sustained": round(100 * r["tflops"] / pk["bf16_tflops_sustained"], 2),
+                          "roofline": r["roofline"]}
+        line["also"] = also
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(w, budget_s=10.0)
+    return line
+
+
+GEMM_CALLS = ("cvmm_forward", "cvmm_backward_x", "cvmm_backward_w")
+
+
+def roofline(w, per_call, steps, pk):
+    """Dominant native call of the step; algorithmic FLOPs per launch for the
+    GEMMs (2*R*d_in*d_out), algorithmic bytes for the memory-bound kernels."""
+    name, (calls, total) = max(per_call.items(), key=lambda kv: kv[1][1])
+    avg_ms = total / max(calls, 1)
+    step_total = sum(v[1] for v in per_call.values())
+    share = total / step_total if step_total else None
+    if name in GEMM_CALLS:
+        work = 2.0 * w.R * w.d_in * w.d_out
+        achieved = work / (avg_ms * 1e-3) / 1e12
+        peak = pk["bf16_tflops_sustained"]
+        return {"kernel": name, "bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+                "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
+                "avg_ms": round(avg_ms, 5), "share_of_native_time": round(share, 3) if share else None,
+                "peak_source": pk["source"] + " bf16 sustained"}
+    achieved = 0.0
+    return {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": None, "traffic": None, "avg_ms": round(avg_ms, 5)}
+
+
+# ------------------------------------------------------------------ CPU baseline / reference arm
+def cpu_baseline(w, budget_s: float):
+    """The reference's pure-PyTorch per-expert math on the host cores (fp32),
+    timed on a bounded token sample and scaled to the metric (TFLOP/s)."""
+    sys.path.insert(0, ROOT)
+    from oracle import cpu_baseline as cb
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    n_tok = max(64, min(w.T, 1024))
+    d = cb.make_sample(w, n_tok)
+    cb.step(w, d)  # warm
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        cb.step(w, d)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or reps >= 50:
+            break
+    per = el / reps
+    flops = 3 * 2 * n_tok * w.k * w.d_in * w.d_out
+    return {"value": round(flops / per / 1e12, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{n_tok} of {w.T} tokens of {w.name}, fp32 torch-CPU per-expert fw+bw, "
+                      f"{reps} reps, {per * 1e3:.1f} ms/rep"}
+
+
+def run_reference(args, rank):
+    from cvmm_codex_b200.workloads import WORKLOADS
+
+    if rank != 0:
+        return None
+    w = WORKLOADS[args.workload]
+    sys.path.insert(0, ROOT)
+    from oracle import cpu_baseline as cb
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    n_tok = max(64, min(w.T, 512))
+    d = cb.make_sample(w, n_tok)
+    for _ in range(min(args.warmup, 3)):
+        cb.step(w, d)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cb.step(w, d)
+    per = (time.perf_counter() - t0) / args.steps
+    flops_sample = 3 * 2 * n_tok * w.k * w.d_in * w.d_out
+    tf = flops_sample / per / 1e12
+    full_ms = per * 1e3 * (w.T / n_tok)
+    sample = f"{n_tok} of {w.T} tokens of {w.name} per step (fp32 torch-CPU per-expert fw+bw, the reference's math)"
+    return {
+        "metric": METRIC, "value": round(tf, 5), "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(full_ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, same recipe as our arm)",
+        "config": {"workload": w.name, "tokens_per_gpu": w.T, "d_in": w.d_in, "d_out": w.d_out, "experts": w.E,
+                   "top_k": w.k, "parallelism": "host CPU"},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(tf, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(tf, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    line = run_ours(args, rank, world, local_rank)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,359 @@
+// extern "C" entry points of libcvmm_sm100.so (declared in include/cvmm_sm100.h),
+// argument validation, engine selection and the small memory-bound kernels
+// (weighted combine, top-k sums, token-input weighted backward tail, casts).
+#include <stdio.h>
+#include <string.h>
+
+#include "gemm.cuh"
+#include "launch.h"
+
+namespace cvmm {
+
+static thread_local char t_err[512];
+
+int fail(int code, const char* msg) {
+  snprintf(t_err, sizeof(t_err), "%s", msg);
+  return code;
+}
+
+int fail_cuda(const char* where) {
+  cudaError_t e = cudaGetLastError();
+  snprintf(t_err, sizeof(t_err), "%s: %s", where, cudaGetErrorString(e));
+  return CVMM_ERR_LAUNCH;
+}
+
+int check_launch(const char* where) {
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return CVMM_OK;
+  snprintf(t_err, sizeof(t_err), "%s: %s", where, cudaGetErrorString(e));
+  return CVMM_ERR_LAUNCH;
+}
+
+// ------------------------------------------------------------------ small kernels
+// out[t][n] = sum_j wj * src[t*k + j][n], wj = round(w[t*k+j], src dtype) or 1.
+// Each thread produces 8 consecutive columns; rows are read with 16-byte loads
+// when the layout allows (vec), which is the case for every hot shape.
+__global__ void combine_kernel(const void* __restrict__ src, int s_dtype, const void* __restrict__ w,
+                               int w_dtype, void* __restrict__ out, int o_dtype, int64_t T,
+                               int64_t k, int64_t N, bool vec) {
+  const int64_t groups = (N + 7) / 8;
+  const int64_t total = T * groups;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / groups, n0 = (i % groups) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int64_t j = 0; j < k; ++j) {
+      const int64_t r = t * k + j;
+      const float wj = w ? round_to(load_as_float(w, w_dtype, r), s_dtype) : 1.f;
+      if (vec && s_dtype != F32) {
+        const uint4 q = *reinterpret_cast<const uint4*>(static_cast<const char*>(src) + (r * N + n0) * 2);
+        const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          acc[2 * c] = fmaf(wj, bits_to_float((uint16_t)(wd[c] & 0xffffu), s_dtype), acc[2 * c]);
+          acc[2 * c + 1] = fmaf(wj, bits_to_float((uint16_t)(wd[c] >> 16), s_dtype), acc[2 * c + 1]);
+        }
+      } else {
+        for (int c = 0; c < 8 && n0 + c < N; ++c)
+          acc[c] = fmaf(wj, load_as_float(src, s_dtype, r * N + n0 + c), acc[c]);
+      }
+    }
+    if (vec && o_dtype != F32) {
+      uint32_t wd[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        wd[c] = (uint32_t)float_to_bits(acc[2 * c], o_dtype) |
+                ((uint32_t)float_to_bits(acc[2 * c + 1], o_dtype) << 16);
+      *reinterpret_cast<uint4*>(static_cast<char*>(out) + (t * N + n0) * 2) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+    } else {
+      for (int c = 0; c < 8 && n0 + c < N; ++c) store_from_float(out, o_dtype, t * N + n0 + c, acc[c]);
+    }
+  }
+}
+
+// One CTA per token: grad_x[t] = sum_j w'[t,j] rg[t,j,:],  gsel[t,j] = <rg[t,j,:], x[t,:]>.
+__global__ void weighted_token_bwd_kernel(const void* __restrict__ rg, int rg_dtype,
+                                          const void* __restrict__ w, int w_dtype,
+                                          const void* __restrict__ x, int x_dtype,
+                                          void* __restrict__ gx, int gx_dtype,
+                                          float* __restrict__ gsel, int64_t k, int64_t d) {
+  const int64_t t = blockIdx.x;
+  extern __shared__ float red[];  // [blockDim.x / 32]
+  for (int64_t j = 0; j < k; ++j) {
+    if (!gsel) break;
+    float part = 0.f;
+    for (int64_t c = threadIdx.x; c < d; c += blockDim.x)
+      part = fmaf(load_as_float(rg, rg_dtype, (t * k + j) * d + c), load_as_float(x, x_dtype, t * d + c), part);
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = part;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float s = 0.f;
+      for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += red[i];
+      gsel[t * k + j] = s;
+    }
+    __syncthreads();
+  }
+  if (!gx) return;
+  for (int64_t c = threadIdx.x; c < d; c += blockDim.x) {
+    float acc = 0.f;
+    for (int64_t j = 0; j < k; ++j) {
+      const float wj = round_to(load_as_float(w, w_dtype, t * k + j), rg_dtype);
+      acc = fmaf(wj, load_as_float(rg, rg_dtype, (t * k + j) * d + c), acc);
+    }
+    store_from_float(gx, gx_dtype, t * d + c, acc);
+  }
+}
+
+__global__ void cast_kernel(const void* __restrict__ src, int s_dtype, void* __restrict__ dst,
+                            int d_dtype, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    store_from_float(dst, d_dtype, i, load_as_float(src, s_dtype, i));
+}
+
+// fp32 -> bf16/fp16, 8 elements per thread with 32-byte loads / 16-byte stores.
+__global__ void cast_f32_to_16_vec(const float4* __restrict__ src, uint4* __restrict__ dst,
+                                   int d_dtype, int64_t n8) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 a = src[2 * i], b = src[2 * i + 1];
+    uint4 o;
+    o.x = (uint32_t)float_to_bits(a.x, d_dtype) | ((uint32_t)float_to_bits(a.y, d_dtype) << 16);
+    o.y = (uint32_t)float_to_bits(a.z, d_dtype) | ((uint32_t)float_to_bits(a.w, d_dtype) << 16);
+    o.z = (uint32_t)float_to_bits(b.x, d_dtype) | ((uint32_t)float_to_bits(b.y, d_dtype) << 16);
+    o.w = (uint32_t)float_to_bits(b.z, d_dtype) | ((uint32_t)float_to_bits(b.w, d_dtype) << 16);
+    dst[i] = o;
+  }
+}
+
+static inline int grid_for(int64_t work, int threads) {
+  int64_t g = (work + threads - 1) / threads;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(g, 148 * 16));
+}
+
+static inline bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+// ------------------------------------------------------------------ GEMM plumbing
+struct GemmWs {
+  int2* tiles;
+  int* n_tiles;
+};
+
+static size_t gemm_ws_bytes(int64_t n_routes, int64_t n_experts) {
+  return 256 + align_up((size_t)max_row_tiles(n_routes, n_experts, 64) * sizeof(int2), 256);
+}
+
+static int carve_gemm_ws(void* ws, size_t bytes, int64_t n_routes, int64_t n_experts, GemmWs* out,
+                         const char* who) {
+  if (!ws || bytes < gemm_ws_bytes(n_routes, n_experts)) {
+    snprintf(t_err, sizeof(t_err), "%s: workspace too small (need %zu bytes)", who,
+             gemm_ws_bytes(n_routes, n_experts));
+    return CVMM_ERR_WORKSPACE;
+  }
+  out->n_tiles = static_cast<int*>(ws);
+  out->tiles = reinterpret_cast<int2*>(static_cast<char*>(ws) + 256);
+  return CVMM_OK;
+}
+
+static int run_row_gemm(RowGemm& p, void* ws, size_t ws_bytes, cudaStream_t stream, const char* who) {
+  GemmWs g;
+  int rc = carve_gemm_ws(ws, ws_bytes, p.n_routes, p.n_experts, &g, who);
+  if (rc) return rc;
+  const bool tensor = p.op_dtype != F32;
+  const int bm = tensor ? 128 : 64;
+  rc = build_tiles(p.offsets, p.n_experts, bm, g.tiles, g.n_tiles, stream);
+  if (rc) return rc;
+  p.tiles = g.tiles;
+  p.n_tiles = g.n_tiles;
+  const int64_t max_tiles = max_row_tiles(p.n_routes, p.n_experts, bm);
+  return tensor ? launch_row_gemm_umma(p, max_tiles, stream) : launch_row_gemm_simt(p, max_tiles, stream);
+}
+
+}  // namespace cvmm
+
+using namespace cvmm;
+
+// ================================================================== C ABI
+extern "C" {
+
+int cvmm_abi_version(void) { return 1; }
+
+const char* cvmm_last_error(void) { return t_err; }
+
+int cvmm_device_status(int reset, int* where, long long* aux, cvmm_stream_t stream) {
+  DeviceStatus st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaMemcpyFromSymbolAsync(&st, g_status, sizeof(st), 0, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return fail_cuda("cvmm_device_status");
+  if (where) *where = st.where;
+  if (aux) *aux = st.aux;
+  if (reset) {
+    DeviceStatus z = {0, 0, 0};
+    if (cudaMemcpyToSymbolAsync(g_status, &z, sizeof(z), 0, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+      return fail_cuda("cvmm_device_status(reset)");
+  }
+  return st.code;
+}
+
+size_t cvmm_sel_prepare_workspace_size(int64_t n_routes) {
+  return sel_prepare_workspace_size(n_routes < 0 ? 0 : n_routes);
+}
+
+int cvmm_sel_prepare(const void* sel, int sel_dtype, int64_t n_routes, int64_t top_k,
+                     int route_input, int32_t* raw_sel, int32_t* sorted_sel, int64_t* sel_index,
+                     int64_t* out_index, void* workspace, size_t workspace_bytes,
+                     cvmm_stream_t stream) {
+  return sel_prepare(sel, sel_dtype, n_routes, top_k, route_input, raw_sel, sorted_sel, sel_index,
+                     out_index, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int cvmm_expert_offsets(const int32_t* sorted_sel, int64_t n_routes, int64_t n_experts,
+                        int64_t* offsets, cvmm_stream_t stream) {
+  return expert_offsets(sorted_sel, n_routes, n_experts, offsets, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t cvmm_gemm_workspace_size(int64_t n_routes, int64_t n_experts, int64_t k_dim, int64_t n_dim,
+                                int x_dtype, int keys_dtype, int op_dtype, int64_t x_rows) {
+  (void)k_dim; (void)n_dim; (void)x_dtype; (void)keys_dtype; (void)op_dtype; (void)x_rows;
+  return gemm_ws_bytes(n_routes < 0 ? 0 : n_routes, n_experts < 0 ? 0 : n_experts);
+}
+
+int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld, const int64_t* sel_index,
+                 const int64_t* out_index, const int64_t* offsets, int64_t n_routes,
+                 const void* keys, int keys_dtype, int64_t n_experts, int64_t k_dim, int64_t n_dim,
+                 int64_t ks_e, int64_t ks_k, int64_t ks_n, void* out, int out_dtype, int64_t out_ld,
+                 int op_dtype, void* workspace, size_t workspace_bytes, cvmm_stream_t stream) {
+  if (!is_float_dtype(x_dtype) || !is_float_dtype(keys_dtype) || !is_float_dtype(out_dtype) ||
+      !is_float_dtype(op_dtype))
+    return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_forward: unsupported dtype");
+  if (n_routes < 0 || n_experts <= 0 || k_dim < 0 || n_dim <= 0 || x_rows < 0 || x_ld < k_dim ||
+      out_ld < n_dim)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: bad sizes");
+  if (n_routes == 0) return CVMM_OK;
+  if (!x || !sel_index || !offsets || !keys || !out)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: null pointer");
+  RowGemm p = {};
+  p.a = x; p.a_dtype = x_dtype; p.a_ld = x_ld; p.a_index = sel_index; p.a_div = 1;
+  p.b = keys; p.b_dtype = keys_dtype; p.bs_e = ks_e; p.bs_k = ks_k; p.bs_n = ks_n;
+  p.c = out; p.c_dtype = out_dtype; p.c_ld = out_ld; p.c_index = out_index ? out_index : sel_index;
+  p.offsets = offsets; p.n_routes = n_routes; p.n_experts = n_experts; p.K = k_dim; p.N = n_dim;
+  p.mode = 0; p.op_dtype = op_dtype;
+  return run_row_gemm(p, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), "cvmm_forward");
+}
+
+int cvmm_weighted_combine(const void* y, int y_dtype, const void* w, int w_dtype, void* out,
+                          int out_dtype, int64_t n_tokens, int64_t top_k, int64_t n_dim,
+                          cvmm_stream_t stream) {
+  if (!is_float_dtype(y_dtype) || (w && !is_float_dtype(w_dtype)) || !is_float_dtype(out_dtype))
+    return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_weighted_combine: unsupported dtype");
+  if (n_tokens < 0 || top_k <= 0 || n_dim <= 0)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_weighted_combine: bad sizes");
+  if (n_tokens == 0) return CVMM_OK;
+  if (!y || !out) return fail(CVMM_ERR_INVALID_ARG, "cvmm_weighted_combine: null pointer");
+  const bool vec = n_dim % 8 == 0 && y_dtype != F32 && out_dtype != F32 && al16(y) && al16(out);
+  const int64_t work = n_tokens * ((n_dim + 7) / 8);
+  combine_kernel<<<grid_for(work, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      y, y_dtype, w, w_dtype, out, out_dtype, n_tokens, top_k, n_dim, vec);
+  return check_launch("cvmm_weighted_combine");
+}
+
+int cvmm_sum_routes(const void* src, int src_dtype, void* out, int out_dtype, int64_t n_tokens,
+                    int64_t top_k, int64_t d, cvmm_stream_t stream) {
+  return cvmm_weighted_combine(src, src_dtype, nullptr, CVMM_F32, out, out_dtype, n_tokens, top_k, d,
+                               stream);
+}
+
+int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_index, int64_t g_div,
+                    const int64_t* out_index, const int64_t* offsets, int64_t n_routes,
+                    const void* keys, int keys_dtype, int64_t n_experts, int64_t k_dim, int64_t n_dim,
+                    int64_t ks_e, int64_t ks_k, int64_t ks_n, void* out, int out_dtype, int64_t out_ld,
+                    int mode, const void* w, int w_dtype, const void* x, int x_dtype, int64_t x_ld,
+                    float* gsel, int op_dtype, void* workspace, size_t workspace_bytes,
+                    cvmm_stream_t stream) {
+  if (!is_float_dtype(g_dtype) || !is_float_dtype(keys_dtype) || !is_float_dtype(out_dtype) ||
+      !is_float_dtype(op_dtype))
+    return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_backward_x: unsupported dtype");
+  if (mode != 0 && mode != 1) return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: mode must be 0 or 1");
+  if (n_routes < 0 || n_experts <= 0 || k_dim <= 0 || n_dim < 0 || g_div <= 0 || g_ld < n_dim ||
+      out_ld < k_dim)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: bad sizes");
+  if (n_routes == 0) return CVMM_OK;
+  if (!g || !g_index || !out_index || !offsets || !keys || !out)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: null pointer");
+  if (mode == 1 && (!w || !x || !gsel || !is_float_dtype(w_dtype) || !is_float_dtype(x_dtype) || x_ld < k_dim))
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: mode 1 needs w, x and gsel");
+  RowGemm p = {};
+  // B_e[kk][nn] = keys[e][nn][kk]: contract over n_dim, produce k_dim columns.
+  p.a = g; p.a_dtype = g_dtype; p.a_ld = g_ld; p.a_index = g_index; p.a_div = g_div;
+  p.b = keys; p.b_dtype = keys_dtype; p.bs_e = ks_e; p.bs_k = ks_n; p.bs_n = ks_k;
+  p.c = out; p.c_dtype = out_dtype; p.c_ld = out_ld; p.c_index = out_index;
+  p.offsets = offsets; p.n_routes = n_routes; p.n_experts = n_experts; p.K = n_dim; p.N = k_dim;
+  p.mode = mode; p.w = w; p.w_dtype = w_dtype; p.x = x; p.x_dtype = x_dtype; p.x_ld = x_ld;
+  p.gsel = gsel; p.op_dtype = op_dtype;
+  return run_row_gemm(p, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), "cvmm_backward_x");
+}
+
+int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_index, int64_t x_div,
+                    const void* g, int g_dtype, int64_t g_ld, const int64_t* g_index, int64_t g_div,
+                    const void* w, int w_dtype, const int64_t* w_index, const int64_t* offsets,
+                    int64_t n_routes, int64_t n_experts, int64_t m_dim, int64_t n_dim, float* grad_w,
+                    int op_dtype, void* workspace, size_t workspace_bytes, cvmm_stream_t stream) {
+  (void)workspace; (void)workspace_bytes;
+  if (!is_float_dtype(x_dtype) || !is_float_dtype(g_dtype) || !is_float_dtype(op_dtype) ||
+      (w && !is_float_dtype(w_dtype)))
+    return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_backward_w: unsupported dtype");
+  if (n_routes < 0 || n_experts <= 0 || m_dim <= 0 || n_dim <= 0 || x_div <= 0 || g_div <= 0 ||
+      x_ld < m_dim || g_ld < n_dim)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: bad sizes");
+  if (!grad_w || !offsets || (n_routes > 0 && (!x || !g || !x_index || !g_index)) || (w && !w_index))
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: null pointer");
+  if (n_experts > 65535) return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: too many experts");
+  SegGemm p = {};
+  p.x = x; p.x_dtype = x_dtype; p.x_ld = x_ld; p.x_index = x_index; p.x_div = x_div;
+  p.g = g; p.g_dtype = g_dtype; p.g_ld = g_ld; p.g_index = g_index; p.g_div = g_div;
+  p.w = w; p.w_dtype = w_dtype; p.w_index = w_index;
+  p.offsets = offsets; p.n_routes = n_routes; p.n_experts = n_experts; p.M = m_dim; p.N = n_dim;
+  p.out = grad_w; p.op_dtype = op_dtype;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return op_dtype == F32 ? launch_seg_gemm_simt(p, s) : launch_seg_gemm_umma(p, s);
+}
+
+int cvmm_weighted_token_backward(const void* route_grad, int rg_dtype, const void* w, int w_dtype,
+                                 const void* x, int x_dtype, void* grad_x, int gx_dtype,
+                                 float* grad_sel, int64_t n_tokens, int64_t top_k, int64_t d,
+                                 cvmm_stream_t stream) {
+  if (!is_float_dtype(rg_dtype) || !is_float_dtype(w_dtype) || !is_float_dtype(x_dtype) ||
+      (grad_x && !is_float_dtype(gx_dtype)))
+    return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_weighted_token_backward: unsupported dtype");
+  if (n_tokens < 0 || top_k <= 0 || d <= 0)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_weighted_token_backward: bad sizes");
+  if (n_tokens == 0) return CVMM_OK;
+  if (!route_grad || !w || (grad_sel && !x))
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_weighted_token_backward: null pointer");
+  const int threads = 256;
+  weighted_token_bwd_kernel<<<(unsigned)n_tokens, threads, (threads / 32) * sizeof(float),
+                              reinterpret_cast<cudaStream_t>(stream)>>>(
+      route_grad, rg_dtype, w, w_dtype, x, x_dtype, grad_x, gx_dtype, grad_sel, top_k, d);
+  return check_launch("cvmm_weighted_token_backward");
+}
+
+int cvmm_cast(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n, cvmm_stream_t stream) {
+  if (!is_float_dtype(src_dtype) || !is_float_dtype(dst_dtype))
+    return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_cast: unsupported dtype");
+  if (n < 0) return fail(CVMM_ERR_INVALID_ARG, "cvmm_cast: bad size");
+  if (n == 0) return CVMM_OK;
+  if (!src || !dst) return fail(CVMM_ERR_INVALID_ARG, "cvmm_cast: null pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (src_dtype == F32 && dst_dtype != F32 && n % 8 == 0 && al16(src) && al16(dst)) {
+    cast_f32_to_16_vec<<<grid_for(n / 8, 256), 256, 0, s>>>(static_cast<const float4*>(src),
+                                                            static_cast<uint4*>(dst), dst_dtype, n / 8);
+  } else {
+    cast_kernel<<<grid_for(n, 256), 256, 0, s>>>(src, src_dtype, dst, dst_dtype, n);
+  }
+  return check_launch("cvmm_cast");
+}
+
+}  // extern "C"

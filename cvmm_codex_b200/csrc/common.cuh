@@ -1,0 +1,85 @@
+// Shared device helpers for the CVMM sm_100a kernels: dtype codes, element
+// conversion, status reporting and the bounded-wait clock.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/cvmm_sm100.h"
+
+namespace cvmm {
+
+// Element dtype codes. The float codes are the reference's dtype_to_type_id
+// values (cvmm.py:36-44): 0 = float32, 1 = float16, 2 = bfloat16.
+enum DType : int { F32 = CVMM_F32, F16 = CVMM_F16, BF16 = CVMM_BF16 };
+
+__host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
+
+__host__ __device__ __forceinline__ int dtype_bytes(int dtype) {
+  return dtype == F32 ? 4 : (dtype == CVMM_I64 ? 8 : (dtype == CVMM_I32 ? 4 : 2));
+}
+
+__device__ __forceinline__ float load_as_float(const void* p, int dtype, int64_t i) {
+  if (dtype == BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  if (dtype == F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+
+// Round an fp32 value to the operation dtype (round-to-nearest-even), returned
+// as fp32. This is the "a.to(bf16)" step the reference applies to every GEMM
+// operand before tl.dot (cvmm.py:198-204).
+__device__ __forceinline__ float round_to(float v, int dtype) {
+  if (dtype == BF16) return __bfloat162float(__float2bfloat16_rn(v));
+  if (dtype == F16) return __half2float(__float2half_rn(v));
+  return v;
+}
+
+__device__ __forceinline__ void store_from_float(void* p, int dtype, int64_t i, float v) {
+  if (dtype == BF16) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else if (dtype == F16) reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+  else reinterpret_cast<float*>(p)[i] = v;
+}
+
+__device__ __forceinline__ uint16_t float_to_bits(float v, int dtype) {
+  if (dtype == F16) return __half_as_ushort(__float2half_rn(v));
+  return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
+__device__ __forceinline__ float bits_to_float(uint16_t b, int dtype) {
+  if (dtype == F16) return __half2float(__ushort_as_half(b));
+  return __bfloat162float(__ushort_as_bfloat16(b));
+}
+
+// Device status word. Kernels never trap: a failed bounded wait or a bad
+// index is recorded here and the kernel returns; the host reads it back with
+// cvmm_device_status().
+struct DeviceStatus {
+  int code;       // first error code recorded (0 = none)
+  int where;      // kernel-specific location tag
+  long long aux;  // e.g. the offending index
+};
+
+// Defined here: the library is one translation unit (csrc/cvmm_sm100.cu).
+__device__ DeviceStatus g_status;
+
+__device__ __forceinline__ void report(int code, int where, long long aux) {
+  if (atomicCAS(&g_status.code, 0, code) == 0) {
+    g_status.where = where;
+    g_status.aux = aux;
+  }
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Upper bound of any single wait inside a kernel (2 s). A healthy wait lasts
+// microseconds; exceeding it means a protocol bug, so the kernel records
+// CVMM_DEV_TIMEOUT and unwinds instead of hanging the GPU.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+}  // namespace cvmm

@@ -1,0 +1,64 @@
+// Problem descriptions shared by the two GEMM engines (tcgen05 tensor-core
+// kernels for bf16/fp16 arithmetic, exact-fp32 FFMA kernels for fp32
+// arithmetic) and the expert-segment tile scheduler.
+#pragma once
+
+#include "common.cuh"
+
+namespace cvmm {
+
+// "Row-gathered" grouped GEMM: the forward pass and grad-input.
+// For sorted position p of expert e:
+//   acc_p[n] = sum_k op(A[a_row(p)][k]) * op(B_e[k][n]),   a_row(p) = a_index[p] / a_div
+//   mode 0: C[c_index[p]][n] = cast(acc_p[n])
+//   mode 1: C[c_index[p]][n] = cast(op(op(acc_p[n]) * op(w[c_index[p]])))
+//           gsel[c_index[p]] += sum_n op(acc_p[n]) * x[c_index[p]][n]
+struct RowGemm {
+  const void* a; int a_dtype; int64_t a_ld;
+  const int64_t* a_index; int64_t a_div;
+  const void* b; int b_dtype; int64_t bs_e, bs_k, bs_n;
+  void* c; int c_dtype; int64_t c_ld;
+  const int64_t* c_index;
+  const int64_t* offsets;
+  int64_t n_routes, n_experts, K, N;
+  int mode;
+  const void* w; int w_dtype;
+  const void* x; int x_dtype; int64_t x_ld;
+  float* gsel;
+  int op_dtype;
+  const int2* tiles;   // (expert, first sorted position) per M tile
+  const int* n_tiles;  // number of valid entries in `tiles`
+};
+
+// Per-expert segment reduction: grad-weight.
+//   out[e][m][n] = sum_{p in seg(e)} op(X[x_row(p)][m]) * G'_p[n]
+//   G'_p[n] = op(G[g_row(p)][n])                       (w == nullptr)
+//           = op(op(G[g_row(p)][n]) * op(w[w_index[p]])) (weighted)
+struct SegGemm {
+  const void* x; int x_dtype; int64_t x_ld; const int64_t* x_index; int64_t x_div;
+  const void* g; int g_dtype; int64_t g_ld; const int64_t* g_index; int64_t g_div;
+  const void* w; int w_dtype; const int64_t* w_index;
+  const int64_t* offsets;
+  int64_t n_routes, n_experts, M, N;
+  float* out;
+  int op_dtype;
+};
+
+__device__ __forceinline__ int64_t seg_begin(const int64_t* offsets, int64_t e) {
+  return e > 0 ? offsets[e - 1] : 0;
+}
+
+// Upper bound of the number of M tiles of height bm over all expert segments.
+inline int64_t max_row_tiles(int64_t n_routes, int64_t n_experts, int bm) {
+  return (n_routes + bm - 1) / bm + n_experts;
+}
+
+// Host launchers (return a CVMM status).
+int build_tiles(const int64_t* offsets, int64_t n_experts, int bm, int2* tiles, int* n_tiles,
+                cudaStream_t stream);
+int launch_row_gemm_simt(const RowGemm& p, int64_t max_tiles, cudaStream_t stream);
+int launch_seg_gemm_simt(const SegGemm& p, cudaStream_t stream);
+int launch_row_gemm_umma(const RowGemm& p, int64_t max_tiles, cudaStream_t stream);
+int launch_seg_gemm_umma(const SegGemm& p, cudaStream_t stream);
+
+}  // namespace cvmm

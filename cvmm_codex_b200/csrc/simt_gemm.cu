@@ -1,0 +1,227 @@
+// Expert-segment tile scheduler and the exact-fp32 (FFMA) GEMM engine.
+//
+// The fp32 engine serves op_dtype == float32, the reference's autocast-off
+// path, which runs tl.dot with allow_tf32=False (cvmm.py:862 and every other
+// launcher): a true fp32 dot product. sm_100 has no fp32 tensor-core MMA, so
+// this path runs on the FMA pipes.
+#include "gemm.cuh"
+#include "launch.h"
+
+namespace cvmm {
+
+// ---------------------------------------------------------------- tiles
+// One CTA: every thread owns a contiguous run of experts, counts their M tiles,
+// and a block scan turns the counts into the write positions.
+__global__ void __launch_bounds__(1024)
+build_tiles_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int bm,
+                   int2* __restrict__ tiles, int* __restrict__ n_tiles) {
+  const int t = threadIdx.x;
+  const int64_t per = (n_experts + blockDim.x - 1) / blockDim.x;
+  const int64_t e0 = min((int64_t)t * per, n_experts), e1 = min(e0 + per, n_experts);
+  int cnt = 0;
+  for (int64_t e = e0; e < e1; ++e) {
+    int64_t len = offsets[e] - seg_begin(offsets, e);
+    cnt += (int)((len + bm - 1) / bm);
+  }
+  __shared__ int warp_tot[32];
+  const int lane = t & 31, warp = t >> 5;
+  int v = cnt;
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += y;
+  }
+  if (lane == 31) warp_tot[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    int s = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    warp_tot[lane] = s;
+  }
+  __syncthreads();
+  int pos = v - cnt + (warp > 0 ? warp_tot[warp - 1] : 0);
+  for (int64_t e = e0; e < e1; ++e) {
+    int64_t b = seg_begin(offsets, e), end = offsets[e];
+    for (int64_t r = b; r < end; r += bm) tiles[pos++] = make_int2((int)e, (int)r);
+  }
+  if (t == blockDim.x - 1) *n_tiles = pos;
+}
+
+int build_tiles(const int64_t* offsets, int64_t n_experts, int bm, int2* tiles, int* n_tiles,
+                cudaStream_t stream) {
+  build_tiles_kernel<<<1, 1024, 0, stream>>>(offsets, n_experts, bm, tiles, n_tiles);
+  return check_launch("build_tiles");
+}
+
+// ---------------------------------------------------------------- fp32 row GEMM
+namespace simt {
+
+constexpr int TM = 64, TN = 64, TK = 16, THREADS = 256;
+
+__global__ void __launch_bounds__(THREADS) row_gemm_kernel(RowGemm p) {
+  if ((int)blockIdx.x >= *p.n_tiles) return;
+  const int2 tile = p.tiles[blockIdx.x];
+  const int64_t e = tile.x, r0 = tile.y;
+  const int64_t seg_end = p.offsets[e];
+  const int rows = (int)imin64(TM, seg_end - r0);
+  const int64_t n0 = (int64_t)blockIdx.y * TN;
+
+  __shared__ float As[TK][TM + 4];
+  __shared__ float Bs[TK][TN + 4];
+  const int t = threadIdx.x;
+  const int ty = t >> 4, tx = t & 15;
+
+  // A rows this thread loads: row = t/16 + 16*i, k = t%16.
+  int64_t a_row[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int rr = (t >> 4) + 16 * i;
+    a_row[i] = rr < rows ? p.a_index[r0 + rr] / p.a_div : -1;
+  }
+  const char* bbase = static_cast<const char*>(p.b);
+  const size_t bsz = p.b_dtype == F32 ? 4 : 2;
+
+  float acc[4][4] = {};
+  for (int64_t k0 = 0; k0 < p.K; k0 += TK) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      int rr = (t >> 4) + 16 * i, kk = t & 15;
+      float v = 0.f;
+      if (a_row[i] >= 0 && k0 + kk < p.K)
+        v = round_to(load_as_float(p.a, p.a_dtype, a_row[i] * p.a_ld + k0 + kk), p.op_dtype);
+      As[kk][rr] = v;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      int idx = t + THREADS * i;
+      int kk = idx / TN, nn = idx % TN;
+      float v = 0.f;
+      if (k0 + kk < p.K && n0 + nn < p.N) {
+        int64_t off = e * p.bs_e + (k0 + kk) * p.bs_k + (n0 + nn) * p.bs_n;
+        v = round_to(load_as_float(bbase, p.b_dtype, off), p.op_dtype);
+      }
+      Bs[kk][nn] = v;
+    }
+    (void)bsz;
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < TK; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int rr = ty * 4 + i;
+    const bool row_ok = rr < rows;
+    int64_t c_row = row_ok ? p.c_index[r0 + rr] : 0;
+    float wv = 0.f, dot = 0.f;
+    if (p.mode == 1 && row_ok) wv = round_to(load_as_float(p.w, p.w_dtype, c_row), p.op_dtype);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t n = n0 + tx * 4 + j;
+      if (!row_ok || n >= p.N) continue;
+      if (p.mode == 0) {
+        store_from_float(p.c, p.c_dtype, c_row * p.c_ld + n, acc[i][j]);
+      } else {
+        const float a = round_to(acc[i][j], p.op_dtype);
+        store_from_float(p.c, p.c_dtype, c_row * p.c_ld + n, round_to(a * wv, p.op_dtype));
+        dot = fmaf(a, load_as_float(p.x, p.x_dtype, c_row * p.x_ld + n), dot);
+      }
+    }
+    if (p.mode == 1) {
+      // The 16 threads sharing `ty` form one half-warp: reduce the row's dot there.
+      for (int o = 8; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      if (tx == 0 && row_ok) atomicAdd(p.gsel + c_row, dot);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- fp32 segment GEMM
+__global__ void __launch_bounds__(THREADS) seg_gemm_kernel(SegGemm p) {
+  const int64_t e = blockIdx.z;
+  const int64_t m0 = (int64_t)blockIdx.x * TM, n0 = (int64_t)blockIdx.y * TN;
+  const int64_t beg = seg_begin(p.offsets, e), end = p.offsets[e];
+  __shared__ float Xs[TK][TM + 4];
+  __shared__ float Gs[TK][TN + 4];
+  const int t = threadIdx.x;
+  const int ty = t >> 4, tx = t & 15;
+  float acc[4][4] = {};
+  for (int64_t r0 = beg; r0 < end; r0 += TK) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int idx = t + THREADS * i;
+      const int kk = idx / TM, mm = idx % TM;
+      const int64_t r = r0 + kk;
+      float xv = 0.f, gv = 0.f;
+      if (r < end) {
+        if (m0 + mm < p.M) {
+          const int64_t xr = p.x_index[r] / p.x_div;
+          xv = round_to(load_as_float(p.x, p.x_dtype, xr * p.x_ld + m0 + mm), p.op_dtype);
+        }
+        if (n0 + mm < p.N) {
+          const int64_t gr = p.g_index[r] / p.g_div;
+          gv = round_to(load_as_float(p.g, p.g_dtype, gr * p.g_ld + n0 + mm), p.op_dtype);
+          if (p.w) {
+            const float wv = round_to(load_as_float(p.w, p.w_dtype, p.w_index[r]), p.op_dtype);
+            gv = round_to(gv * wv, p.op_dtype);
+          }
+        }
+      }
+      Xs[kk][mm] = xv;
+      Gs[kk][mm] = gv;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < TK; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = Xs[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Gs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t m = m0 + ty * 4 + i;
+    if (m >= p.M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t n = n0 + tx * 4 + j;
+      if (n < p.N) p.out[(e * p.M + m) * p.N + n] = acc[i][j];
+    }
+  }
+}
+
+}  // namespace simt
+
+int launch_row_gemm_simt(const RowGemm& p, int64_t max_tiles, cudaStream_t stream) {
+  dim3 grid((unsigned)max_tiles, (unsigned)((p.N + simt::TN - 1) / simt::TN));
+  simt::row_gemm_kernel<<<grid, simt::THREADS, 0, stream>>>(p);
+  return check_launch("row_gemm_simt");
+}
+
+int launch_seg_gemm_simt(const SegGemm& p, cudaStream_t stream) {
+  dim3 grid((unsigned)((p.M + simt::TM - 1) / simt::TM), (unsigned)((p.N + simt::TN - 1) / simt::TN),
+            (unsigned)p.n_experts);
+  simt::seg_gemm_kernel<<<grid, simt::THREADS, 0, stream>>>(p);
+  return check_launch("seg_gemm_simt");
+}
+
+}  // namespace cvmm

@@ -1,0 +1,179 @@
+/*
+ * cvmm_sm100.h — C ABI of the B200 (sm_100a) CVMM library (libcvmm_sm100.so).
+ *
+ * CVMM ("conditional vector-matrix multiplication") is the top-k
+ * mixture-of-experts projection of RobertCsordas/cvmm_codex: every route r
+ * (one token's choice of one expert) multiplies one input row by the weight
+ * matrix keys[e] of the expert e it was routed to.
+ *
+ * Conventions shared by every entry point:
+ *   - all pointers are device pointers; sizes are element counts;
+ *   - every function is stream-ordered on `stream` (a cudaStream_t) and never
+ *     synchronises the host;
+ *   - no function allocates device memory. Scratch comes from the caller as
+ *     `workspace` / `workspace_bytes`, sized by the matching *_workspace_size
+ *     query;
+ *   - the return value is a status code (CVMM_OK or a negative CVMM_ERR_*);
+ *     cvmm_last_error() gives a message for the last failure on this thread;
+ *   - dtype codes follow the reference's dtype_to_type_id (cvmm.py:36-44).
+ *
+ * "Sorted order" below means the expert-major stable order produced by
+ * cvmm_sel_prepare: position p of the sorted arrays is the p-th route when
+ * routes are ordered by (expert id, route id).
+ */
+#ifndef CVMM_SM100_H
+#define CVMM_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* cvmm_stream_t; /* == cudaStream_t */
+
+/* dtype codes */
+#define CVMM_F32 0
+#define CVMM_F16 1
+#define CVMM_BF16 2
+#define CVMM_I32 3
+#define CVMM_I64 4
+
+/* status codes */
+#define CVMM_OK 0
+#define CVMM_ERR_INVALID_ARG -1
+#define CVMM_ERR_UNSUPPORTED_DTYPE -2
+#define CVMM_ERR_LAUNCH -3
+#define CVMM_ERR_WORKSPACE -4
+#define CVMM_ERR_DEVICE -5
+/* device status word codes (cvmm_device_status) */
+#define CVMM_DEV_TIMEOUT 1
+#define CVMM_DEV_BAD_INDEX 2
+
+/* ABI version of this header; bumped on any signature change. */
+int cvmm_abi_version(void);
+
+/* Message for the last failed call on the calling host thread. */
+const char* cvmm_last_error(void);
+
+/* Reads (and with reset != 0 clears) the device status word that kernels set
+ * instead of trapping. Synchronises `stream`. Returns the code (0 = clean);
+ * where/aux receive the kernel tag and offending value when non-NULL. */
+int cvmm_device_status(int reset, int* where, long long* aux, cvmm_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Selector preparation.
+ * Replaces cvmm_prepare_sel2 (cvmm.py:1786-1803) and cvmm_prepare_sel
+ * (cvmm.py:24-27): fsel = int32(sel); (ssel, idx) = fsel.sort();
+ *   route_input == 0: sel_index = idx // top_k, out_index = idx
+ *   route_input != 0: sel_index = idx,          out_index unused (may be NULL)
+ * The sort is a stable device radix sort, so ties keep route order; this is
+ * bit-exact with torch.sort(stable=True).
+ *   sel: [n_routes] int64 or int32 (sel_dtype CVMM_I64 / CVMM_I32)
+ *   raw_sel, sorted_sel: [n_routes] int32; sel_index, out_index: [n_routes] int64
+ * ------------------------------------------------------------------------ */
+size_t cvmm_sel_prepare_workspace_size(int64_t n_routes);
+int cvmm_sel_prepare(const void* sel, int sel_dtype, int64_t n_routes, int64_t top_k,
+                     int route_input, int32_t* raw_sel, int32_t* sorted_sel,
+                     int64_t* sel_index, int64_t* out_index, void* workspace,
+                     size_t workspace_bytes, cvmm_stream_t stream);
+
+/* Inclusive end offset of every expert's segment in sorted order:
+ * offsets[e] = #routes with expert <= e (missing experts repeat the previous
+ * value). Replaces _cvmm_expert_offsets / cvmm_expert_offsets_kernel
+ * (cvmm.py:68-78, 315-335, 1108-1120). */
+int cvmm_expert_offsets(const int32_t* sorted_sel, int64_t n_routes, int64_t n_experts,
+                        int64_t* offsets, cvmm_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Forward gathered GEMM. Replaces torch op mylib::cvmm_triton / cvmm_triton
+ * (cvmm.py:808-867) and cvmm_kernel (cvmm.py:121-243).
+ * For every sorted position p with expert e (from offsets):
+ *   out[row_p] = cast_out( op(x[sel_index[p]]) . op(keys[e]) )   fp32 accumulate
+ *   row_p = out_index[p] if out_index != NULL else sel_index[p]
+ * x: [x_rows, k_dim] row-major with leading dimension x_ld;
+ * keys[e][k][n] at keys + e*ks_e + k*ks_k + n*ks_n (any strides);
+ * out: [n_routes, n_dim] with leading dimension out_ld.
+ * op_dtype selects the arithmetic: CVMM_BF16 / CVMM_F16 run on the tcgen05
+ * tensor cores (operands rounded to op_dtype, fp32 accumulate), CVMM_F32 runs
+ * an exact fp32 FFMA kernel (the reference's allow_tf32=False path).
+ * ------------------------------------------------------------------------ */
+size_t cvmm_gemm_workspace_size(int64_t n_routes, int64_t n_experts, int64_t k_dim,
+                                int64_t n_dim, int x_dtype, int keys_dtype, int op_dtype,
+                                int64_t x_rows);
+int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld,
+                 const int64_t* sel_index, const int64_t* out_index, const int64_t* offsets,
+                 int64_t n_routes, const void* keys, int keys_dtype, int64_t n_experts,
+                 int64_t k_dim, int64_t n_dim, int64_t ks_e, int64_t ks_k, int64_t ks_n,
+                 void* out, int out_dtype, int64_t out_ld, int op_dtype, void* workspace,
+                 size_t workspace_bytes, cvmm_stream_t stream);
+
+/* Weighted combine of the forward: out[t] = cast( sum_j cast_y(w[t,j]) * y[t*top_k+j] ),
+ * fp32 accumulate. Replaces the bmm at cvmm.py:1543-1545. */
+int cvmm_weighted_combine(const void* y, int y_dtype, const void* w, int w_dtype,
+                          void* out, int out_dtype, int64_t n_tokens, int64_t top_k,
+                          int64_t n_dim, cvmm_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Backward grad-input GEMM. Replaces cvmm_grouped_bwd_x_kernel
+ * (cvmm.py:363-421) with its launcher (cvmm.py:1199-1223) and the fused
+ * cvmm_weighted_route_bwd_x_kernel (cvmm.py:1008-1105, launcher 1386-1433).
+ * For every sorted position p with expert e:
+ *   a_p = op(g[g_index[p] / g_div]) . op(keys[e])^T          (fp32 acc)
+ *   mode 0: out[out_index[p]] = cast_out(a_p)
+ *   mode 1 (weighted, route-shaped x):
+ *           out[out_index[p]]  = cast_out( op(op(a_p) * op(w[out_index[p]])) )
+ *           gsel[out_index[p]] += sum_j op(a_p)_j * x[out_index[p]]_j   (fp32)
+ * keys strides are those of keys[e][k_dim][n_dim] as in cvmm_forward; the
+ * product contracts over n_dim and produces k_dim columns.
+ * gsel must be zeroed by the caller (mode 1 accumulates into it).
+ * ------------------------------------------------------------------------ */
+int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_index,
+                    int64_t g_div, const int64_t* out_index, const int64_t* offsets,
+                    int64_t n_routes, const void* keys, int keys_dtype, int64_t n_experts,
+                    int64_t k_dim, int64_t n_dim, int64_t ks_e, int64_t ks_k, int64_t ks_n,
+                    void* out, int out_dtype, int64_t out_ld, int mode, const void* w,
+                    int w_dtype, const void* x, int x_dtype, int64_t x_ld, float* gsel,
+                    int op_dtype, void* workspace, size_t workspace_bytes,
+                    cvmm_stream_t stream);
+
+/* Backward grad-weight. Replaces cvmm_grouped_bwd_w_gather_x_kernel /
+ * cvmm_grouped_bwd_w_kernel / cvmm_grouped_bwd_w_weighted_kernel
+ * (cvmm.py:424-604, launchers 1141-1198, 1341-1383):
+ *   grad_w[e][m][n] = sum_{p in seg(e)} op(x[x_index[p]/x_div][m]) * s_p * op(g[g_index[p]/g_div][n])
+ *   s_p = 1, or with w != NULL: the g row is first multiplied by op(w[w_index[p]])
+ *   and rounded to op_dtype (cvmm.py:591-599).
+ * grad_w: [n_experts, m_dim, n_dim] fp32, fully written (empty experts get 0). */
+int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_index,
+                    int64_t x_div, const void* g, int g_dtype, int64_t g_ld,
+                    const int64_t* g_index, int64_t g_div, const void* w, int w_dtype,
+                    const int64_t* w_index, const int64_t* offsets, int64_t n_routes,
+                    int64_t n_experts, int64_t m_dim, int64_t n_dim, float* grad_w,
+                    int op_dtype, void* workspace, size_t workspace_bytes,
+                    cvmm_stream_t stream);
+
+/* Sum over the top-k routes of each token: out[t] = cast( sum_j src[t*top_k+j] ),
+ * fp32 accumulate. Replaces grouped_x.view(..., top_k, d).sum(-2) (cvmm.py:1223). */
+int cvmm_sum_routes(const void* src, int src_dtype, void* out, int out_dtype,
+                    int64_t n_tokens, int64_t top_k, int64_t d, cvmm_stream_t stream);
+
+/* Token-input weighted backward tail (cvmm.py:1737-1746):
+ *   grad_x[t]      = cast( sum_j cast_r(w[t,j]) * route_grad[t,j] )       (if grad_x)
+ *   grad_sel[t,j]  = sum_d float(route_grad[t,j,d]) * float(x[t,d])        (if grad_sel, fp32)
+ * route_grad: [n_tokens*top_k, d]; x: [n_tokens, d]. */
+int cvmm_weighted_token_backward(const void* route_grad, int rg_dtype, const void* w,
+                                 int w_dtype, const void* x, int x_dtype, void* grad_x,
+                                 int gx_dtype, float* grad_sel, int64_t n_tokens,
+                                 int64_t top_k, int64_t d, cvmm_stream_t stream);
+
+/* Elementwise dtype conversion (round-to-nearest-even), e.g. fp32 expert
+ * weights to a bf16 operand copy. Supports the float dtypes only. */
+int cvmm_cast(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n,
+              cvmm_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CVMM_SM100_H */

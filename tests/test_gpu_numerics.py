@@ -1,0 +1,144 @@
+"""Forward and backward on the GPU against the fp64 oracle and the reference's fixtures.
+
+Tolerances:
+  * against the oracle (exact math on op-dtype-rounded operands, float64):
+    max-abs error relative to the largest magnitude <= 2e-2 for bf16/fp16
+    arithmetic and <= 1e-3 for fp32 arithmetic (the contract's bounds), plus
+    RMS error relative to the RMS <= 1e-2 / 1e-4;
+  * against the reference's `_reference` outputs (fixtures): the reference's
+    own per-tensor (atol, rtol) table (benchmark_correctness_original.py:47-66).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from cvmm_codex_b200 import cvmm, cvmm_prepare_sel2
+from oracle import cvmm_oracle as O
+
+pytestmark = pytest.mark.gpu
+NUM = torch.load(os.path.join(os.path.dirname(__file__), "golden", "numerics.pt"))
+
+REF_TOL = {  # (atol, rtol) per tensor, per dtype mode
+    "float32": {"out": (2e-4, 2e-4), "x_grad": (5e-4, 5e-4), "keys_grad": (2e-3, 2e-3), "w_grad": (2e-3, 2e-3)},
+    "bf16_amp": {"out": (1.5e-1, 6e-2), "x_grad": (2.5e-1, 8e-2), "keys_grad": (3.5e-1, 8e-2), "w_grad": (3.5e-1, 8e-2)},
+    "bf16_params": {"out": (2.0e-1, 8e-2), "x_grad": (3.0e-1, 1e-1), "keys_grad": (3.5e-1, 1e-1), "w_grad": (3.5e-1, 1e-1)},
+}
+MAX_TOL = {"float32": 1e-3, "bfloat16": 2e-2, "float16": 2e-2}
+RMS_TOL = {"float32": 1e-4, "bfloat16": 1e-2, "float16": 1e-2}
+
+
+def run_case(x, keys, sel, w, grad, route_input, amp_dtype):
+    x = x.cuda().requires_grad_(True)
+    keys = keys.cuda().requires_grad_(True)
+    sel = sel.cuda()
+    wc = None if w is None else w.cuda().requires_grad_(True)
+    sel2 = cvmm_prepare_sel2(sel, wc, route_input=route_input)
+    if amp_dtype is not None:
+        with torch.autocast(device_type="cuda", dtype=amp_dtype):
+            out = cvmm(x, sel2, keys)
+    else:
+        out = cvmm(x, sel2, keys)
+    out.backward(grad.cuda().to(out.dtype))
+    return out, x.grad, keys.grad, None if wc is None else wc.grad
+
+
+def _np(t):
+    return None if t is None else t.detach().float().cpu().numpy().astype(np.float64)
+
+
+def check_oracle(out, gx, gk, gw, x, keys, sel, w, grad, op):
+    eo = O.forward(_np(x), sel.numpy(), _np(keys), _np(w), op=op)
+    ex, ek, ew = O.backward(_np(x), sel.numpy(), _np(keys), _np(grad.to(out.dtype)), _np(w), op=op)
+    pairs = [("out", out, eo), ("x_grad", gx, ex), ("keys_grad", gk, ek)]
+    if w is not None:
+        pairs.append(("w_grad", gw, ew))
+    for name, a, e in pairs:
+        a = _np(a)
+        assert a.shape == e.shape, name
+        assert O.rel_max_err(a, e) <= MAX_TOL[op], (name, O.rel_max_err(a, e))
+        assert O.rel_rms_err(a, e) <= RMS_TOL[op], (name, O.rel_rms_err(a, e))
+
+
+@pytest.mark.parametrize("key", sorted(NUM))
+def test_reference_case_list(key):
+    c = NUM[key]
+    mode = c["mode"]
+    amp = None if mode == "float32" else torch.bfloat16
+    op = "float32" if mode == "float32" else "bfloat16"
+    out, gx, gk, gw = run_case(c["x"], c["keys"], c["sel"], c["w"], c["grad"], c["route_input"], amp)
+    # dtypes follow the reference: output in the op dtype, grads in the leaves' dtypes
+    assert out.dtype == (torch.float32 if amp is None else torch.bfloat16)
+    assert gx.dtype == c["x"].dtype and gk.dtype == c["keys"].dtype
+    check_oracle(out, gx, gk, gw, c["x"], c["keys"], c["sel"], c["w"], c["grad"], op)
+    tol = REF_TOL[mode]
+    for name, a in (("out", out), ("x_grad", gx), ("keys_grad", gk), ("w_grad", gw)):
+        if c[name] is None:
+            continue
+        at, rt = tol[name]
+        torch.testing.assert_close(a.float().cpu(), c[name].float(), atol=at, rtol=rt)
+
+
+@pytest.mark.parametrize("amp", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("weighted,route_input", [(False, False), (True, False), (True, True), (False, True)])
+def test_aligned_tensor_core_shapes(amp, weighted, route_input):
+    """Shapes whose rows meet the 16-byte cp.async fast path (d multiples of 8)."""
+    g = torch.Generator().manual_seed(17 + weighted * 2 + route_input)
+    T, k, E, d_in, d_out = 300, 4, 12, 192, 136
+    x = torch.randn(*((T, k, d_in) if route_input else (T, d_in)), generator=g).to(amp)
+    keys = torch.randn(E, d_in, d_out, generator=g) / d_in ** 0.5
+    sel = torch.randint(0, E, (T, k), generator=g)
+    w = torch.rand(T, k, generator=g) if weighted else None
+    grad = torch.randn(*((T, d_out) if weighted else (T, k, d_out)), generator=g)
+    out, gx, gk, gw = run_case(x, keys, sel, w, grad, route_input, amp)
+    check_oracle(out, gx, gk, gw, x, keys, sel, w, grad, "float16" if amp == torch.float16 else "bfloat16")
+
+
+@pytest.mark.parametrize("d_in,d_out", [(64, 64), (128, 256), (256, 512), (72, 200), (1024, 128), (128, 1024)])
+def test_tile_shapes(d_in, d_out):
+    """Every N-tile variant (64/128/256), multi-tile N, K not a multiple of 64, ragged segments."""
+    g = torch.Generator().manual_seed(d_in * 7 + d_out)
+    T, k, E = 700, 3, 9
+    x = torch.randn(T, d_in, generator=g).bfloat16()
+    keys = torch.randn(E, d_in, d_out, generator=g) / d_in ** 0.5
+    sel = torch.randint(0, E, (T, k), generator=g)
+    sel[:50] = 2  # one heavy expert: segments longer than several M tiles
+    grad = torch.randn(T, k, d_out, generator=g)
+    out, gx, gk, gw = run_case(x, keys, sel, None, grad, False, torch.bfloat16)
+    check_oracle(out, gx, gk, gw, x, keys, sel, None, grad, "bfloat16")
+
+
+def test_missing_experts_get_zero_grad():
+    g = torch.Generator().manual_seed(3)
+    T, k, E, d = 64, 2, 40, 32
+    x = torch.randn(T, d, generator=g).bfloat16()
+    keys = torch.randn(E, d, 24, generator=g)
+    sel = torch.randint(0, 5, (T, k), generator=g) * 3  # experts 0,3,6,9,12 only
+    grad = torch.randn(T, k, 24, generator=g)
+    out, gx, gk, gw = run_case(x, keys, sel, None, grad, False, torch.bfloat16)
+    used = set(sel.flatten().tolist())
+    for e in range(E):
+        if e not in used:
+            assert torch.count_nonzero(gk[e]) == 0
+    check_oracle(out, gx, gk, gw, x, keys, sel, None, grad, "bfloat16")
+
+
+def test_top1_and_raw_selector():
+    """A raw index tensor goes through cvmm_prepare_sel (route-indexed): x has one row per route."""
+    g = torch.Generator().manual_seed(9)
+    T, E, d, n = 333, 6, 40, 24
+    x = torch.randn(T, d, generator=g).bfloat16().cuda().requires_grad_(True)
+    keys = torch.randn(E, d, n, generator=g).cuda().requires_grad_(True)
+    sel = torch.randint(0, E, (T,), generator=g).cuda()
+    with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+        out = cvmm(x, sel, keys)
+    assert out.shape == (T, n)
+    e = O.forward(_np(x), sel.cpu().numpy()[:, None], _np(keys), op="bfloat16").reshape(T, n)
+    assert O.rel_max_err(_np(out), e) < 2e-2
+
+
+def test_device_status_clean():
+    from cvmm_codex_b200 import _lib
+    code, where, aux = _lib.device_status(reset=True)
+    assert code == 0, (code, where, aux)
