@@ -260,7 +260,7 @@ def run_ours(args, rank, world, local_rank):
         line["e2e"] = main["e2e"]
     if world == 1 and args.also:
         also = {}
-        for name in [s for s in args.also.split(",") if s and s != args.workload]:
+        for name in [s for s in args.also.split(",") if s in WORKLOADS and s != args.workload]:
             r = measure(name, False, True)
             also[name] = {"value": round(r["tflops"], 3), "unit": "TFLOP/s", "ms_per_step": round(r["ms"], 4),
                           "pct_bf16_peak_sustained": round(100 * r["tflops"] / pk["bf16_tflops_sustained"], 2),

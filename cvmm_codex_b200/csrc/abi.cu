@@ -135,37 +135,71 @@ static inline int grid_for(int64_t work, int threads) {
 static inline bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
 // ------------------------------------------------------------------ GEMM plumbing
+// Workspace layout shared by the GEMM entry points:
+//   [0, 256)           tile / unit count
+//   tiles or units     int4 x max_row_tiles(n_routes, n_experts, 64)
+//   expert_slots       int2 x n_experts                 (grad-W only)
+//   partials           fp32 x max_slots x m_dim x n_dim (grad-W only)
 struct GemmWs {
-  int2* tiles;
-  int* n_tiles;
+  int* count;
+  void* tiles;
+  int2* expert_slots;
+  float* partials;
 };
 
-static size_t gemm_ws_bytes(int64_t n_routes, int64_t n_experts) {
-  return 256 + align_up((size_t)max_row_tiles(n_routes, n_experts, 64) * sizeof(int2), 256);
+static size_t table_bytes(int64_t n_routes, int64_t n_experts) {
+  return 256 + align_up((size_t)max_row_tiles(n_routes, n_experts, 64) * sizeof(int4), 256);
 }
 
-static int carve_gemm_ws(void* ws, size_t bytes, int64_t n_routes, int64_t n_experts, GemmWs* out,
-                         const char* who) {
-  if (!ws || bytes < gemm_ws_bytes(n_routes, n_experts)) {
-    snprintf(t_err, sizeof(t_err), "%s: workspace too small (need %zu bytes)", who,
-             gemm_ws_bytes(n_routes, n_experts));
+// Split-K chunk of the grad-W units (routes per unit): no split when the
+// expert tiles alone fill the GPU several times; otherwise 1024 routes (16
+// tensor-core stages), halved while the grid would not fill two CTAs per SM,
+// and doubled while the partial slots would exceed 256 MiB.
+static int64_t segw_chunk(int64_t n_routes, int64_t n_experts, int64_t m_dim, int64_t n_dim, bool tensor) {
+  const int64_t mt = (m_dim + (tensor ? 127 : 63)) / (tensor ? 128 : 64);
+  const int64_t nt = (n_dim + (tensor ? 255 : 63)) / (tensor ? 256 : 64);
+  if (n_experts * mt * nt >= 8 * 148) return std::max<int64_t>(64, (n_routes + 63) / 64 * 64);
+  int64_t chunk = 1024;
+  while (chunk > 128 && (n_routes / chunk) * mt * nt < 2 * 148) chunk /= 2;
+  while (2 * ((n_routes + chunk - 1) / chunk) * m_dim * n_dim * 4 > ((int64_t)256 << 20)) chunk *= 2;
+  return chunk;
+}
+
+static int64_t segw_max_slots(int64_t n_routes, int64_t chunk) { return 2 * ((n_routes + chunk - 1) / chunk); }
+
+static size_t segw_ws_bytes(int64_t n_routes, int64_t n_experts, int64_t m_dim, int64_t n_dim, bool tensor) {
+  const int64_t chunk = segw_chunk(n_routes, n_experts, m_dim, n_dim, tensor);
+  return table_bytes(n_routes, n_experts) + align_up((size_t)n_experts * sizeof(int2), 256) +
+         align_up((size_t)segw_max_slots(n_routes, chunk) * m_dim * n_dim * sizeof(float), 256);
+}
+
+static int carve_ws(void* ws, size_t bytes, size_t need, int64_t n_routes, int64_t n_experts, GemmWs* out,
+                    const char* who) {
+  if (!ws || bytes < need) {
+    snprintf(t_err, sizeof(t_err), "%s: workspace too small (need %zu bytes)", who, need);
     return CVMM_ERR_WORKSPACE;
   }
-  out->n_tiles = static_cast<int*>(ws);
-  out->tiles = reinterpret_cast<int2*>(static_cast<char*>(ws) + 256);
+  char* b = static_cast<char*>(ws);
+  out->count = reinterpret_cast<int*>(b);
+  out->tiles = b + 256;
+  b += table_bytes(n_routes, n_experts);
+  out->expert_slots = reinterpret_cast<int2*>(b);
+  b += align_up((size_t)n_experts * sizeof(int2), 256);
+  out->partials = reinterpret_cast<float*>(b);
   return CVMM_OK;
 }
 
 static int run_row_gemm(RowGemm& p, void* ws, size_t ws_bytes, cudaStream_t stream, const char* who) {
   GemmWs g;
-  int rc = carve_gemm_ws(ws, ws_bytes, p.n_routes, p.n_experts, &g, who);
+  int rc = carve_ws(ws, ws_bytes, table_bytes(p.n_routes, p.n_experts), p.n_routes, p.n_experts, &g, who);
   if (rc) return rc;
   const bool tensor = p.op_dtype != F32;
   const int bm = tensor ? 128 : 64;
-  rc = build_tiles(p.offsets, p.n_experts, bm, g.tiles, g.n_tiles, stream);
+  int2* tiles = static_cast<int2*>(g.tiles);
+  rc = build_tiles(p.offsets, p.n_experts, bm, tiles, g.count, stream);
   if (rc) return rc;
-  p.tiles = g.tiles;
-  p.n_tiles = g.n_tiles;
+  p.tiles = tiles;
+  p.n_tiles = g.count;
   const int64_t max_tiles = max_row_tiles(p.n_routes, p.n_experts, bm);
   return tensor ? launch_row_gemm_umma(p, max_tiles, stream) : launch_row_gemm_simt(p, max_tiles, stream);
 }
@@ -217,8 +251,13 @@ int cvmm_expert_offsets(const int32_t* sorted_sel, int64_t n_routes, int64_t n_e
 
 size_t cvmm_gemm_workspace_size(int64_t n_routes, int64_t n_experts, int64_t k_dim, int64_t n_dim,
                                 int x_dtype, int keys_dtype, int op_dtype, int64_t x_rows) {
-  (void)k_dim; (void)n_dim; (void)x_dtype; (void)keys_dtype; (void)op_dtype; (void)x_rows;
-  return gemm_ws_bytes(n_routes < 0 ? 0 : n_routes, n_experts < 0 ? 0 : n_experts);
+  (void)x_dtype; (void)keys_dtype; (void)x_rows;
+  n_routes = n_routes < 0 ? 0 : n_routes;
+  n_experts = n_experts < 1 ? 1 : n_experts;
+  size_t b = table_bytes(n_routes, n_experts);
+  if (k_dim > 0 && n_dim > 0)
+    b = std::max(b, segw_ws_bytes(n_routes, n_experts, k_dim, n_dim, op_dtype != CVMM_F32));
+  return b;
 }
 
 int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld, const int64_t* sel_index,
@@ -233,6 +272,7 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld, const
       out_ld < n_dim)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: bad sizes");
   if (n_routes == 0) return CVMM_OK;
+  if (n_routes > (int64_t)INT32_MAX) return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: too many routes");
   if (!x || !sel_index || !offsets || !keys || !out)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: null pointer");
   RowGemm p = {};
@@ -281,6 +321,7 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
       out_ld < k_dim)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: bad sizes");
   if (n_routes == 0) return CVMM_OK;
+  if (n_routes > (int64_t)INT32_MAX) return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: too many routes");
   if (!g || !g_index || !out_index || !offsets || !keys || !out)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: null pointer");
   if (mode == 1 && (!w || !x || !gsel || !is_float_dtype(w_dtype) || !is_float_dtype(x_dtype) || x_ld < k_dim))
@@ -301,24 +342,41 @@ int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_i
                     const void* w, int w_dtype, const int64_t* w_index, const int64_t* offsets,
                     int64_t n_routes, int64_t n_experts, int64_t m_dim, int64_t n_dim, float* grad_w,
                     int op_dtype, void* workspace, size_t workspace_bytes, cvmm_stream_t stream) {
-  (void)workspace; (void)workspace_bytes;
   if (!is_float_dtype(x_dtype) || !is_float_dtype(g_dtype) || !is_float_dtype(op_dtype) ||
       (w && !is_float_dtype(w_dtype)))
     return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_backward_w: unsupported dtype");
   if (n_routes < 0 || n_experts <= 0 || m_dim <= 0 || n_dim <= 0 || x_div <= 0 || g_div <= 0 ||
-      x_ld < m_dim || g_ld < n_dim)
+      x_ld < m_dim || g_ld < n_dim || n_routes > (int64_t)INT32_MAX)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: bad sizes");
   if (!grad_w || !offsets || (n_routes > 0 && (!x || !g || !x_index || !g_index)) || (w && !w_index))
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: null pointer");
   if (n_experts > 65535) return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: too many experts");
+  const bool tensor = op_dtype != F32;
+  GemmWs ws;
+  int rc = carve_ws(workspace, workspace_bytes, segw_ws_bytes(n_routes, n_experts, m_dim, n_dim, tensor),
+                    n_routes, n_experts, &ws, "cvmm_backward_w");
+  if (rc) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   SegGemm p = {};
   p.x = x; p.x_dtype = x_dtype; p.x_ld = x_ld; p.x_index = x_index; p.x_div = x_div;
   p.g = g; p.g_dtype = g_dtype; p.g_ld = g_ld; p.g_index = g_index; p.g_div = g_div;
   p.w = w; p.w_dtype = w_dtype; p.w_index = w_index;
   p.offsets = offsets; p.n_routes = n_routes; p.n_experts = n_experts; p.M = m_dim; p.N = n_dim;
   p.out = grad_w; p.op_dtype = op_dtype;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return op_dtype == F32 ? launch_seg_gemm_simt(p, s) : launch_seg_gemm_umma(p, s);
+  p.chunk = segw_chunk(n_routes, n_experts, m_dim, n_dim, tensor);
+  p.units = static_cast<int4*>(ws.tiles);
+  p.n_units = ws.count;
+  p.partials = ws.partials;
+  rc = build_units(offsets, n_experts, p.chunk, static_cast<int4*>(ws.tiles), ws.count, ws.expert_slots, s);
+  if (rc) return rc;
+  if (n_routes > 0) {
+    const int64_t max_units = max_row_tiles(n_routes, n_experts, (int)p.chunk);
+    rc = tensor ? launch_seg_gemm_umma(p, max_units, s) : launch_seg_gemm_simt(p, max_units, s);
+    if (rc) return rc;
+  }
+  // Sums split experts' partial slots in chunk order and zero-fills experts
+  // without routes (the reference writes 0 for them, cvmm.py:476-478).
+  return seg_reduce(ws.expert_slots, ws.partials, grad_w, n_experts, m_dim * n_dim, s);
 }
 
 int cvmm_weighted_token_backward(const void* route_grad, int rg_dtype, const void* w, int w_dtype,

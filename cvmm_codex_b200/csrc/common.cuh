@@ -17,6 +17,12 @@ enum DType : int { F32 = CVMM_F32, F16 = CVMM_F16, BF16 = CVMM_BF16 };
 
 __host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 
+// Row index / divisor for non-negative 32-bit-range indices (every index
+// array here indexes fewer than 2^31 rows): avoids 64-bit division.
+__device__ __forceinline__ int64_t idx_div(int64_t v, int64_t d) {
+  return d == 1 ? v : (int64_t)((uint32_t)v / (uint32_t)d);
+}
+
 __host__ __device__ __forceinline__ int dtype_bytes(int dtype) {
   return dtype == F32 ? 4 : (dtype == CVMM_I64 ? 8 : (dtype == CVMM_I32 ? 4 : 2));
 }

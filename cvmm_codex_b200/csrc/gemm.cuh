@@ -42,6 +42,10 @@ struct SegGemm {
   int64_t n_routes, n_experts, M, N;
   float* out;
   int op_dtype;
+  int64_t chunk;        // routes per work unit (split-K)
+  const int4* units;    // (expert, first sorted position, partial slot or -1, 0)
+  const int* n_units;
+  float* partials;      // [slots][M][N] partial sums of split experts
 };
 
 __device__ __forceinline__ int64_t seg_begin(const int64_t* offsets, int64_t e) {
@@ -56,9 +60,13 @@ inline int64_t max_row_tiles(int64_t n_routes, int64_t n_experts, int bm) {
 // Host launchers (return a CVMM status).
 int build_tiles(const int64_t* offsets, int64_t n_experts, int bm, int2* tiles, int* n_tiles,
                 cudaStream_t stream);
+int build_units(const int64_t* offsets, int64_t n_experts, int64_t chunk, int4* units, int* n_units,
+                int2* expert_slots, cudaStream_t stream);
+int seg_reduce(const int2* expert_slots, const float* partials, float* out, int64_t n_experts, int64_t mn,
+               cudaStream_t stream);
 int launch_row_gemm_simt(const RowGemm& p, int64_t max_tiles, cudaStream_t stream);
-int launch_seg_gemm_simt(const SegGemm& p, cudaStream_t stream);
+int launch_seg_gemm_simt(const SegGemm& p, int64_t max_units, cudaStream_t stream);
 int launch_row_gemm_umma(const RowGemm& p, int64_t max_tiles, cudaStream_t stream);
-int launch_seg_gemm_umma(const SegGemm& p, cudaStream_t stream);
+int launch_seg_gemm_umma(const SegGemm& p, int64_t max_units, cudaStream_t stream);
 
 }  // namespace cvmm

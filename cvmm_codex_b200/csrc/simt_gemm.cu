@@ -55,6 +55,111 @@ int build_tiles(const int64_t* offsets, int64_t n_experts, int bm, int2* tiles, 
   return check_launch("build_tiles");
 }
 
+// Block-wide exclusive prefix of one int per thread (blockDim.x <= 1024).
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  int incl = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  __syncthreads();
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int s = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    warp_tot[lane] = s;
+  }
+  __syncthreads();
+  return incl - v + (warp > 0 ? warp_tot[warp - 1] : 0);
+}
+
+// Work units of the split-K grad-W: every expert segment is cut into chunks
+// of `chunk` routes. An expert with a single chunk writes grad_w directly
+// (slot -1); the chunks of a split expert write consecutive partial slots
+// that seg_reduce_kernel later sums in chunk order, so the result does not
+// depend on scheduling.
+__global__ void __launch_bounds__(1024)
+build_units_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int64_t chunk,
+                   int4* __restrict__ units, int* __restrict__ n_units, int2* __restrict__ expert_slots) {
+  __shared__ int warp_tot[32];
+  const int t = threadIdx.x;
+  const int64_t per = (n_experts + blockDim.x - 1) / blockDim.x;
+  const int64_t e0 = min((int64_t)t * per, n_experts), e1 = min(e0 + per, n_experts);
+  int cnt = 0, slots = 0;
+  for (int64_t e = e0; e < e1; ++e) {
+    const int64_t len = offsets[e] - seg_begin(offsets, e);
+    const int nch = (int)((len + chunk - 1) / chunk);
+    cnt += nch;
+    if (nch > 1) slots += nch;
+  }
+  int pos = block_exclusive_scan(cnt, warp_tot);
+  int sbase = block_exclusive_scan(slots, warp_tot);
+  for (int64_t e = e0; e < e1; ++e) {
+    const int64_t b = seg_begin(offsets, e), end = offsets[e];
+    const int nch = (int)((end - b + chunk - 1) / chunk);
+    expert_slots[e] = make_int2(nch > 1 ? sbase : -1, nch);
+    int c = 0;
+    for (int64_t r = b; r < end; r += chunk, ++c)
+      units[pos++] = make_int4((int)e, (int)r, nch > 1 ? sbase + c : -1, 0);
+    if (nch > 1) sbase += nch;
+  }
+  if (t == blockDim.x - 1) *n_units = pos;
+}
+
+int build_units(const int64_t* offsets, int64_t n_experts, int64_t chunk, int4* units, int* n_units,
+                int2* expert_slots, cudaStream_t stream) {
+  build_units_kernel<<<1, 1024, 0, stream>>>(offsets, n_experts, chunk, units, n_units, expert_slots);
+  return check_launch("build_units");
+}
+
+// grad_w[e] = sum over the expert's partial slots in chunk order (split
+// experts), or 0 for experts without routes; single-chunk experts were
+// written by their unit and are skipped.
+__global__ void seg_reduce_kernel(const int2* __restrict__ expert_slots, const float4* __restrict__ partials,
+                                  float4* __restrict__ out, int64_t mn4) {
+  const int64_t e = blockIdx.y;
+  const int2 es = expert_slots[e];
+  if (es.y == 1) return;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < mn4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c = 0; c < es.y; ++c) {
+      const float4 v = partials[(int64_t)(es.x + c) * mn4 + i];
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    out[e * mn4 + i] = acc;
+  }
+}
+
+__global__ void seg_reduce_scalar_kernel(const int2* __restrict__ expert_slots, const float* __restrict__ partials,
+                                         float* __restrict__ out, int64_t mn) {
+  const int64_t e = blockIdx.y;
+  const int2 es = expert_slots[e];
+  if (es.y == 1) return;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < mn; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int c = 0; c < es.y; ++c) acc += partials[(int64_t)(es.x + c) * mn + i];
+    out[e * mn + i] = acc;
+  }
+}
+
+int seg_reduce(const int2* expert_slots, const float* partials, float* out, int64_t n_experts, int64_t mn,
+               cudaStream_t stream) {
+  const bool vec = mn % 4 == 0 && ((uintptr_t)partials & 15u) == 0 && ((uintptr_t)out & 15u) == 0;
+  const int64_t work = vec ? mn / 4 : mn;
+  dim3 grid((unsigned)std::min<int64_t>((work + 255) / 256, 64), (unsigned)n_experts);
+  if (vec)
+    seg_reduce_kernel<<<grid, 256, 0, stream>>>(expert_slots, reinterpret_cast<const float4*>(partials),
+                                                reinterpret_cast<float4*>(out), mn / 4);
+  else
+    seg_reduce_scalar_kernel<<<grid, 256, 0, stream>>>(expert_slots, partials, out, mn);
+  return check_launch("seg_reduce");
+}
+
 // ---------------------------------------------------------------- fp32 row GEMM
 namespace simt {
 
@@ -78,7 +183,7 @@ __global__ void __launch_bounds__(THREADS) row_gemm_kernel(RowGemm p) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     int rr = (t >> 4) + 16 * i;
-    a_row[i] = rr < rows ? p.a_index[r0 + rr] / p.a_div : -1;
+    a_row[i] = rr < rows ? idx_div(p.a_index[r0 + rr], p.a_div) : -1;
   }
   const char* bbase = static_cast<const char*>(p.b);
   const size_t bsz = p.b_dtype == F32 ? 4 : 2;
@@ -149,10 +254,15 @@ __global__ void __launch_bounds__(THREADS) row_gemm_kernel(RowGemm p) {
 }
 
 // ---------------------------------------------------------------- fp32 segment GEMM
+// Split-K like the tensor-core kernel: one CTA per (work unit, m tile, n tile),
+// writing grad_w directly or the unit's partial slot.
 __global__ void __launch_bounds__(THREADS) seg_gemm_kernel(SegGemm p) {
-  const int64_t e = blockIdx.z;
-  const int64_t m0 = (int64_t)blockIdx.x * TM, n0 = (int64_t)blockIdx.y * TN;
-  const int64_t beg = seg_begin(p.offsets, e), end = p.offsets[e];
+  if ((int)blockIdx.x >= *p.n_units) return;
+  const int4 unit = p.units[blockIdx.x];
+  const int64_t e = unit.x;
+  const int64_t m0 = (int64_t)blockIdx.y * TM, n0 = (int64_t)blockIdx.z * TN;
+  const int64_t beg = unit.y, end = imin64(beg + p.chunk, p.offsets[e]);
+  float* dst_base = unit.z < 0 ? p.out + e * p.M * p.N : p.partials + (int64_t)unit.z * p.M * p.N;
   __shared__ float Xs[TK][TM + 4];
   __shared__ float Gs[TK][TN + 4];
   const int t = threadIdx.x;
@@ -167,11 +277,11 @@ __global__ void __launch_bounds__(THREADS) seg_gemm_kernel(SegGemm p) {
       float xv = 0.f, gv = 0.f;
       if (r < end) {
         if (m0 + mm < p.M) {
-          const int64_t xr = p.x_index[r] / p.x_div;
+          const int64_t xr = idx_div(p.x_index[r], p.x_div);
           xv = round_to(load_as_float(p.x, p.x_dtype, xr * p.x_ld + m0 + mm), p.op_dtype);
         }
         if (n0 + mm < p.N) {
-          const int64_t gr = p.g_index[r] / p.g_div;
+          const int64_t gr = idx_div(p.g_index[r], p.g_div);
           gv = round_to(load_as_float(p.g, p.g_dtype, gr * p.g_ld + n0 + mm), p.op_dtype);
           if (p.w) {
             const float wv = round_to(load_as_float(p.w, p.w_dtype, p.w_index[r]), p.op_dtype);
@@ -204,7 +314,7 @@ __global__ void __launch_bounds__(THREADS) seg_gemm_kernel(SegGemm p) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int64_t n = n0 + tx * 4 + j;
-      if (n < p.N) p.out[(e * p.M + m) * p.N + n] = acc[i][j];
+      if (n < p.N) dst_base[m * p.N + n] = acc[i][j];
     }
   }
 }
@@ -217,9 +327,9 @@ int launch_row_gemm_simt(const RowGemm& p, int64_t max_tiles, cudaStream_t strea
   return check_launch("row_gemm_simt");
 }
 
-int launch_seg_gemm_simt(const SegGemm& p, cudaStream_t stream) {
-  dim3 grid((unsigned)((p.M + simt::TM - 1) / simt::TM), (unsigned)((p.N + simt::TN - 1) / simt::TN),
-            (unsigned)p.n_experts);
+int launch_seg_gemm_simt(const SegGemm& p, int64_t max_units, cudaStream_t stream) {
+  dim3 grid((unsigned)max_units, (unsigned)((p.M + simt::TM - 1) / simt::TM),
+            (unsigned)((p.N + simt::TN - 1) / simt::TN));
   simt::seg_gemm_kernel<<<grid, simt::THREADS, 0, stream>>>(p);
   return check_launch("seg_gemm_simt");
 }

@@ -22,6 +22,8 @@
 // Every wait is bounded (ptx::mbar_wait); on a timeout the CTA records the
 // failure in the device status word, stops issuing work, waits for what it
 // already issued and frees its TMEM before returning.
+#include <stdlib.h>
+
 #include "gemm.cuh"
 #include "launch.h"
 #include "ptx.cuh"
@@ -34,6 +36,26 @@ constexpr int BK = 64;              // K per stage: one 128-byte swizzle atom of
 constexpr int kProducers = 128;
 constexpr int kThreads = 160;
 constexpr uint32_t kAtomRowsBytes = 64 * 128;  // one 64-row x 128-byte MN-major atom column
+
+// Development-only phase timestamps (compiled in with -DCVMM_TRACE; absent
+// from the shipped library).
+#ifdef CVMM_TRACE
+__device__ unsigned long long* g_trace;
+#define CVMM_TRACE_AT(slot)                                                                     \
+  do {                                                                                        \
+    if (g_trace) {                                                                            \
+      unsigned smid;                                                                          \
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));                                      \
+      const size_t b = blockIdx.x + (size_t)gridDim.x * (blockIdx.y + (size_t)gridDim.y * blockIdx.z); \
+      g_trace[b * 10 + (slot)] = globaltimer_ns();                                            \
+      g_trace[b * 10 + 9] = smid;                                                             \
+    }                                                                                         \
+  } while (0)
+#else
+#define CVMM_TRACE_AT(slot) \
+  do {                      \
+  } while (0)
+#endif
 
 // Wait-site tags reported with CVMM_DEV_TIMEOUT.
 enum : int { kTagEmpty = 1, kTagFull = 2, kTagAccum = 3 };
@@ -116,11 +138,40 @@ __device__ __forceinline__ void store_row32(void* c, int c_dtype, int64_t off, c
     if (j < ncols) store_from_float(c, c_dtype, off + j, v[j]);
 }
 
+// Multiplies this thread's G chunks of stage `j` by their route weights (kept
+// in `scales`) and rounds to the op dtype: the reference multiplies the bf16
+// grad row by the bf16 weight and rounds the product to bf16 before the dot
+// (cvmm.py:591-599).
+template <int BN, int S>
+__device__ __forceinline__ void scale_rows(uint8_t* smem, const float* scales, int j, int t, int op) {
+  using L = Smem<BN, S, true>;
+  constexpr int GCPR = BN / 8;
+  const int sj = j % S, sl = j % (S + 1);
+  const int gc = t % GCPR;
+  const uint32_t bj = ptx::smem_u32(smem + sj * L::stage_bytes) + L::a_bytes;
+#pragma unroll
+  for (int i = 0; i < BN / 16; ++i) {
+    const int kr = t / GCPR + (kProducers / GCPR) * i;
+    const float sc = scales[sl * 64 + kr];
+    const uint32_t addr = bj + swz(kr, gc, kAtomRowsBytes);
+    uint32_t w4[4];
+    ptx::ld_shared_v4(addr, w4[0], w4[1], w4[2], w4[3]);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float lo = bits_to_float((uint16_t)(w4[q] & 0xffffu), op) * sc;
+      const float hi = bits_to_float((uint16_t)(w4[q] >> 16), op) * sc;
+      w4[q] = (uint32_t)float_to_bits(lo, op) | ((uint32_t)float_to_bits(hi, op) << 16);
+    }
+    ptx::st_shared_v4(addr, w4[0], w4[1], w4[2], w4[3]);
+  }
+}
+
 // ============================================================ row-gathered GEMM
 // flags bit0: A fast path (cp.async), bit1: B fast path, bit2: C vector stores.
 template <int BN, int S, bool B_KMAJOR>
 __global__ void __launch_bounds__(kThreads, 1) row_gemm_kernel(RowGemm p, int flags) {
   if ((int)blockIdx.x >= *p.n_tiles) return;
+  if (threadIdx.x == 0) CVMM_TRACE_AT(0);
   using L = Smem<BN, S, false>;
   constexpr int LAG = S - 1;
   extern __shared__ uint8_t smem_raw[];
@@ -138,6 +189,11 @@ __global__ void __launch_bounds__(kThreads, 1) row_gemm_kernel(RowGemm p, int fl
   const int nkb = (int)((p.K + BK - 1) / BK);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool a_fast = flags & 1, b_fast = flags & 2, c_vec = flags & 4;
+#ifdef CVMM_TRACE
+  const bool dbg_no_mma = flags & 256, dbg_no_a = flags & 512, dbg_no_b = flags & 1024;
+#else
+  constexpr bool dbg_no_mma = false, dbg_no_a = false, dbg_no_b = false;
+#endif
   const int op = p.op_dtype;
 
   if (threadIdx.x == 0) {
@@ -157,6 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_gemm_kernel(RowGemm p, int fl
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) CVMM_TRACE_AT(1);
 
   if (warp < 4) {
     const int t = threadIdx.x;
@@ -167,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_gemm_kernel(RowGemm p, int fl
     for (int i = 0; i < 8; ++i) {
       const int rr = (t >> 3) + 16 * i;
       a_rows[i] = rr < rows ? static_cast<const char*>(p.a) +
-                                  (p.a_index[r0 + rr] / p.a_div) * p.a_ld * (int64_t)dtype_bytes(p.a_dtype)
+                                  idx_div(p.a_index[r0 + rr], p.a_div) * p.a_ld * (int64_t)dtype_bytes(p.a_dtype)
                             : nullptr;
     }
     const char* bbase = static_cast<const char*>(p.b);
@@ -197,9 +254,11 @@ __global__ void __launch_bounds__(kThreads, 1) row_gemm_kernel(RowGemm p, int fl
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int rr = (t >> 3) + 16 * i;
-        load_chunk(a_u + swz(rr, ac, 0), a_rows[i], k0 + ac * 8, p.K, p.a_dtype, 1, op, a_fast, p.a);
+        if (!dbg_no_a)
+          load_chunk(a_u + swz(rr, ac, 0), a_rows[i], k0 + ac * 8, p.K, p.a_dtype, 1, op, a_fast, p.a);
       }
-      if (B_KMAJOR) {
+      if (dbg_no_b) {
+      } else if (B_KMAJOR) {
 #pragma unroll
         for (int i = 0; i < BKR; ++i) {
           const int nr = (t >> 3) + 16 * i;
@@ -218,12 +277,14 @@ __global__ void __launch_bounds__(kThreads, 1) row_gemm_kernel(RowGemm p, int fl
         }
       }
       ptx::cp_async_commit();
+      if (t == 0 && kb == 0) CVMM_TRACE_AT(2);
       if (kb >= LAG) {
         ptx::cp_async_wait<LAG>();
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(&full[(kb - LAG) % S]);
       }
     }
+    if (t == 0) CVMM_TRACE_AT(3);
     ptx::cp_async_wait_all();
     ptx::fence_proxy_async_smem();
     if (!aborted)
@@ -235,6 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_gemm_kernel(RowGemm p, int fl
     const int64_t c_row = row_ok ? p.c_index[r0 + rr] : 0;
     const bool have_acc = nkb > 0 && ptx::mbar_wait(accum, 0, kTagAccum) && *abort_flag == 0;
     ptx::tc_fence_after();
+    if (t == 0) CVMM_TRACE_AT(6);
     float wv = 0.f, dot = 0.f;
     if (p.mode == 1 && row_ok) wv = round_to(load_as_float(p.w, p.w_dtype, c_row), op);
     for (int ch = 0; ch < BN / 32; ++ch) {
@@ -274,20 +336,23 @@ __global__ void __launch_bounds__(kThreads, 1) row_gemm_kernel(RowGemm p, int fl
         break;
       }
       ptx::tc_fence_after();
+      if (kb == 0) CVMM_TRACE_AT(4);
       const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes), b_u = a_u + L::a_bytes;
 #pragma unroll
       for (int j = 0; j < BK / 16; ++j) {
         const uint64_t ad = ptx::smem_desc_sw128(a_u + j * 32, 16, 1024);
         const uint64_t bd = B_KMAJOR ? ptx::smem_desc_sw128(b_u + j * 32, 16, 1024)
                                      : ptx::smem_desc_sw128(b_u + j * 2048, kAtomRowsBytes, 1024);
-        ptx::mma_f16(tmem, ad, bd, idesc, (kb | j) != 0 ? 1u : 0u);
+        if (!dbg_no_mma) ptx::mma_f16(tmem, ad, bd, idesc, (kb | j) != 0 ? 1u : 0u);
       }
       ptx::mma_commit(&empty[s]);
     }
     ptx::mma_commit(accum);
+    CVMM_TRACE_AT(5);
   }
   ptx::tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) CVMM_TRACE_AT(7);
   if (warp == 4) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, BN);
@@ -295,11 +360,18 @@ __global__ void __launch_bounds__(kThreads, 1) row_gemm_kernel(RowGemm p, int fl
 }
 
 // ============================================================ segment GEMM (grad-W)
+// Split-K over each expert segment: a work unit is (expert, chunk of at most
+// p.chunk sorted routes) x (m tile) x (n tile), so a heavily loaded expert is
+// spread over many CTAs instead of one CTA walking its whole segment. Partial
+// sums go to per-chunk slots and are reduced in a fixed order (deterministic).
 // flags bit0: X fast path, bit1: G fast path, bit2: out vector stores.
 template <int BN, int S, bool WEIGHTED>
 __global__ void __launch_bounds__(kThreads, 1) seg_gemm_kernel(SegGemm p, int flags) {
+  if ((int)blockIdx.x >= *p.n_units) return;
   using L = Smem<BN, S, WEIGHTED>;
   constexpr int LAG = S - 1;
+  constexpr int GCPR = BN / 8;            // G tile: 16-byte chunks per route row
+  constexpr int GROWS = BN / 16;          // G rows per producer thread per stage
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_smem(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bars);
@@ -309,9 +381,11 @@ __global__ void __launch_bounds__(kThreads, 1) seg_gemm_kernel(SegGemm p, int fl
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::misc + 4);
   float* scales = reinterpret_cast<float*>(smem + L::scales);
 
-  const int64_t e = blockIdx.z;
-  const int64_t m0 = (int64_t)blockIdx.x * BM, n0 = (int64_t)blockIdx.y * BN;
-  const int64_t beg = seg_begin(p.offsets, e), end = p.offsets[e];
+  const int4 unit = p.units[blockIdx.x];
+  const int64_t e = unit.x;
+  const int64_t beg = unit.y;
+  const int64_t end = imin64(beg + p.chunk, p.offsets[e]);
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.z * BN;
   const int nkb = (int)((end - beg + BK - 1) / BK);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool x_fast = flags & 1, g_fast = flags & 2, o_vec = flags & 4;
@@ -340,9 +414,26 @@ __global__ void __launch_bounds__(kThreads, 1) seg_gemm_kernel(SegGemm p, int fl
     const char* xbase = static_cast<const char*>(p.x);
     const char* gbase = static_cast<const char*>(p.g);
     const int64_t xsz = dtype_bytes(p.x_dtype), gsz = dtype_bytes(p.g_dtype);
-    constexpr int GCPR = BN / 8;
     const int xc = t & 15;       // X tile: 64 route rows x 16 chunks (128 m columns)
     const int gc = t % GCPR;     // G tile: 64 route rows x GCPR chunks
+    // Row indices of the next stage are loaded one stage ahead so that their
+    // latency overlaps the copies of the current stage.
+    int64_t xi[8], gi[GROWS], wi[GROWS];
+    auto fetch = [&](int kb) {
+      const int64_t rb = beg + (int64_t)kb * BK;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int64_t r = rb + (t >> 4) + 8 * i;
+        xi[i] = r < end ? p.x_index[r] : -1;
+      }
+#pragma unroll
+      for (int i = 0; i < GROWS; ++i) {
+        const int64_t r = rb + t / GCPR + (kProducers / GCPR) * i;
+        gi[i] = r < end ? p.g_index[r] : -1;
+        if (WEIGHTED) wi[i] = r < end ? p.w_index[r] : -1;
+      }
+    };
+    if (nkb > 0) fetch(0);
     bool aborted = false;
     for (int kb = 0; kb < nkb; ++kb) {
       const int s = kb % S;
@@ -355,104 +446,70 @@ __global__ void __launch_bounds__(kThreads, 1) seg_gemm_kernel(SegGemm p, int fl
         aborted = true;
         break;
       }
+      const char* xrow[8];
+      const char* grow[GROWS];
+      float wsc[GROWS];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        xrow[i] = xi[i] >= 0 ? xbase + (idx_div(xi[i], p.x_div) * p.x_ld + m0) * xsz : nullptr;
+#pragma unroll
+      for (int i = 0; i < GROWS; ++i) {
+        grow[i] = gi[i] >= 0 ? gbase + (idx_div(gi[i], p.g_div) * p.g_ld + n0) * gsz : nullptr;
+        if (WEIGHTED) wsc[i] = wi[i] >= 0 ? round_to(load_as_float(p.w, p.w_dtype, wi[i]), op) : 0.f;
+      }
+      if (kb + 1 < nkb) fetch(kb + 1);
       const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes), b_u = a_u + L::a_bytes;
-      const int64_t rbase = beg + (int64_t)kb * BK;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int kr = (t >> 4) + 8 * i;
-        const int64_t r = rbase + kr;
-        const char* row = r < end ? xbase + ((p.x_index[r] / p.x_div) * p.x_ld + m0) * xsz : nullptr;
-        load_chunk(a_u + swz(kr, xc, kAtomRowsBytes), row, xc * 8, p.M - m0, p.x_dtype, 1, op,
+        load_chunk(a_u + swz(kr, xc, kAtomRowsBytes), xrow[i], xc * 8, p.M - m0, p.x_dtype, 1, op,
                    x_fast, p.x);
       }
 #pragma unroll
-      for (int i = 0; i < BN / 16; ++i) {
+      for (int i = 0; i < GROWS; ++i) {
         const int kr = t / GCPR + (kProducers / GCPR) * i;
-        const int64_t r = rbase + kr;
-        const char* row = r < end ? gbase + ((p.g_index[r] / p.g_div) * p.g_ld + n0) * gsz : nullptr;
-        load_chunk(b_u + swz(kr, gc, kAtomRowsBytes), row, gc * 8, p.N - n0, p.g_dtype, 1, op,
+        load_chunk(b_u + swz(kr, gc, kAtomRowsBytes), grow[i], gc * 8, p.N - n0, p.g_dtype, 1, op,
                    g_fast, p.g);
-        if (WEIGHTED && gc == 0)
-          scales[(kb % (S + 1)) * 64 + kr] = r < end ? round_to(load_as_float(p.w, p.w_dtype, p.w_index[r]), op) : 0.f;
+        if (WEIGHTED && gc == 0) scales[(kb % (S + 1)) * 64 + kr] = wsc[i];
       }
       ptx::cp_async_commit();
       if (WEIGHTED) ptx::named_bar_sync(1, kProducers);
       if (kb >= LAG) {
         ptx::cp_async_wait<LAG>();
-        if (WEIGHTED) {
-          // Scale this thread's own G chunks of stage kb-LAG by bf16(w): the
-          // reference multiplies the bf16 grad row by the bf16 weight and
-          // rounds the product to bf16 before the dot (cvmm.py:591-599).
-          const int sj = (kb - LAG) % S, sl = (kb - LAG) % (S + 1);
-          const uint32_t bj = ptx::smem_u32(smem + sj * L::stage_bytes) + L::a_bytes;
-#pragma unroll
-          for (int i = 0; i < BN / 16; ++i) {
-            const int kr = t / GCPR + (kProducers / GCPR) * i;
-            const float sc = scales[sl * 64 + kr];
-            const uint32_t addr = bj + swz(kr, gc, kAtomRowsBytes);
-            uint32_t w4[4];
-            ptx::ld_shared_v4(addr, w4[0], w4[1], w4[2], w4[3]);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              float lo = bits_to_float((uint16_t)(w4[q] & 0xffffu), op) * sc;
-              float hi = bits_to_float((uint16_t)(w4[q] >> 16), op) * sc;
-              w4[q] = (uint32_t)float_to_bits(lo, op) | ((uint32_t)float_to_bits(hi, op) << 16);
-            }
-            ptx::st_shared_v4(addr, w4[0], w4[1], w4[2], w4[3]);
-          }
-        }
+        if (WEIGHTED) scale_rows<BN, S>(smem, scales, kb - LAG, t, op);
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(&full[(kb - LAG) % S]);
       }
     }
     ptx::cp_async_wait_all();
-    if (WEIGHTED && !aborted) {
-      for (int j = max(0, nkb - LAG); j < nkb; ++j) {
-        const int sj = j % S, sl = j % (S + 1);
-        const uint32_t bj = ptx::smem_u32(smem + sj * L::stage_bytes) + L::a_bytes;
-#pragma unroll
-        for (int i = 0; i < BN / 16; ++i) {
-          const int kr = t / GCPR + (kProducers / GCPR) * i;
-          const float sc = scales[sl * 64 + kr];
-          const uint32_t addr = bj + swz(kr, gc, kAtomRowsBytes);
-          uint32_t w4[4];
-          ptx::ld_shared_v4(addr, w4[0], w4[1], w4[2], w4[3]);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            float lo = bits_to_float((uint16_t)(w4[q] & 0xffffu), op) * sc;
-            float hi = bits_to_float((uint16_t)(w4[q] >> 16), op) * sc;
-            w4[q] = (uint32_t)float_to_bits(lo, op) | ((uint32_t)float_to_bits(hi, op) << 16);
-          }
-          ptx::st_shared_v4(addr, w4[0], w4[1], w4[2], w4[3]);
-        }
-      }
-    }
+    if (WEIGHTED && !aborted)
+      for (int j = max(0, nkb - LAG); j < nkb; ++j) scale_rows<BN, S>(smem, scales, j, t, op);
     ptx::fence_proxy_async_smem();
     if (!aborted)
       for (int j = max(0, nkb - LAG); j < nkb; ++j) ptx::mbar_arrive(&full[j % S]);
 
-    // ---- epilogue: TMEM lane = m row of this expert's grad tile.
+    // ---- epilogue: TMEM lane = m row of this expert's grad tile. A unit that
+    // covers its whole expert writes grad_w; a chunk of a split expert writes
+    // its partial slot (summed in order by seg_reduce).
     const int mr = warp * 32 + lane;
     const int64_t m = m0 + mr;
     const bool have_acc = nkb > 0 && ptx::mbar_wait(accum, 0, kTagAccum) && *abort_flag == 0;
     ptx::tc_fence_after();
-    for (int ch = 0; ch < BN / 32; ++ch) {
-      const int64_t nc = n0 + ch * 32;
-      if (nc >= p.N) break;
-      const int ncols = (int)imin64(32, p.N - nc);
-      float v[32];
-      if (have_acc) {
+    float* dst_base = unit.z < 0 ? p.out + e * p.M * p.N : p.partials + (int64_t)unit.z * p.M * p.N;
+    if (have_acc) {
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        const int64_t nc = n0 + ch * 32;
+        if (nc >= p.N) break;
+        const int ncols = (int)imin64(32, p.N - nc);
         uint32_t r[32];
         ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + ch * 32, r);
         ptx::tmem_wait_ld();
+        if (m >= p.M) continue;
+        float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        store_row32(dst_base, F32, m * p.N + nc, v, ncols, o_vec);
       }
-      if (m >= p.M || (nkb > 0 && !have_acc)) continue;
-      store_row32(p.out, F32, (e * p.M + m) * p.N + nc, v, ncols, o_vec);
     }
   } else if (warp == 4 && lane == 0) {
     const uint32_t idesc = ptx::instr_desc_f16(BM, BN, op == BF16, true, true);
@@ -504,17 +561,24 @@ static int row_launch(const RowGemm& p, int64_t max_tiles, int flags, cudaStream
 }
 
 template <int BN, int S, bool W>
-static int seg_launch(const SegGemm& p, int flags, cudaStream_t stream) {
+static int seg_launch(const SegGemm& p, int64_t max_units, int flags, cudaStream_t stream) {
   using L = Smem<BN, S, W>;
   auto kern = seg_gemm_kernel<BN, S, W>;
   int rc = set_smem(kern, L::alloc);
   if (rc) return rc;
-  dim3 grid((unsigned)((p.M + BM - 1) / BM), (unsigned)((p.N + BN - 1) / BN), (unsigned)p.n_experts);
+  dim3 grid((unsigned)max_units, (unsigned)((p.M + BM - 1) / BM), (unsigned)((p.N + BN - 1) / BN));
   kern<<<grid, kThreads, L::alloc, stream>>>(p, flags);
   return check_launch("seg_gemm_umma");
 }
 
 }  // namespace umma
+
+#ifdef CVMM_TRACE
+extern "C" int cvmm_debug_set_trace(void* buf) {
+  unsigned long long* p = static_cast<unsigned long long*>(buf);
+  return cudaMemcpyToSymbol(umma::g_trace, &p, sizeof(p)) == cudaSuccess ? 0 : -3;
+}
+#endif
 
 int launch_row_gemm_umma(const RowGemm& p, int64_t max_tiles, cudaStream_t stream) {
   using namespace umma;
@@ -525,6 +589,9 @@ int launch_row_gemm_umma(const RowGemm& p, int64_t max_tiles, cudaStream_t strea
       (b_kmajor ? (p.bs_k == 1 && p.bs_n % 8 == 0) : (p.bs_n == 1 && p.bs_k % 8 == 0)))
     flags |= 2;
   if (p.c_ld % 8 == 0 && aligned16(p.c)) flags |= 4;
+#ifdef CVMM_TRACE
+  if (const char* e = getenv("CVMM_DBG_FLAGS")) flags |= atoi(e);
+#endif
   if (p.N <= 64) {
     return b_kmajor ? row_launch<64, 6, true>(p, max_tiles, flags, stream)
                     : row_launch<64, 6, false>(p, max_tiles, flags, stream);
@@ -536,16 +603,16 @@ int launch_row_gemm_umma(const RowGemm& p, int64_t max_tiles, cudaStream_t strea
                   : row_launch<256, 4, false>(p, max_tiles, flags, stream);
 }
 
-int launch_seg_gemm_umma(const SegGemm& p, cudaStream_t stream) {
+int launch_seg_gemm_umma(const SegGemm& p, int64_t max_units, cudaStream_t stream) {
   using namespace umma;
   int flags = 0;
   if (p.x_dtype == p.op_dtype && p.x_ld % 8 == 0 && aligned16(p.x)) flags |= 1;
   if (p.g_dtype == p.op_dtype && p.g_ld % 8 == 0 && aligned16(p.g)) flags |= 2;
-  if (p.N % 4 == 0 && aligned16(p.out)) flags |= 4;
+  if (p.N % 4 == 0 && aligned16(p.out) && aligned16(p.partials)) flags |= 4;
   const bool w = p.w != nullptr;
-  if (p.N <= 64) return w ? seg_launch<64, 6, true>(p, flags, stream) : seg_launch<64, 6, false>(p, flags, stream);
-  if (p.N <= 128) return w ? seg_launch<128, 4, true>(p, flags, stream) : seg_launch<128, 4, false>(p, flags, stream);
-  return w ? seg_launch<256, 4, true>(p, flags, stream) : seg_launch<256, 4, false>(p, flags, stream);
+  if (p.N <= 64) return w ? seg_launch<64, 6, true>(p, max_units, flags, stream) : seg_launch<64, 6, false>(p, max_units, flags, stream);
+  if (p.N <= 128) return w ? seg_launch<128, 4, true>(p, max_units, flags, stream) : seg_launch<128, 4, false>(p, max_units, flags, stream);
+  return w ? seg_launch<256, 4, true>(p, max_units, flags, stream) : seg_launch<256, 4, false>(p, max_units, flags, stream);
 }
 
 }  // namespace cvmm

@@ -18,7 +18,7 @@ from ._lib import check, dtype_code, ptr
 # Kernels each native entry point launches (for launch accounting).
 KERNELS_PER_CALL = {
     "cvmm_sel_prepare": 10, "cvmm_expert_offsets": 1, "cvmm_forward": 2, "cvmm_backward_x": 2,
-    "cvmm_backward_w": 1, "cvmm_weighted_combine": 1, "cvmm_sum_routes": 1,
+    "cvmm_backward_w": 3, "cvmm_weighted_combine": 1, "cvmm_sum_routes": 1,
     "cvmm_weighted_token_backward": 1, "cvmm_cast": 1,
 }
 
@@ -151,8 +151,9 @@ def expert_offsets(sorted_sel: torch.Tensor, n_experts: int) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------ GEMMs
-def _gemm_ws(lib, n_routes, n_experts, dev):
-    return _ws(lib.cvmm_gemm_workspace_size(n_routes, n_experts, 0, 0, 0, 0, 0, 0), dev)
+def _gemm_ws(lib, n_routes, n_experts, dev, m_dim=0, n_dim=0, op_dtype=torch.bfloat16):
+    return _ws(lib.cvmm_gemm_workspace_size(n_routes, n_experts, m_dim, n_dim, 0, 0,
+                                            dtype_code(op_dtype), 0), dev)
 
 
 def forward(x: torch.Tensor, sel_index: torch.Tensor, offsets: torch.Tensor, keys: torch.Tensor,
@@ -263,12 +264,13 @@ def backward_w(x: torch.Tensor, x_index: torch.Tensor, x_div: int, g: torch.Tens
     M, N = x2.shape[1], g2.shape[1]
     out = torch.empty((int(n_experts), M, N), dtype=torch.float32, device=x.device)
     w2 = None if w is None else w.reshape(-1).contiguous()
+    ws = _gemm_ws(lib, n_routes, int(n_experts), x.device, M, N, op_dtype)
     with _Device(x.device) as stream:
         rc = _invoke("cvmm_backward_w", lib.cvmm_backward_w, ptr(x2), dtype_code(x2.dtype), x2.stride(0), ptr(x_index), int(x_div),
                                  ptr(g2), dtype_code(g2.dtype), g2.stride(0), ptr(g_index), int(g_div),
                                  ptr(w2), dtype_code(w2.dtype) if w2 is not None else 0, ptr(w_index),
                                  ptr(offsets), n_routes, int(n_experts), M, N, ptr(out),
-                                 dtype_code(op_dtype), None, 0, stream)
+                                 dtype_code(op_dtype), ptr(ws), ws.numel(), stream)
     check(rc, "cvmm_backward_w")
     return out
 

@@ -99,6 +99,10 @@ int cvmm_expert_offsets(const int32_t* sorted_sel, int64_t n_routes, int64_t n_e
  * tensor cores (operands rounded to op_dtype, fp32 accumulate), CVMM_F32 runs
  * an exact fp32 FFMA kernel (the reference's allow_tf32=False path).
  * ------------------------------------------------------------------------ */
+/* Workspace bytes that suffice for cvmm_forward, cvmm_backward_x and
+ * cvmm_backward_w on n_routes routes over n_experts experts with
+ * keys[e] of shape [k_dim, n_dim] (pass k_dim = n_dim = 0 for the
+ * forward / grad-input tile table alone). */
 size_t cvmm_gemm_workspace_size(int64_t n_routes, int64_t n_experts, int64_t k_dim,
                                 int64_t n_dim, int x_dtype, int keys_dtype, int op_dtype,
                                 int64_t x_rows);
@@ -144,7 +148,10 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
  *   grad_w[e][m][n] = sum_{p in seg(e)} op(x[x_index[p]/x_div][m]) * s_p * op(g[g_index[p]/g_div][n])
  *   s_p = 1, or with w != NULL: the g row is first multiplied by op(w[w_index[p]])
  *   and rounded to op_dtype (cvmm.py:591-599).
- * grad_w: [n_experts, m_dim, n_dim] fp32, fully written (empty experts get 0). */
+ * grad_w: [n_experts, m_dim, n_dim] fp32, fully written (empty experts get 0).
+ * Long expert segments are split over several CTAs (split-K); their partial
+ * sums live in the workspace (cvmm_gemm_workspace_size with k_dim = m_dim)
+ * and are added in a fixed order, so results are deterministic. */
 int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_index,
                     int64_t x_div, const void* g, int g_dtype, int64_t g_ld,
                     const int64_t* g_index, int64_t g_div, const void* w, int w_dtype,
