@@ -38,6 +38,7 @@ SIGNATURES = {
     "cvmm_device_status": (_I, [_I, ctypes.POINTER(_I), ctypes.POINTER(ctypes.c_longlong), _P]),
     "cvmm_sel_prepare_workspace_size": (_S, [_L]),
     "cvmm_sel_prepare": (_I, [_P, _I, _L, _L, _I, _P, _P, _P, _P, _P, _S, _P]),
+    "cvmm_sel_prepare_noalloc": (_I, [_P, _I, _L, _L, _I, _P, _P, _P, _P, _P]),
     "cvmm_expert_offsets": (_I, [_P, _L, _L, _P, _P]),
     "cvmm_gemm_workspace_size": (_S, [_L, _L, _L, _L, _I, _I, _I, _L]),
     "cvmm_forward": (_I, [_P, _I, _L, _L, _P, _P, _P, _L, _P, _I, _L, _L, _L, _L, _L, _L,

@@ -3,5 +3,6 @@
 // with relocatable device code.
 #include "abi.cu"
 #include "sel_prep.cu"
+#include "sel_prep_noalloc.cu"
 #include "simt_gemm.cu"
 #include "umma_gemm.cu"

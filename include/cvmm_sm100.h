@@ -79,6 +79,23 @@ int cvmm_sel_prepare(const void* sel, int sel_dtype, int64_t n_routes, int64_t t
                      int64_t* sel_index, int64_t* out_index, void* workspace,
                      size_t workspace_bytes, cvmm_stream_t stream);
 
+/* Allocation-free cvmm_sel_prepare, for callers that cannot allocate device
+ * memory on the call path (a host owning all device memory through its own
+ * fixed plan, a serving loop that must not call cudaMalloc because it can
+ * synchronise the device). It has no counterpart in the reference.
+ * Same arguments and results as cvmm_sel_prepare minus the workspace: the
+ * scratch is a static device array of about 1.5 MiB that every GPU loading
+ * the library keeps until exit, so n_routes is limited to
+ * CVMM_NOALLOC_MAX_ROUTES (larger inputs return CVMM_ERR_INVALID_ARG).
+ * The first call on a device looks up that array's address with that device
+ * current; make that first call before any stream capture. All calls share
+ * the one array, so calls whose work overlaps on the GPU (different streams,
+ * or different host threads) race and must be serialised by the caller. */
+#define CVMM_NOALLOC_MAX_ROUTES 65536
+int cvmm_sel_prepare_noalloc(const void* sel, int sel_dtype, int64_t n_routes, int64_t top_k,
+                             int route_input, int32_t* raw_sel, int32_t* sorted_sel,
+                             int64_t* sel_index, int64_t* out_index, cvmm_stream_t stream);
+
 /* Inclusive end offset of every expert's segment in sorted order:
  * offsets[e] = #routes with expert <= e (missing experts repeat the previous
  * value). Replaces _cvmm_expert_offsets / cvmm_expert_offsets_kernel
