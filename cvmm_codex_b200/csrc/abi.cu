@@ -195,7 +195,7 @@ static int run_row_gemm(RowGemm& p, void* ws, size_t ws_bytes, cudaStream_t stre
   if (rc) return rc;
   const bool tensor = p.op_dtype != F32;
   const int bm = tensor ? 128 : 64;
-  int2* tiles = static_cast<int2*>(g.tiles);
+  int4* tiles = static_cast<int4*>(g.tiles);
   rc = build_tiles(p.offsets, p.n_experts, bm, tiles, g.count, stream);
   if (rc) return rc;
   p.tiles = tiles;
@@ -272,7 +272,8 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld, const
       out_ld < n_dim)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: bad sizes");
   if (n_routes == 0) return CVMM_OK;
-  if (n_routes > (int64_t)INT32_MAX) return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: too many routes");
+  if (n_routes > (int64_t)INT32_MAX || x_rows > (int64_t)INT32_MAX)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: more than 2^31 routes or rows");
   if (!x || !sel_index || !offsets || !keys || !out)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: null pointer");
   RowGemm p = {};

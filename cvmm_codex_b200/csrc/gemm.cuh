@@ -26,7 +26,7 @@ struct RowGemm {
   const void* x; int x_dtype; int64_t x_ld;
   float* gsel;
   int op_dtype;
-  const int2* tiles;   // (expert, first sorted position) per M tile
+  const int4* tiles;   // (expert, first sorted position, rows, 0) per M tile
   const int* n_tiles;  // number of valid entries in `tiles`
 };
 
@@ -43,7 +43,7 @@ struct SegGemm {
   float* out;
   int op_dtype;
   int64_t chunk;        // routes per work unit (split-K)
-  const int4* units;    // (expert, first sorted position, partial slot or -1, 0)
+  const int4* units;    // (expert, first sorted position, partial slot or -1, end position)
   const int* n_units;
   float* partials;      // [slots][M][N] partial sums of split experts
 };
@@ -58,7 +58,7 @@ inline int64_t max_row_tiles(int64_t n_routes, int64_t n_experts, int bm) {
 }
 
 // Host launchers (return a CVMM status).
-int build_tiles(const int64_t* offsets, int64_t n_experts, int bm, int2* tiles, int* n_tiles,
+int build_tiles(const int64_t* offsets, int64_t n_experts, int bm, int4* tiles, int* n_tiles,
                 cudaStream_t stream);
 int build_units(const int64_t* offsets, int64_t n_experts, int64_t chunk, int4* units, int* n_units,
                 int2* expert_slots, cudaStream_t stream);

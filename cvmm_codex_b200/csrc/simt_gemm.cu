@@ -14,7 +14,7 @@ namespace cvmm {
 // and a block scan turns the counts into the write positions.
 __global__ void __launch_bounds__(1024)
 build_tiles_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int bm,
-                   int2* __restrict__ tiles, int* __restrict__ n_tiles) {
+                   int4* __restrict__ tiles, int* __restrict__ n_tiles) {
   const int t = threadIdx.x;
   const int64_t per = (n_experts + blockDim.x - 1) / blockDim.x;
   const int64_t e0 = min((int64_t)t * per, n_experts), e1 = min(e0 + per, n_experts);
@@ -44,12 +44,12 @@ build_tiles_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int b
   int pos = v - cnt + (warp > 0 ? warp_tot[warp - 1] : 0);
   for (int64_t e = e0; e < e1; ++e) {
     int64_t b = seg_begin(offsets, e), end = offsets[e];
-    for (int64_t r = b; r < end; r += bm) tiles[pos++] = make_int2((int)e, (int)r);
+    for (int64_t r = b; r < end; r += bm) tiles[pos++] = make_int4((int)e, (int)r, (int)min((int64_t)bm, end - r), 0);
   }
   if (t == blockDim.x - 1) *n_tiles = pos;
 }
 
-int build_tiles(const int64_t* offsets, int64_t n_experts, int bm, int2* tiles, int* n_tiles,
+int build_tiles(const int64_t* offsets, int64_t n_experts, int bm, int4* tiles, int* n_tiles,
                 cudaStream_t stream) {
   build_tiles_kernel<<<1, 1024, 0, stream>>>(offsets, n_experts, bm, tiles, n_tiles);
   return check_launch("build_tiles");
@@ -105,7 +105,7 @@ build_units_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int64
     expert_slots[e] = make_int2(nch > 1 ? sbase : -1, nch);
     int c = 0;
     for (int64_t r = b; r < end; r += chunk, ++c)
-      units[pos++] = make_int4((int)e, (int)r, nch > 1 ? sbase + c : -1, 0);
+      units[pos++] = make_int4((int)e, (int)r, nch > 1 ? sbase + c : -1, (int)min(r + chunk, end));
     if (nch > 1) sbase += nch;
   }
   if (t == blockDim.x - 1) *n_units = pos;
@@ -167,10 +167,9 @@ constexpr int TM = 64, TN = 64, TK = 16, THREADS = 256;
 
 __global__ void __launch_bounds__(THREADS) row_gemm_kernel(RowGemm p) {
   if ((int)blockIdx.x >= *p.n_tiles) return;
-  const int2 tile = p.tiles[blockIdx.x];
+  const int4 tile = p.tiles[blockIdx.x];
   const int64_t e = tile.x, r0 = tile.y;
-  const int64_t seg_end = p.offsets[e];
-  const int rows = (int)imin64(TM, seg_end - r0);
+  const int rows = tile.z;
   const int64_t n0 = (int64_t)blockIdx.y * TN;
 
   __shared__ float As[TK][TM + 4];
@@ -261,7 +260,7 @@ __global__ void __launch_bounds__(THREADS) seg_gemm_kernel(SegGemm p) {
   const int4 unit = p.units[blockIdx.x];
   const int64_t e = unit.x;
   const int64_t m0 = (int64_t)blockIdx.y * TM, n0 = (int64_t)blockIdx.z * TN;
-  const int64_t beg = unit.y, end = imin64(beg + p.chunk, p.offsets[e]);
+  const int64_t beg = unit.y, end = unit.w;
   float* dst_base = unit.z < 0 ? p.out + e * p.M * p.N : p.partials + (int64_t)unit.z * p.M * p.N;
   __shared__ float Xs[TK][TM + 4];
   __shared__ float Gs[TK][TN + 4];

@@ -1,16 +1,21 @@
 // tcgen05 (5th-generation tensor core) grouped GEMMs for bf16/fp16 arithmetic.
 //
-// Both kernels are warp-specialised, one output tile per CTA:
-//   warps 0-3 (128 threads): producers, then epilogue. They gather operand
-//     rows with 16-byte cp.async straight into the 128-byte-swizzled
-//     shared-memory layout tcgen05.mma reads (zero-filling ragged edges), and
-//     after the accumulator is complete read it back from TMEM (one TMEM lane
-//     = one output row per thread) and store it.
-//   warp 4: allocates the TMEM accumulator; its lane 0 issues tcgen05.mma
-//     (M=128, N=BN, K=16 per instruction) and tcgen05.commit.
-// Stages are handed over with mbarriers: full[s] (128 producer arrivals, after
-// each producer's copies landed and a generic->async proxy fence) and empty[s]
-// (tcgen05.commit when the MMAs reading stage s finished).
+// Both kernels are persistent and warp-specialised (320 threads, one CTA per
+// SM, tiles assigned round-robin):
+//   warps 0-3  producers: gather the operand rows of every stage with 16-byte
+//              cp.async straight into the 128-byte-swizzled shared-memory
+//              layout tcgen05.mma reads (zero-filling ragged edges), then hand
+//              the stage over with cp.async.mbarrier.arrive.noinc, which
+//              arrives on the stage's `full` barrier when the copies land, so
+//              the producers never wait for their own loads;
+//   warps 4-7  epilogue: read finished accumulators from TMEM (one TMEM lane =
+//              one output row per thread), convert and store them;
+//   warp 8     allocates TMEM (two accumulator slots) and its lane 0 issues
+//              tcgen05.mma (M=128, N=BN, K=16) and tcgen05.commit;
+//   warp 9     lane 0 loads the expert-weight tiles with TMA (row GEMM).
+// Barriers: full[s] / empty[s] per smem stage (S stages), acc_full[a] /
+// acc_empty[a] per TMEM accumulator slot (2 slots), so the epilogue of tile i
+// overlaps the main loop of tile i+1.
 //
 // Row gathering is the heart of CVMM: the A rows of a forward tile are
 // x[sel_index[p]] for 128 consecutive sorted routes p of one expert, so no
@@ -19,10 +24,14 @@
 // unlike the reference kernel which re-runs the K loop per expert present in
 // a tile (cvmm.py:167,236-238).
 //
-// Every wait is bounded (ptx::mbar_wait); on a timeout the CTA records the
-// failure in the device status word, stops issuing work, waits for what it
-// already issued and frees its TMEM before returning.
+// Every wait is bounded; on a timeout the CTA records the failure in the
+// device status word, stops issuing work, lets what it issued finish and
+// frees its TMEM before returning.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <stdlib.h>
+
+#include <mutex>
 
 #include "gemm.cuh"
 #include "launch.h"
@@ -33,44 +42,57 @@ namespace umma {
 
 constexpr int BM = 128;             // MMA M (TMEM lanes)
 constexpr int BK = 64;              // K per stage: one 128-byte swizzle atom of bf16
-constexpr int kProducers = 128;
-constexpr int kThreads = 160;
+constexpr int kProducers = 128;     // warps 0-3
+constexpr int kEpilogue = 128;      // warps 4-7
+constexpr int kMmaWarp = 8;
+constexpr int kThreads = 320;
 constexpr uint32_t kAtomRowsBytes = 64 * 128;  // one 64-row x 128-byte MN-major atom column
 
-// Development-only phase timestamps (compiled in with -DCVMM_TRACE; absent
-// from the shipped library).
+// Development-only knobs (compiled in with -DCVMM_TRACE; absent from the
+// shipped library): bit 8 skips the MMAs, bit 9 / bit 10 skip the A / B loads.
 #ifdef CVMM_TRACE
-__device__ unsigned long long* g_trace;
-#define CVMM_TRACE_AT(slot)                                                                     \
-  do {                                                                                        \
-    if (g_trace) {                                                                            \
-      unsigned smid;                                                                          \
-      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));                                      \
-      const size_t b = blockIdx.x + (size_t)gridDim.x * (blockIdx.y + (size_t)gridDim.y * blockIdx.z); \
-      g_trace[b * 10 + (slot)] = globaltimer_ns();                                            \
-      g_trace[b * 10 + 9] = smid;                                                             \
-    }                                                                                         \
-  } while (0)
+#define CVMM_DBG(flags, bit) (((flags) & (bit)) != 0)
 #else
-#define CVMM_TRACE_AT(slot) \
-  do {                      \
-  } while (0)
+#define CVMM_DBG(flags, bit) false
 #endif
 
 // Wait-site tags reported with CVMM_DEV_TIMEOUT.
-enum : int { kTagEmpty = 1, kTagFull = 2, kTagAccum = 3 };
+enum : int { kTagEmpty = 1, kTagFull = 2, kTagAccFull = 3, kTagAccEmpty = 4, kTagDrain = 5 };
 
 template <int BN, int S, bool WEIGHTED>
 struct Smem {
   static constexpr uint32_t a_bytes = BM * BK * 2;
   static constexpr uint32_t b_bytes = BN * BK * 2;
   static constexpr uint32_t stage_bytes = a_bytes + b_bytes;
-  static constexpr uint32_t bars = S * stage_bytes;               // full[S], empty[S], accum
-  static constexpr uint32_t misc = bars + (2 * S + 1) * 8;        // tmem slot, abort flag
-  static constexpr uint32_t scales = misc + 16;                   // WEIGHTED: float[S+1][64]
+  static constexpr uint32_t bars = S * stage_bytes;         // full[S] empty[S] accf[2] acce[2] drain
+  static constexpr uint32_t misc = bars + (2 * S + 5) * 8;  // tmem slot, abort flag
+  static constexpr uint32_t scales = misc + 16;             // WEIGHTED: float[S+1][64]
   static constexpr uint32_t used = scales + (WEIGHTED ? (S + 1) * 64 * 4 : 0);
-  static constexpr uint32_t alloc = used + 1024;                  // slack to align the base
+  static constexpr uint32_t alloc = used + 1024;            // slack to align the base
 };
+
+struct Bars {
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* accf;
+  uint64_t* acce;
+  uint64_t* drain;
+  volatile uint32_t* tmem_slot;
+  volatile int* abort;
+};
+
+template <class L, int S>
+__device__ __forceinline__ Bars carve_bars(uint8_t* smem) {
+  Bars b;
+  b.full = reinterpret_cast<uint64_t*>(smem + L::bars);
+  b.empty = b.full + S;
+  b.accf = b.empty + S;
+  b.acce = b.accf + 2;
+  b.drain = b.acce + 2;
+  b.tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + L::misc);
+  b.abort = reinterpret_cast<volatile int*>(smem + L::misc + 4);
+  return b;
+}
 
 // Byte offset of 16-byte chunk `chunk` of row `row` in a 128-byte-swizzled
 // tile whose rows are 128 bytes (64 bf16) and whose 64-column atoms are
@@ -138,12 +160,282 @@ __device__ __forceinline__ void store_row32(void* c, int c_dtype, int64_t off, c
     if (j < ncols) store_from_float(c, c_dtype, off + j, v[j]);
 }
 
+__device__ __forceinline__ void load_acc32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  ptx::tmem_ld_32x32b_x32(taddr, r);
+  ptx::tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// Barrier set-up and TMEM allocation (2 accumulator slots of BN columns).
+template <int BN, int S>
+__device__ __forceinline__ uint32_t setup(const Bars& b, int full_count) {
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      ptx::mbar_init(&b.full[s], full_count);
+      ptx::mbar_init(&b.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(&b.accf[a], 1);
+      ptx::mbar_init(&b.acce[a], kEpilogue);
+    }
+    ptx::mbar_init(b.drain, 1);
+    *b.abort = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    ptx::tmem_alloc(const_cast<uint32_t*>(b.tmem_slot), 2 * BN);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  return *b.tmem_slot;
+}
+
+// MMA issuer shared by both kernels: tile_nkb(t) gives the K stages of tile t.
+template <int BN, int S, class NkbFn>
+__device__ __forceinline__ void mma_loop(const Bars& b, uint8_t* smem, uint32_t tmem, uint32_t idesc,
+                                         bool a_mn, bool b_mn, int total, NkbFn tile_nkb, bool skip_mma) {
+  using L = Smem<BN, S, false>;
+  uint32_t it = 0;
+  int local = 0;
+  for (int tt = blockIdx.x; tt < total; tt += gridDim.x, ++local) {
+    const int a = local & 1;
+    if (local >= 2 && !ptx::mbar_wait_or_abort(&b.acce[a], ((local >> 1) - 1) & 1, kTagAccEmpty, b.abort))
+      break;
+    ptx::tc_fence_after();
+    const uint32_t d = tmem + a * BN;
+    const int nkb = tile_nkb(tt);
+    bool ok = true;
+    for (int kb = 0; kb < nkb; ++kb, ++it) {
+      const int s = it % S;
+      if (!ptx::mbar_wait_or_abort(&b.full[s], (it / S) & 1, kTagFull, b.abort)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      ptx::fence_proxy_async_smem();
+      const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes);
+      const uint32_t b_u = a_u + L::a_bytes;
+#pragma unroll
+      for (int j = 0; j < BK / 16; ++j) {
+        const uint64_t ad = a_mn ? ptx::smem_desc_sw128(a_u + j * 2048, kAtomRowsBytes, 1024)
+                                 : ptx::smem_desc_sw128(a_u + j * 32, 16, 1024);
+        const uint64_t bd = b_mn ? ptx::smem_desc_sw128(b_u + j * 2048, kAtomRowsBytes, 1024)
+                                 : ptx::smem_desc_sw128(b_u + j * 32, 16, 1024);
+        if (!skip_mma) ptx::mma_f16(d, ad, bd, idesc, (kb | j) != 0 ? 1u : 0u);
+      }
+      ptx::mma_commit(&b.empty[s]);
+    }
+    if (!ok) break;
+    ptx::mma_commit(&b.accf[a]);
+  }
+  // Everything issued must finish before TMEM is released.
+  ptx::mma_commit(b.drain);
+  ptx::mbar_wait(b.drain, 0, kTagDrain);
+}
+
+// ============================================================ row-gathered GEMM
+// flags bit0: A fast path (cp.async), bit1: B fast path (cp.async when not
+// TMA), bit2: C vector stores.
+template <int BN, int S, bool B_KMAJOR, bool B_TMA>
+__global__ void __launch_bounds__(kThreads, 1)
+row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b, int flags, int n_n) {
+  using L = Smem<BN, S, false>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_smem(smem_raw);
+  const Bars bar = carve_bars<L, S>(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = *p.n_tiles * n_n;
+  const int nkb = (int)((p.K + BK - 1) / BK);
+  const int op = p.op_dtype;
+  const bool a_fast = flags & 1, b_fast = flags & 2, c_vec = flags & 4;
+  const uint32_t tmem = setup<BN, S>(bar, kProducers + (B_TMA ? 1 : 0));
+
+  auto entry = [&](int tt) -> int4 {
+    return tt < total ? p.tiles[tt / n_n] : make_int4(0, 0, 0, 0);
+  };
+
+  if (warp < 4) {
+    // ------------------------------------------------------------ producers
+    const int t = threadIdx.x;
+    const int ac = t & 7;
+    const int64_t asz = dtype_bytes(p.a_dtype);
+    const char* bbase = static_cast<const char*>(p.b);
+    const int64_t bsz = dtype_bytes(p.b_dtype);
+    // Row indices of the next tile are loaded during the current one, and the
+    // tile entry two tiles ahead, so tile changes do not stall on index loads.
+    // Indices are below 2^31 (checked by the launcher): 32-bit registers.
+    int4 ent = entry(blockIdx.x);
+    int idx[8], idx_next[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rr = (t >> 3) + 16 * i;
+      idx[i] = rr < ent.z ? (int)p.a_index[ent.y + rr] : -1;
+    }
+    int4 ent_next = entry(blockIdx.x + gridDim.x);
+    uint32_t it = 0;
+    bool aborted = false;
+    for (int tt = blockIdx.x; tt < total && !aborted; tt += gridDim.x) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int rr = (t >> 3) + 16 * i;
+        idx_next[i] = rr < ent_next.z ? (int)p.a_index[ent_next.y + rr] : -1;
+      }
+      const int4 ent_after = entry(tt + 2 * gridDim.x);
+      const int64_t e = ent.x;
+      const int64_t n0 = (int64_t)(tt % n_n) * BN;
+      const char* a_rows[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        a_rows[i] = idx[i] >= 0 ? static_cast<const char*>(p.a) + idx_div(idx[i], p.a_div) * p.a_ld * asz : nullptr;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % S;
+        if (it >= S && !ptx::mbar_wait_or_abort(&bar.empty[s], ((it / S) - 1) & 1, kTagEmpty, bar.abort)) {
+          aborted = true;
+          break;
+        }
+        const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes), b_u = a_u + L::a_bytes;
+        const int64_t k0 = (int64_t)kb * BK;
+        if (!CVMM_DBG(flags, 512)) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int rr = (t >> 3) + 16 * i;
+            load_chunk(a_u + swz(rr, ac, 0), a_rows[i], k0 + ac * 8, p.K, p.a_dtype, 1, op, a_fast, p.a);
+          }
+        }
+        if (!B_TMA && !CVMM_DBG(flags, 1024)) {
+          if (B_KMAJOR) {
+#pragma unroll
+            for (int i = 0; i < BN / 16; ++i) {
+              const int nr = (t >> 3) + 16 * i;
+              const int64_t n = n0 + nr;
+              const char* row = n < p.N ? bbase + (e * p.bs_e + n * p.bs_n) * bsz : nullptr;
+              load_chunk(b_u + swz(nr, ac, 0), row, k0 + ac * 8, p.K, p.b_dtype, p.bs_k, op, b_fast, p.b);
+            }
+          } else {
+            constexpr int CPR = BN / 8;
+            const int bc = t % CPR;
+#pragma unroll
+            for (int i = 0; i < BN / 16; ++i) {
+              const int kr = t / CPR + (kProducers / CPR) * i;
+              const int64_t k = k0 + kr;
+              const char* row = k < p.K ? bbase + (e * p.bs_e + k * p.bs_k + n0 * p.bs_n) * bsz : nullptr;
+              load_chunk(b_u + swz(kr, bc, kAtomRowsBytes), row, bc * 8, p.N - n0, p.b_dtype, p.bs_n, op,
+                         b_fast, p.b);
+            }
+          }
+        }
+        if (!a_fast || (!B_TMA && !b_fast)) ptx::fence_proxy_async_smem();
+        ptx::cp_async_arrive_noinc(&bar.full[s]);
+      }
+      ent = ent_next;
+      ent_next = ent_after;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) idx[i] = idx_next[i];
+    }
+    ptx::cp_async_wait_all();
+  } else if (warp < 8) {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 4;
+    const int rr = ew * 32 + lane;
+    int4 ent = entry(blockIdx.x);
+    int64_t crow = rr < ent.z ? p.c_index[ent.y + rr] : -1;
+    int4 ent_next = entry(blockIdx.x + gridDim.x);
+    int local = 0;
+    for (int tt = blockIdx.x; tt < total; tt += gridDim.x, ++local) {
+      const int64_t crow_next = rr < ent_next.z ? p.c_index[ent_next.y + rr] : -1;
+      const int4 ent_after = entry(tt + 2 * gridDim.x);
+      const int a = local & 1;
+      if (!ptx::mbar_wait_or_abort(&bar.accf[a], (local >> 1) & 1, kTagAccFull, bar.abort)) break;
+      ptx::tc_fence_after();
+      const int64_t n0 = (int64_t)(tt % n_n) * BN;
+      const bool row_ok = crow >= 0;
+      float wv = 0.f, dot = 0.f;
+      if (p.mode == 1 && row_ok) wv = round_to(load_as_float(p.w, p.w_dtype, crow), op);
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        const int64_t nc = n0 + ch * 32;
+        if (nc >= p.N) break;
+        const int ncols = (int)imin64(32, p.N - nc);
+        float v[32];
+        load_acc32(tmem + ((uint32_t)(ew * 32) << 16) + a * BN + ch * 32, v);
+        if (nkb == 0) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        }
+        if (!row_ok) continue;
+        if (p.mode == 1) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float av = round_to(v[j], op);
+            if (j < ncols) dot = fmaf(av, load_as_float(p.x, p.x_dtype, crow * p.x_ld + nc + j), dot);
+            v[j] = round_to(av * wv, op);
+          }
+        }
+        store_row32(p.c, p.c_dtype, crow * p.c_ld + nc, v, ncols, c_vec);
+      }
+      if (p.mode == 1 && row_ok) atomicAdd(p.gsel + crow, dot);
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(&bar.acce[a]);
+      ent = ent_next;
+      ent_next = ent_after;
+      crow = crow_next;
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = ptx::instr_desc_f16(BM, BN, op == BF16, false, !B_KMAJOR);
+      mma_loop<BN, S>(bar, smem, tmem, idesc, false, !B_KMAJOR, total, [&](int) { return nkb; },
+                      CVMM_DBG(flags, 256));
+    }
+    __syncwarp();
+  } else if (B_TMA && lane == 0) {
+    // ------------------------------------------------------------ B tiles by TMA
+    ptx::tma_prefetch_desc(&tmap_b);
+    uint32_t it = 0;
+    int4 ent = entry(blockIdx.x);
+    for (int tt = blockIdx.x; tt < total; tt += gridDim.x) {
+      const int4 ent_next = entry(tt + gridDim.x);
+      const int e = ent.x;
+      const int n0 = (tt % n_n) * BN;
+      bool aborted = false;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % S;
+        if (it >= S && !ptx::mbar_wait_or_abort(&bar.empty[s], ((it / S) - 1) & 1, kTagEmpty, bar.abort)) {
+          aborted = true;
+          break;
+        }
+        const uint32_t b_u = ptx::smem_u32(smem + s * L::stage_bytes) + L::a_bytes;
+        ptx::mbar_arrive_expect_tx(&bar.full[s], L::b_bytes);
+        if (B_KMAJOR) {
+          ptx::tma_load_3d(b_u, &tmap_b, &bar.full[s], kb * BK, n0, e);
+        } else {
+#pragma unroll
+          for (int q = 0; q < BN / 64; ++q)
+            ptx::tma_load_3d(b_u + q * kAtomRowsBytes, &tmap_b, &bar.full[s], n0 + 64 * q, kb * BK, e);
+        }
+      }
+      if (aborted) break;
+      ent = ent_next;
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 2 * BN);
+  }
+}
+
 // Multiplies this thread's G chunks of stage `j` by their route weights (kept
 // in `scales`) and rounds to the op dtype: the reference multiplies the bf16
 // grad row by the bf16 weight and rounds the product to bf16 before the dot
 // (cvmm.py:591-599).
 template <int BN, int S>
-__device__ __forceinline__ void scale_rows(uint8_t* smem, const float* scales, int j, int t, int op) {
+__device__ __forceinline__ void scale_rows(uint8_t* smem, const float* scales, uint32_t j, int t, int op) {
   using L = Smem<BN, S, true>;
   constexpr int GCPR = BN / 8;
   const int sj = j % S, sl = j % (S + 1);
@@ -166,397 +458,260 @@ __device__ __forceinline__ void scale_rows(uint8_t* smem, const float* scales, i
   }
 }
 
-// ============================================================ row-gathered GEMM
-// flags bit0: A fast path (cp.async), bit1: B fast path, bit2: C vector stores.
-template <int BN, int S, bool B_KMAJOR>
-__global__ void __launch_bounds__(kThreads, 1) row_gemm_kernel(RowGemm p, int flags) {
-  if ((int)blockIdx.x >= *p.n_tiles) return;
-  if (threadIdx.x == 0) CVMM_TRACE_AT(0);
-  using L = Smem<BN, S, false>;
-  constexpr int LAG = S - 1;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = align_smem(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bars);
-  uint64_t* empty = full + S;
-  uint64_t* accum = empty + S;
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + L::misc);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::misc + 4);
-
-  const int2 tile = p.tiles[blockIdx.x];
-  const int64_t e = tile.x, r0 = tile.y;
-  const int rows = (int)imin64(BM, p.offsets[e] - r0);
-  const int64_t n0 = (int64_t)blockIdx.y * BN;
-  const int nkb = (int)((p.K + BK - 1) / BK);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool a_fast = flags & 1, b_fast = flags & 2, c_vec = flags & 4;
-#ifdef CVMM_TRACE
-  const bool dbg_no_mma = flags & 256, dbg_no_a = flags & 512, dbg_no_b = flags & 1024;
-#else
-  constexpr bool dbg_no_mma = false, dbg_no_a = false, dbg_no_b = false;
-#endif
-  const int op = p.op_dtype;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      ptx::mbar_init(&full[s], kProducers);
-      ptx::mbar_init(&empty[s], 1);
-    }
-    ptx::mbar_init(accum, 1);
-    *abort_flag = 0;
-    ptx::fence_mbar_init();
-  }
-  if (warp == 4) {
-    ptx::tmem_alloc(const_cast<uint32_t*>(tmem_slot), BN);
-    ptx::tmem_relinquish();
-  }
-  ptx::tc_fence_before();
-  __syncthreads();
-  ptx::tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  if (threadIdx.x == 0) CVMM_TRACE_AT(1);
-
-  if (warp < 4) {
-    const int t = threadIdx.x;
-    // ---- producer: A (K-major): 128 gathered rows x 8 chunks per stage.
-    const int ac = t & 7;
-    const char* a_rows[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int rr = (t >> 3) + 16 * i;
-      a_rows[i] = rr < rows ? static_cast<const char*>(p.a) +
-                                  idx_div(p.a_index[r0 + rr], p.a_div) * p.a_ld * (int64_t)dtype_bytes(p.a_dtype)
-                            : nullptr;
-    }
-    const char* bbase = static_cast<const char*>(p.b);
-    const int64_t bsz = dtype_bytes(p.b_dtype);
-    // B K-major rows (n) are fixed over the K loop.
-    constexpr int BKR = B_KMAJOR ? BN / 16 : 1;
-    const char* b_rows[BKR];
-    if (B_KMAJOR) {
-#pragma unroll
-      for (int i = 0; i < BKR; ++i) {
-        const int64_t n = n0 + (t >> 3) + 16 * i;
-        b_rows[i] = n < p.N ? bbase + (e * p.bs_e + n * p.bs_n) * bsz : nullptr;
-      }
-    }
-    constexpr int CPR = BN / 8;  // MN-major B: 16-byte chunks per k row
-    bool aborted = false;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % S;
-      if (kb >= S && !ptx::mbar_wait(&empty[s], ((kb / S) - 1) & 1, kTagEmpty)) {
-        *abort_flag = 1;
-        aborted = true;
-        break;
-      }
-      uint8_t* a_st = smem + s * L::stage_bytes;
-      const uint32_t a_u = ptx::smem_u32(a_st), b_u = a_u + L::a_bytes;
-      const int64_t k0 = (int64_t)kb * BK;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int rr = (t >> 3) + 16 * i;
-        if (!dbg_no_a)
-          load_chunk(a_u + swz(rr, ac, 0), a_rows[i], k0 + ac * 8, p.K, p.a_dtype, 1, op, a_fast, p.a);
-      }
-      if (dbg_no_b) {
-      } else if (B_KMAJOR) {
-#pragma unroll
-        for (int i = 0; i < BKR; ++i) {
-          const int nr = (t >> 3) + 16 * i;
-          load_chunk(b_u + swz(nr, ac, 0), b_rows[i], k0 + ac * 8, p.K, p.b_dtype, p.bs_k, op,
-                     b_fast, p.b);
-        }
-      } else {
-        const int bc = t % CPR;
-#pragma unroll
-        for (int i = 0; i < BN / 16; ++i) {
-          const int kr = t / CPR + (kProducers / CPR) * i;
-          const int64_t k = k0 + kr;
-          const char* row = k < p.K ? bbase + (e * p.bs_e + k * p.bs_k + n0 * p.bs_n) * bsz : nullptr;
-          load_chunk(b_u + swz(kr, bc, kAtomRowsBytes), row, bc * 8, p.N - n0, p.b_dtype, p.bs_n,
-                     op, b_fast, p.b);
-        }
-      }
-      ptx::cp_async_commit();
-      if (t == 0 && kb == 0) CVMM_TRACE_AT(2);
-      if (kb >= LAG) {
-        ptx::cp_async_wait<LAG>();
-        ptx::fence_proxy_async_smem();
-        ptx::mbar_arrive(&full[(kb - LAG) % S]);
-      }
-    }
-    if (t == 0) CVMM_TRACE_AT(3);
-    ptx::cp_async_wait_all();
-    ptx::fence_proxy_async_smem();
-    if (!aborted)
-      for (int j = max(0, nkb - LAG); j < nkb; ++j) ptx::mbar_arrive(&full[j % S]);
-
-    // ---- epilogue: TMEM lane (32*warp + lane) holds output row rr.
-    const int rr = warp * 32 + lane;
-    const bool row_ok = rr < rows;
-    const int64_t c_row = row_ok ? p.c_index[r0 + rr] : 0;
-    const bool have_acc = nkb > 0 && ptx::mbar_wait(accum, 0, kTagAccum) && *abort_flag == 0;
-    ptx::tc_fence_after();
-    if (t == 0) CVMM_TRACE_AT(6);
-    float wv = 0.f, dot = 0.f;
-    if (p.mode == 1 && row_ok) wv = round_to(load_as_float(p.w, p.w_dtype, c_row), op);
-    for (int ch = 0; ch < BN / 32; ++ch) {
-      const int64_t nc = n0 + ch * 32;
-      if (nc >= p.N) break;
-      const int ncols = (int)imin64(32, p.N - nc);
-      float v[32];
-      if (have_acc) {
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + ch * 32, r);
-        ptx::tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = 0.f;
-      }
-      if (!row_ok || (nkb > 0 && !have_acc)) continue;
-      if (p.mode == 1) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float a = round_to(v[j], op);
-          if (j < ncols) dot = fmaf(a, load_as_float(p.x, p.x_dtype, c_row * p.x_ld + nc + j), dot);
-          v[j] = round_to(a * wv, op);
-        }
-      }
-      store_row32(p.c, p.c_dtype, c_row * p.c_ld + nc, v, ncols, c_vec);
-    }
-    if (p.mode == 1 && row_ok && (nkb == 0 || have_acc)) atomicAdd(p.gsel + c_row, dot);
-  } else if (warp == 4 && lane == 0) {
-    // ---- MMA issuer.
-    const uint32_t idesc = ptx::instr_desc_f16(BM, BN, op == BF16, false, !B_KMAJOR);
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % S;
-      if (*abort_flag || !ptx::mbar_wait(&full[s], (kb / S) & 1, kTagFull)) {
-        *abort_flag = 1;
-        break;
-      }
-      ptx::tc_fence_after();
-      if (kb == 0) CVMM_TRACE_AT(4);
-      const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes), b_u = a_u + L::a_bytes;
-#pragma unroll
-      for (int j = 0; j < BK / 16; ++j) {
-        const uint64_t ad = ptx::smem_desc_sw128(a_u + j * 32, 16, 1024);
-        const uint64_t bd = B_KMAJOR ? ptx::smem_desc_sw128(b_u + j * 32, 16, 1024)
-                                     : ptx::smem_desc_sw128(b_u + j * 2048, kAtomRowsBytes, 1024);
-        if (!dbg_no_mma) ptx::mma_f16(tmem, ad, bd, idesc, (kb | j) != 0 ? 1u : 0u);
-      }
-      ptx::mma_commit(&empty[s]);
-    }
-    ptx::mma_commit(accum);
-    CVMM_TRACE_AT(5);
-  }
-  ptx::tc_fence_before();
-  __syncthreads();
-  if (threadIdx.x == 0) CVMM_TRACE_AT(7);
-  if (warp == 4) {
-    ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem, BN);
-  }
-}
-
 // ============================================================ segment GEMM (grad-W)
-// Split-K over each expert segment: a work unit is (expert, chunk of at most
-// p.chunk sorted routes) x (m tile) x (n tile), so a heavily loaded expert is
-// spread over many CTAs instead of one CTA walking its whole segment. Partial
-// sums go to per-chunk slots and are reduced in a fixed order (deterministic).
+// Work = (unit, m tile, n tile) where a unit is a chunk of at most p.chunk
+// sorted routes of one expert (split-K): a heavily loaded expert is spread
+// over many tiles. A unit covering its whole expert writes grad_w; chunks of
+// a split expert write partial slots that seg_reduce adds in a fixed order.
+// Both operands are gathered rows: A = x^T (MN-major, rows = routes), B = the
+// (weight-scaled) grad rows (MN-major).
 // flags bit0: X fast path, bit1: G fast path, bit2: out vector stores.
 template <int BN, int S, bool WEIGHTED>
-__global__ void __launch_bounds__(kThreads, 1) seg_gemm_kernel(SegGemm p, int flags) {
-  if ((int)blockIdx.x >= *p.n_units) return;
+__global__ void __launch_bounds__(kThreads, 1) seg_gemm_kernel(const SegGemm p, int flags, int n_m, int n_n) {
   using L = Smem<BN, S, WEIGHTED>;
-  constexpr int LAG = S - 1;
-  constexpr int GCPR = BN / 8;            // G tile: 16-byte chunks per route row
-  constexpr int GROWS = BN / 16;          // G rows per producer thread per stage
+  constexpr int GCPR = BN / 8;    // G tile: 16-byte chunks per route row
+  constexpr int GROWS = BN / 16;  // G rows per producer thread per stage
+  // The weighted variant scales G in shared memory after it lands, so its
+  // producers hand a stage over LAG stages after issuing it.
+  constexpr int LAG = S / 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_smem(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bars);
-  uint64_t* empty = full + S;
-  uint64_t* accum = empty + S;
-  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + L::misc);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::misc + 4);
+  const Bars bar = carve_bars<L, S>(smem);
   float* scales = reinterpret_cast<float*>(smem + L::scales);
-
-  const int4 unit = p.units[blockIdx.x];
-  const int64_t e = unit.x;
-  const int64_t beg = unit.y;
-  const int64_t end = imin64(beg + p.chunk, p.offsets[e]);
-  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.z * BN;
-  const int nkb = (int)((end - beg + BK - 1) / BK);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool x_fast = flags & 1, g_fast = flags & 2, o_vec = flags & 4;
+  const int per_unit = n_m * n_n;
+  const int total = *p.n_units * per_unit;
   const int op = p.op_dtype;
+  const bool x_fast = flags & 1, g_fast = flags & 2, o_vec = flags & 4;
+  const uint32_t tmem = setup<BN, S>(bar, kProducers);
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      ptx::mbar_init(&full[s], kProducers);
-      ptx::mbar_init(&empty[s], 1);
-    }
-    ptx::mbar_init(accum, 1);
-    *abort_flag = 0;
-    ptx::fence_mbar_init();
-  }
-  if (warp == 4) {
-    ptx::tmem_alloc(const_cast<uint32_t*>(tmem_slot), BN);
-    ptx::tmem_relinquish();
-  }
-  ptx::tc_fence_before();
-  __syncthreads();
-  ptx::tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  auto entry = [&](int tt) -> int4 {
+    return tt < total ? p.units[tt / per_unit] : make_int4(0, 0, -1, 0);
+  };
+  auto nkb_of = [&](const int4& u) -> int { return (int)((u.w - u.y + BK - 1) / BK); };
 
   if (warp < 4) {
+    // ------------------------------------------------------------ producers
     const int t = threadIdx.x;
     const char* xbase = static_cast<const char*>(p.x);
     const char* gbase = static_cast<const char*>(p.g);
     const int64_t xsz = dtype_bytes(p.x_dtype), gsz = dtype_bytes(p.g_dtype);
-    const int xc = t & 15;       // X tile: 64 route rows x 16 chunks (128 m columns)
-    const int gc = t % GCPR;     // G tile: 64 route rows x GCPR chunks
-    // Row indices of the next stage are loaded one stage ahead so that their
-    // latency overlaps the copies of the current stage.
-    int64_t xi[8], gi[GROWS], wi[GROWS];
-    auto fetch = [&](int kb) {
-      const int64_t rb = beg + (int64_t)kb * BK;
+    const int xc = t & 15;    // X tile: 64 route rows x 16 chunks (128 m columns)
+    const int gc = t % GCPR;  // G tile: 64 route rows x GCPR chunks
+    // Indices are below 2^31 (checked by the launcher): 32-bit registers.
+    int xi[8], gi[GROWS], wi[GROWS];
+    // Row indices of stage (u, kb) are fetched one stage ahead.
+    auto fetch = [&](const int4& u, int kb) {
+      const int64_t rb = u.y + (int64_t)kb * BK;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int64_t r = rb + (t >> 4) + 8 * i;
-        xi[i] = r < end ? p.x_index[r] : -1;
+        xi[i] = r < u.w ? (int)p.x_index[r] : -1;
       }
 #pragma unroll
       for (int i = 0; i < GROWS; ++i) {
         const int64_t r = rb + t / GCPR + (kProducers / GCPR) * i;
-        gi[i] = r < end ? p.g_index[r] : -1;
-        if (WEIGHTED) wi[i] = r < end ? p.w_index[r] : -1;
+        gi[i] = r < u.w ? (int)p.g_index[r] : -1;
+        if (WEIGHTED) wi[i] = r < u.w ? (int)p.w_index[r] : -1;
       }
     };
-    if (nkb > 0) fetch(0);
+    int4 u = entry(blockIdx.x);
+    int4 u_next = entry(blockIdx.x + gridDim.x);
+    if ((int)blockIdx.x < total) fetch(u, 0);
+    uint32_t it = 0;
     bool aborted = false;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % S;
-      bool bad = kb >= S && !ptx::mbar_wait(&empty[s], ((kb / S) - 1) & 1, kTagEmpty);
-      // The weighted variant synchronises the producers below, so its abort
-      // decision must be uniform across them.
-      if (WEIGHTED) bad = ptx::named_bar_or(1, kProducers, bad);
-      if (bad) {
-        *abort_flag = 1;
-        aborted = true;
-        break;
-      }
-      const char* xrow[8];
-      const char* grow[GROWS];
-      float wsc[GROWS];
+    for (int tt = blockIdx.x; tt < total && !aborted; tt += gridDim.x) {
+      const int4 u_after = entry(tt + 2 * gridDim.x);
+      const int rem = tt % per_unit;
+      const int64_t m0 = (int64_t)(rem / n_n) * BM, n0 = (int64_t)(rem % n_n) * BN;
+      const int nkb = nkb_of(u);
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % S;
+        bool bad = it >= S && !ptx::mbar_wait_or_abort(&bar.empty[s], ((it / S) - 1) & 1, kTagEmpty, bar.abort);
+        if (WEIGHTED) bad = ptx::named_bar_or(1, kProducers, bad);
+        if (bad) {
+          aborted = true;
+          break;
+        }
+        const char* xrow[8];
+        const char* grow[GROWS];
+        float wsc[GROWS];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        xrow[i] = xi[i] >= 0 ? xbase + (idx_div(xi[i], p.x_div) * p.x_ld + m0) * xsz : nullptr;
+        for (int i = 0; i < 8; ++i)
+          xrow[i] = xi[i] >= 0 ? xbase + (idx_div(xi[i], p.x_div) * p.x_ld + m0) * xsz : nullptr;
 #pragma unroll
-      for (int i = 0; i < GROWS; ++i) {
-        grow[i] = gi[i] >= 0 ? gbase + (idx_div(gi[i], p.g_div) * p.g_ld + n0) * gsz : nullptr;
-        if (WEIGHTED) wsc[i] = wi[i] >= 0 ? round_to(load_as_float(p.w, p.w_dtype, wi[i]), op) : 0.f;
-      }
-      if (kb + 1 < nkb) fetch(kb + 1);
-      const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes), b_u = a_u + L::a_bytes;
+        for (int i = 0; i < GROWS; ++i) {
+          grow[i] = gi[i] >= 0 ? gbase + (idx_div(gi[i], p.g_div) * p.g_ld + n0) * gsz : nullptr;
+          if (WEIGHTED) wsc[i] = wi[i] >= 0 ? round_to(load_as_float(p.w, p.w_dtype, wi[i]), op) : 0.f;
+        }
+        if (kb + 1 < nkb) fetch(u, kb + 1);
+        else if (tt + (int)gridDim.x < total) fetch(u_next, 0);
+        const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes), b_u = a_u + L::a_bytes;
+        if (!CVMM_DBG(flags, 512)) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int kr = (t >> 4) + 8 * i;
-        load_chunk(a_u + swz(kr, xc, kAtomRowsBytes), xrow[i], xc * 8, p.M - m0, p.x_dtype, 1, op,
-                   x_fast, p.x);
-      }
+          for (int i = 0; i < 8; ++i) {
+            const int kr = (t >> 4) + 8 * i;
+            load_chunk(a_u + swz(kr, xc, kAtomRowsBytes), xrow[i], xc * 8, p.M - m0, p.x_dtype, 1, op, x_fast, p.x);
+          }
+        }
 #pragma unroll
-      for (int i = 0; i < GROWS; ++i) {
-        const int kr = t / GCPR + (kProducers / GCPR) * i;
-        load_chunk(b_u + swz(kr, gc, kAtomRowsBytes), grow[i], gc * 8, p.N - n0, p.g_dtype, 1, op,
-                   g_fast, p.g);
-        if (WEIGHTED && gc == 0) scales[(kb % (S + 1)) * 64 + kr] = wsc[i];
+        for (int i = 0; i < GROWS; ++i) {
+          const int kr = t / GCPR + (kProducers / GCPR) * i;
+          if (!CVMM_DBG(flags, 1024))
+            load_chunk(b_u + swz(kr, gc, kAtomRowsBytes), grow[i], gc * 8, p.N - n0, p.g_dtype, 1, op, g_fast, p.g);
+          if (WEIGHTED && gc == 0) scales[(it % (S + 1)) * 64 + kr] = wsc[i];
+        }
+        if (!WEIGHTED) {
+          if (!x_fast || !g_fast) ptx::fence_proxy_async_smem();
+          ptx::cp_async_arrive_noinc(&bar.full[s]);
+        } else {
+          ptx::cp_async_commit();
+          ptx::named_bar_sync(1, kProducers);
+          if (it >= (uint32_t)LAG) {
+            ptx::cp_async_wait<LAG>();
+            scale_rows<BN, S>(smem, scales, it - LAG, t, op);
+            ptx::fence_proxy_async_smem();
+            ptx::mbar_arrive(&bar.full[(it - LAG) % S]);
+          }
+        }
       }
-      ptx::cp_async_commit();
-      if (WEIGHTED) ptx::named_bar_sync(1, kProducers);
-      if (kb >= LAG) {
-        ptx::cp_async_wait<LAG>();
-        if (WEIGHTED) scale_rows<BN, S>(smem, scales, kb - LAG, t, op);
-        ptx::fence_proxy_async_smem();
-        ptx::mbar_arrive(&full[(kb - LAG) % S]);
-      }
+      u = u_next;
+      u_next = u_after;
     }
     ptx::cp_async_wait_all();
-    if (WEIGHTED && !aborted)
-      for (int j = max(0, nkb - LAG); j < nkb; ++j) scale_rows<BN, S>(smem, scales, j, t, op);
-    ptx::fence_proxy_async_smem();
-    if (!aborted)
-      for (int j = max(0, nkb - LAG); j < nkb; ++j) ptx::mbar_arrive(&full[j % S]);
-
-    // ---- epilogue: TMEM lane = m row of this expert's grad tile. A unit that
-    // covers its whole expert writes grad_w; a chunk of a split expert writes
-    // its partial slot (summed in order by seg_reduce).
-    const int mr = warp * 32 + lane;
-    const int64_t m = m0 + mr;
-    const bool have_acc = nkb > 0 && ptx::mbar_wait(accum, 0, kTagAccum) && *abort_flag == 0;
-    ptx::tc_fence_after();
-    float* dst_base = unit.z < 0 ? p.out + e * p.M * p.N : p.partials + (int64_t)unit.z * p.M * p.N;
-    if (have_acc) {
+    if (WEIGHTED && !aborted) {
+      const uint32_t first = it > (uint32_t)LAG ? it - LAG : 0;
+      for (uint32_t j = first; j < it; ++j) scale_rows<BN, S>(smem, scales, j, t, op);
+      ptx::fence_proxy_async_smem();
+      for (uint32_t j = first; j < it; ++j) ptx::mbar_arrive(&bar.full[j % S]);
+    }
+  } else if (warp < 8) {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 4;
+    const int mr = ew * 32 + lane;
+    int local = 0;
+    for (int tt = blockIdx.x; tt < total; tt += gridDim.x, ++local) {
+      const int4 u = entry(tt);
+      const int rem = tt % per_unit;
+      const int64_t m0 = (int64_t)(rem / n_n) * BM, n0 = (int64_t)(rem % n_n) * BN;
+      const int a = local & 1;
+      if (!ptx::mbar_wait_or_abort(&bar.accf[a], (local >> 1) & 1, kTagAccFull, bar.abort)) break;
+      ptx::tc_fence_after();
+      const int64_t e = u.x;
+      const int64_t m = m0 + mr;
+      float* dst = u.z < 0 ? p.out + e * p.M * p.N : p.partials + (int64_t)u.z * p.M * p.N;
+      const bool empty_unit = nkb_of(u) == 0;
       for (int ch = 0; ch < BN / 32; ++ch) {
         const int64_t nc = n0 + ch * 32;
         if (nc >= p.N) break;
         const int ncols = (int)imin64(32, p.N - nc);
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(warp * 32) << 16) + ch * 32, r);
-        ptx::tmem_wait_ld();
-        if (m >= p.M) continue;
         float v[32];
+        load_acc32(tmem + ((uint32_t)(ew * 32) << 16) + a * BN + ch * 32, v);
+        if (empty_unit) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        store_row32(dst_base, F32, m * p.N + nc, v, ncols, o_vec);
+          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        }
+        if (m < p.M) store_row32(dst, F32, m * p.N + nc, v, ncols, o_vec);
       }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(&bar.acce[a]);
     }
-  } else if (warp == 4 && lane == 0) {
-    const uint32_t idesc = ptx::instr_desc_f16(BM, BN, op == BF16, true, true);
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % S;
-      if (*abort_flag || !ptx::mbar_wait(&full[s], (kb / S) & 1, kTagFull)) {
-        *abort_flag = 1;
-        break;
-      }
-      ptx::tc_fence_after();
-      const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes), b_u = a_u + L::a_bytes;
-#pragma unroll
-      for (int j = 0; j < BK / 16; ++j) {
-        const uint64_t ad = ptx::smem_desc_sw128(a_u + j * 2048, kAtomRowsBytes, 1024);
-        const uint64_t bd = ptx::smem_desc_sw128(b_u + j * 2048, kAtomRowsBytes, 1024);
-        ptx::mma_f16(tmem, ad, bd, idesc, (kb | j) != 0 ? 1u : 0u);
-      }
-      ptx::mma_commit(&empty[s]);
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      const uint32_t idesc = ptx::instr_desc_f16(BM, BN, op == BF16, true, true);
+      mma_loop<BN, S>(bar, smem, tmem, idesc, true, true, total, [&](int tt) { return nkb_of(entry(tt)); },
+                      CVMM_DBG(flags, 256));
     }
-    ptx::mma_commit(accum);
+    __syncwarp();
   }
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem, BN);
+    ptx::tmem_dealloc(tmem, 2 * BN);
   }
 }
 
+// ------------------------------------------------------------ host side
 template <typename K>
 static int set_smem(K kernel, uint32_t bytes) {
-  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
-      cudaSuccess)
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
     return fail_cuda("cudaFuncSetAttribute(max dynamic smem)");
   return CVMM_OK;
 }
 
 static inline bool aligned16(const void* ptr) { return ((uintptr_t)ptr & 15u) == 0; }
 
+static int sm_count() {
+  int dev = 0, v = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+      v > 0)
+    return v;
+  return 148;
+}
+
+static int dbg_flags() {
+#ifdef CVMM_TRACE
+  if (const char* ev = getenv("CVMM_DBG_FLAGS")) return atoi(ev);
+#endif
+  return 0;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 3-D TMA map of the expert weights keys[e][r][c] (c contiguous) with a
+// 64 x box_rows box and 128-byte swizzle. Returns false when the layout does
+// not meet TMA's alignment rules (the caller then loads B with cp.async).
+static bool make_b_map(CUtensorMap* map, const void* base, int dtype, int64_t cols, int64_t rows, int64_t experts,
+                       int64_t row_stride, int64_t expert_stride, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn || !aligned16(base) || (row_stride * 2) % 16 != 0 || (expert_stride * 2) % 16 != 0) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)experts};
+  cuuint64_t strides[2] = {(cuuint64_t)row_stride * 2, (cuuint64_t)expert_stride * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dtype == BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <int BN, int S, bool BK_MAJOR>
 static int row_launch(const RowGemm& p, int64_t max_tiles, int flags, cudaStream_t stream) {
   using L = Smem<BN, S, false>;
-  auto kern = row_gemm_kernel<BN, S, BK_MAJOR>;
-  int rc = set_smem(kern, L::alloc);
-  if (rc) return rc;
-  dim3 grid((unsigned)max_tiles, (unsigned)((p.N + BN - 1) / BN));
-  kern<<<grid, kThreads, L::alloc, stream>>>(p, flags);
+  const int n_n = (int)((p.N + BN - 1) / BN);
+  CUtensorMap map;
+  memset(&map, 0, sizeof(map));
+  bool tma = false;
+  if (flags & 2) {
+    tma = BK_MAJOR ? make_b_map(&map, p.b, p.op_dtype, p.K, p.N, p.n_experts, p.bs_n, p.bs_e, BN)
+                   : make_b_map(&map, p.b, p.op_dtype, p.N, p.K, p.n_experts, p.bs_k, p.bs_e, 64);
+  }
+  if (dbg_flags() & 2048) tma = false;
+  const int64_t work = max_tiles * n_n;
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(work, sm_count()));
+  if (tma) {
+    auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true>;
+    int rc = set_smem(kern, L::alloc);
+    if (rc) return rc;
+    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, flags, n_n);
+  } else {
+    auto kern = row_gemm_kernel<BN, S, BK_MAJOR, false>;
+    int rc = set_smem(kern, L::alloc);
+    if (rc) return rc;
+    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, flags, n_n);
+  }
   return check_launch("row_gemm_umma");
 }
 
@@ -566,38 +721,30 @@ static int seg_launch(const SegGemm& p, int64_t max_units, int flags, cudaStream
   auto kern = seg_gemm_kernel<BN, S, W>;
   int rc = set_smem(kern, L::alloc);
   if (rc) return rc;
-  dim3 grid((unsigned)max_units, (unsigned)((p.M + BM - 1) / BM), (unsigned)((p.N + BN - 1) / BN));
-  kern<<<grid, kThreads, L::alloc, stream>>>(p, flags);
+  const int n_m = (int)((p.M + BM - 1) / BM), n_n = (int)((p.N + BN - 1) / BN);
+  const int64_t work = max_units * n_m * n_n;
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(work, sm_count()));
+  kern<<<grid, kThreads, L::alloc, stream>>>(p, flags, n_m, n_n);
   return check_launch("seg_gemm_umma");
 }
 
 }  // namespace umma
 
-#ifdef CVMM_TRACE
-extern "C" int cvmm_debug_set_trace(void* buf) {
-  unsigned long long* p = static_cast<unsigned long long*>(buf);
-  return cudaMemcpyToSymbol(umma::g_trace, &p, sizeof(p)) == cudaSuccess ? 0 : -3;
-}
-#endif
-
 int launch_row_gemm_umma(const RowGemm& p, int64_t max_tiles, cudaStream_t stream) {
   using namespace umma;
   const bool b_kmajor = p.bs_k == 1 && p.bs_n != 1;
-  int flags = 0;
+  int flags = dbg_flags() & ~2048;
   if (p.a_dtype == p.op_dtype && p.a_ld % 8 == 0 && aligned16(p.a)) flags |= 1;
   if (p.b_dtype == p.op_dtype && aligned16(p.b) && p.bs_e % 8 == 0 &&
       (b_kmajor ? (p.bs_k == 1 && p.bs_n % 8 == 0) : (p.bs_n == 1 && p.bs_k % 8 == 0)))
     flags |= 2;
   if (p.c_ld % 8 == 0 && aligned16(p.c)) flags |= 4;
-#ifdef CVMM_TRACE
-  if (const char* e = getenv("CVMM_DBG_FLAGS")) flags |= atoi(e);
-#endif
   if (p.N <= 64) {
-    return b_kmajor ? row_launch<64, 6, true>(p, max_tiles, flags, stream)
-                    : row_launch<64, 6, false>(p, max_tiles, flags, stream);
+    return b_kmajor ? row_launch<64, 8, true>(p, max_tiles, flags, stream)
+                    : row_launch<64, 8, false>(p, max_tiles, flags, stream);
   } else if (p.N <= 128) {
-    return b_kmajor ? row_launch<128, 4, true>(p, max_tiles, flags, stream)
-                    : row_launch<128, 4, false>(p, max_tiles, flags, stream);
+    return b_kmajor ? row_launch<128, 6, true>(p, max_tiles, flags, stream)
+                    : row_launch<128, 6, false>(p, max_tiles, flags, stream);
   }
   return b_kmajor ? row_launch<256, 4, true>(p, max_tiles, flags, stream)
                   : row_launch<256, 4, false>(p, max_tiles, flags, stream);
@@ -605,13 +752,13 @@ int launch_row_gemm_umma(const RowGemm& p, int64_t max_tiles, cudaStream_t strea
 
 int launch_seg_gemm_umma(const SegGemm& p, int64_t max_units, cudaStream_t stream) {
   using namespace umma;
-  int flags = 0;
+  int flags = dbg_flags();
   if (p.x_dtype == p.op_dtype && p.x_ld % 8 == 0 && aligned16(p.x)) flags |= 1;
   if (p.g_dtype == p.op_dtype && p.g_ld % 8 == 0 && aligned16(p.g)) flags |= 2;
   if (p.N % 4 == 0 && aligned16(p.out) && aligned16(p.partials)) flags |= 4;
   const bool w = p.w != nullptr;
-  if (p.N <= 64) return w ? seg_launch<64, 6, true>(p, max_units, flags, stream) : seg_launch<64, 6, false>(p, max_units, flags, stream);
-  if (p.N <= 128) return w ? seg_launch<128, 4, true>(p, max_units, flags, stream) : seg_launch<128, 4, false>(p, max_units, flags, stream);
+  if (p.N <= 64) return w ? seg_launch<64, 8, true>(p, max_units, flags, stream) : seg_launch<64, 8, false>(p, max_units, flags, stream);
+  if (p.N <= 128) return w ? seg_launch<128, 6, true>(p, max_units, flags, stream) : seg_launch<128, 6, false>(p, max_units, flags, stream);
   return w ? seg_launch<256, 4, true>(p, max_units, flags, stream) : seg_launch<256, 4, false>(p, max_units, flags, stream);
 }
 
