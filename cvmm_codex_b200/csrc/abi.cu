@@ -170,7 +170,8 @@ static int64_t segw_max_slots(int64_t n_routes, int64_t chunk) { return 2 * ((n_
 static size_t segw_ws_bytes(int64_t n_routes, int64_t n_experts, int64_t m_dim, int64_t n_dim, bool tensor) {
   const int64_t chunk = segw_chunk(n_routes, n_experts, m_dim, n_dim, tensor);
   return table_bytes(n_routes, n_experts) + align_up((size_t)n_experts * sizeof(int2), 256) +
-         align_up((size_t)segw_max_slots(n_routes, chunk) * m_dim * n_dim * sizeof(float), 256);
+         align_up((size_t)segw_max_slots(n_routes, chunk) * m_dim * n_dim * sizeof(float), 256) +
+         3 * align_up((size_t)(n_routes + kRouteRowsPad) * 4, 256);
 }
 
 static int carve_ws(void* ws, size_t bytes, size_t need, int64_t n_routes, int64_t n_experts, GemmWs* out,
@@ -277,7 +278,7 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld, const
   if (!x || !sel_index || !offsets || !keys || !out)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: null pointer");
   RowGemm p = {};
-  p.a = x; p.a_dtype = x_dtype; p.a_ld = x_ld; p.a_index = sel_index; p.a_div = 1;
+  p.a = x; p.a_dtype = x_dtype; p.a_ld = x_ld; p.a_rows = x_rows; p.a_index = sel_index; p.a_div = 1;
   p.b = keys; p.b_dtype = keys_dtype; p.bs_e = ks_e; p.bs_k = ks_k; p.bs_n = ks_n;
   p.c = out; p.c_dtype = out_dtype; p.c_ld = out_ld; p.c_index = out_index ? out_index : sel_index;
   p.offsets = offsets; p.n_routes = n_routes; p.n_experts = n_experts; p.K = k_dim; p.N = n_dim;
@@ -329,7 +330,7 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: mode 1 needs w, x and gsel");
   RowGemm p = {};
   // B_e[kk][nn] = keys[e][nn][kk]: contract over n_dim, produce k_dim columns.
-  p.a = g; p.a_dtype = g_dtype; p.a_ld = g_ld; p.a_index = g_index; p.a_div = g_div;
+  p.a = g; p.a_dtype = g_dtype; p.a_ld = g_ld; p.a_rows = n_routes; p.a_index = g_index; p.a_div = g_div;
   p.b = keys; p.b_dtype = keys_dtype; p.bs_e = ks_e; p.bs_k = ks_n; p.bs_n = ks_k;
   p.c = out; p.c_dtype = out_dtype; p.c_ld = out_ld; p.c_index = out_index;
   p.offsets = offsets; p.n_routes = n_routes; p.n_experts = n_experts; p.K = n_dim; p.N = k_dim;
@@ -370,6 +371,19 @@ int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_i
   p.partials = ws.partials;
   rc = build_units(offsets, n_experts, p.chunk, static_cast<int4*>(ws.tiles), ws.count, ws.expert_slots, s);
   if (rc) return rc;
+  if (tensor && n_routes > 0) {
+    char* rr = reinterpret_cast<char*>(ws.partials) +
+               align_up((size_t)segw_max_slots(n_routes, p.chunk) * m_dim * n_dim * sizeof(float), 256);
+    const size_t arr = align_up((size_t)(n_routes + kRouteRowsPad) * 4, 256);
+    int* xrow = reinterpret_cast<int*>(rr);
+    int* grow = reinterpret_cast<int*>(rr + arr);
+    float* wsc = reinterpret_cast<float*>(rr + 2 * arr);
+    rc = resolve_route_rows(p, xrow, grow, wsc, s);
+    if (rc) return rc;
+    p.xrow = xrow;
+    p.grow = grow;
+    p.wsc = wsc;
+  }
   if (n_routes > 0) {
     const int64_t max_units = max_row_tiles(n_routes, n_experts, (int)p.chunk);
     rc = tensor ? launch_seg_gemm_umma(p, max_units, s) : launch_seg_gemm_simt(p, max_units, s);

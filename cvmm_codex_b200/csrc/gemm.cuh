@@ -14,7 +14,7 @@ namespace cvmm {
 //   mode 1: C[c_index[p]][n] = cast(op(op(acc_p[n]) * op(w[c_index[p]])))
 //           gsel[c_index[p]] += sum_n op(acc_p[n]) * x[c_index[p]][n]
 struct RowGemm {
-  const void* a; int a_dtype; int64_t a_ld;
+  const void* a; int a_dtype; int64_t a_ld; int64_t a_rows;  // a_rows: bound on indexed rows
   const int64_t* a_index; int64_t a_div;
   const void* b; int b_dtype; int64_t bs_e, bs_k, bs_n;
   void* c; int c_dtype; int64_t c_ld;
@@ -46,7 +46,16 @@ struct SegGemm {
   const int4* units;    // (expert, first sorted position, partial slot or -1, end position)
   const int* n_units;
   float* partials;      // [slots][M][N] partial sums of split experts
+  // Per sorted route, resolved before the GEMM (tensor-core path): x row,
+  // grad row (int32) and op-rounded route weight (fp32); padded by
+  // kRouteRowsPad entries so 16-byte-aligned bulk copies may run past the end.
+  const int* xrow;
+  const int* grow;
+  const float* wsc;
 };
+
+constexpr int64_t kRouteRowsPad = 128;
+int resolve_route_rows(const SegGemm& p, int* xrow, int* grow, float* wsc, cudaStream_t stream);
 
 __device__ __forceinline__ int64_t seg_begin(const int64_t* offsets, int64_t e) {
   return e > 0 ? offsets[e - 1] : 0;

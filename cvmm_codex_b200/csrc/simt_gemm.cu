@@ -117,6 +117,25 @@ int build_units(const int64_t* offsets, int64_t n_experts, int64_t chunk, int4* 
   return check_launch("build_units");
 }
 
+// x row, grad row and op-rounded weight of every sorted route (for the
+// tensor-core grad-W, whose index warp bulk-copies them into shared memory).
+__global__ void resolve_route_rows_kernel(SegGemm p, int* __restrict__ xrow, int* __restrict__ grow,
+                                          float* __restrict__ wsc, int64_t padded) {
+  for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < padded; r += (int64_t)gridDim.x * blockDim.x) {
+    const bool ok = r < p.n_routes;
+    xrow[r] = ok ? (int)idx_div(p.x_index[r], p.x_div) : -1;
+    grow[r] = ok ? (int)idx_div(p.g_index[r], p.g_div) : -1;
+    if (p.w) wsc[r] = ok ? round_to(load_as_float(p.w, p.w_dtype, p.w_index[r]), p.op_dtype) : 0.f;
+  }
+}
+
+int resolve_route_rows(const SegGemm& p, int* xrow, int* grow, float* wsc, cudaStream_t stream) {
+  const int64_t padded = p.n_routes + kRouteRowsPad;
+  const int grid = (int)std::min<int64_t>((padded + 255) / 256, 148 * 8);
+  resolve_route_rows_kernel<<<grid, 256, 0, stream>>>(p, xrow, grow, wsc, padded);
+  return check_launch("resolve_route_rows");
+}
+
 // grad_w[e] = sum over the expert's partial slots in chunk order (split
 // experts), or 0 for experts without routes; single-chunk experts were
 // written by their unit and are skipped.

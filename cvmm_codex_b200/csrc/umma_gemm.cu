@@ -56,19 +56,54 @@ constexpr uint32_t kAtomRowsBytes = 64 * 128;  // one 64-row x 128-byte MN-major
 #define CVMM_DBG(flags, bit) false
 #endif
 
+#ifdef CVMM_TRACE
+// Per-stage timestamps of CTA 0: [role][stage] (roles: 0 producer t0 issued,
+// 1 MMA saw full, 2 index warp published, 3 epilogue tile done).
+__device__ unsigned long long* g_trace;
+#define CVMM_STAMP(role, idx)                                                     \
+  do {                                                                            \
+    if (g_trace && blockIdx.x == 0 && (idx) < 4096) g_trace[(role) * 4096 + (idx)] = globaltimer_ns(); \
+  } while (0)
+#else
+#define CVMM_STAMP(role, idx) \
+  do {                        \
+  } while (0)
+#endif
+
 // Wait-site tags reported with CVMM_DEV_TIMEOUT.
 enum : int { kTagEmpty = 1, kTagFull = 2, kTagAccFull = 3, kTagAccEmpty = 4, kTagDrain = 5 };
 
-template <int BN, int S, bool WEIGHTED>
+// Shared-memory plan of one CTA (offsets from a 1024-byte aligned base):
+//   S operand stages (A tile 16 KiB + B tile BN x 128 B);
+//   barriers: full[S] empty[S] acc_full[2] acc_empty[2] drain idx_full[S] idx_empty[S] ready[S];
+//   epilogue staging: per epilogue warp a 32 x 32 block (rows of 144 B; the
+//   16-byte pad spreads the rows over the shared-memory banks);
+//   index ring (grad-W): S slots of the stage's x rows, grad rows and route
+//   weights, bulk-copied from a 16-byte aligned start 0-3 entries before the
+//   stage's first route (`off`).
+constexpr uint32_t kStageRowBytes = 144;
+constexpr int kRingEntries = 72;
+struct IdxSlot {
+  int x[kRingEntries];
+  int g[kRingEntries];
+  float w[kRingEntries];
+  int off;
+  int pad[3];
+};
+
+template <int BN, int S>
 struct Smem {
   static constexpr uint32_t a_bytes = BM * BK * 2;
   static constexpr uint32_t b_bytes = BN * BK * 2;
   static constexpr uint32_t stage_bytes = a_bytes + b_bytes;
-  static constexpr uint32_t bars = S * stage_bytes;         // full[S] empty[S] accf[2] acce[2] drain
-  static constexpr uint32_t misc = bars + (2 * S + 5) * 8;  // tmem slot, abort flag
-  static constexpr uint32_t scales = misc + 16;             // WEIGHTED: float[S+1][64]
-  static constexpr uint32_t used = scales + (WEIGHTED ? (S + 1) * 64 * 4 : 0);
-  static constexpr uint32_t alloc = used + 1024;            // slack to align the base
+  static constexpr uint32_t bars = S * stage_bytes;
+  static constexpr uint32_t misc = bars + (5 * S + 5) * 8;  // tmem slot, abort flag
+  static constexpr uint32_t staging = (misc + 16 + 127) / 128 * 128;  // 16-byte vector stores, bulk copies
+  static constexpr uint32_t ring = staging + 4 * 32 * kStageRowBytes;
+  static constexpr uint32_t used = ring + S * (uint32_t)sizeof(IdxSlot);
+  static constexpr uint32_t alloc = used + 1024;  // slack to align the base
+  static_assert(alloc <= 232448, "shared memory plan exceeds 227 KiB");
+  static_assert(staging % 128 == 0 && kStageRowBytes % 16 == 0 && ring % 16 == 0, "misaligned smem region");
 };
 
 struct Bars {
@@ -77,6 +112,9 @@ struct Bars {
   uint64_t* accf;
   uint64_t* acce;
   uint64_t* drain;
+  uint64_t* idxf;
+  uint64_t* idxe;
+  uint64_t* ready;
   volatile uint32_t* tmem_slot;
   volatile int* abort;
 };
@@ -89,6 +127,9 @@ __device__ __forceinline__ Bars carve_bars(uint8_t* smem) {
   b.accf = b.empty + S;
   b.acce = b.accf + 2;
   b.drain = b.acce + 2;
+  b.idxf = b.drain + 1;
+  b.idxe = b.idxf + S;
+  b.ready = b.idxe + S;
   b.tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + L::misc);
   b.abort = reinterpret_cast<volatile int*>(smem + L::misc + 4);
   return b;
@@ -168,9 +209,66 @@ __device__ __forceinline__ void load_acc32(uint32_t taddr, float (&v)[32]) {
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
+// Warp-cooperative store of a 32-row x 32-column block. Lane l holds row l's
+// 32 accumulator values `v` and `row_off`, the element offset of the row's
+// first column in `c` (-1: row not stored); `ncols` (<= 32) is warp-uniform.
+// The block is transposed through the warp's staging area (32 rows of 144 B)
+// so every st.global.v4 instruction writes whole row segments: 4 rows x 128 B
+// for fp32 outputs, 8 rows x 64 B for 16-bit ones, instead of 32 scattered
+// 16-byte pieces. Falls back to per-row stores for ragged or unaligned blocks.
+__device__ __forceinline__ void warp_store_block(void* c, int c_dtype, int64_t row_off, const float* v, int ncols,
+                                                 uint32_t stage, bool vec) {
+  const int lane = threadIdx.x & 31;
+  if (!vec || ncols != 32) {
+    if (row_off >= 0) store_row32(c, c_dtype, row_off, v, ncols, false);
+    return;
+  }
+  const uint32_t my = stage + lane * kStageRowBytes;
+  if (c_dtype == F32) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      ptx::st_shared_v4(my + 16 * q, __float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]),
+                        __float_as_uint(v[4 * q + 2]), __float_as_uint(v[4 * q + 3]));
+    __syncwarp();
+    const int q = lane & 7;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = (lane >> 3) + 4 * i;
+      const int64_t off = __shfl_sync(0xffffffffu, row_off, r);
+      uint32_t w0, w1, w2, w3;
+      ptx::ld_shared_v4(stage + r * kStageRowBytes + 16 * q, w0, w1, w2, w3);
+      if (off >= 0)
+        *reinterpret_cast<uint4*>(static_cast<float*>(c) + off + 4 * q) = make_uint4(w0, w1, w2, w3);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        w[i] = (uint32_t)float_to_bits(v[8 * q + 2 * i], c_dtype) |
+               ((uint32_t)float_to_bits(v[8 * q + 2 * i + 1], c_dtype) << 16);
+      ptx::st_shared_v4(my + 16 * q, w[0], w[1], w[2], w[3]);
+    }
+    __syncwarp();
+    const int q = lane & 3;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = (lane >> 2) + 8 * i;
+      const int64_t off = __shfl_sync(0xffffffffu, row_off, r);
+      uint32_t w0, w1, w2, w3;
+      ptx::ld_shared_v4(stage + r * kStageRowBytes + 16 * q, w0, w1, w2, w3);
+      if (off >= 0)
+        *reinterpret_cast<uint4*>(static_cast<char*>(c) + (off + 8 * q) * 2) = make_uint4(w0, w1, w2, w3);
+    }
+  }
+  __syncwarp();
+}
+
 // Barrier set-up and TMEM allocation (2 accumulator slots of BN columns).
 template <int BN, int S>
-__device__ __forceinline__ uint32_t setup(const Bars& b, int full_count) {
+__device__ __forceinline__ uint32_t setup(const Bars& b, int full_count, int idxe_count = kProducers,
+                                          int ready_count = 1) {
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -182,6 +280,11 @@ __device__ __forceinline__ uint32_t setup(const Bars& b, int full_count) {
       ptx::mbar_init(&b.acce[a], kEpilogue);
     }
     ptx::mbar_init(b.drain, 1);
+    for (int s = 0; s < S; ++s) {
+      ptx::mbar_init(&b.idxf[s], 1);
+      ptx::mbar_init(&b.idxe[s], idxe_count);
+      ptx::mbar_init(&b.ready[s], ready_count);
+    }
     *b.abort = 0;
     ptx::fence_mbar_init();
   }
@@ -197,9 +300,10 @@ __device__ __forceinline__ uint32_t setup(const Bars& b, int full_count) {
 
 // MMA issuer shared by both kernels: tile_nkb(t) gives the K stages of tile t.
 template <int BN, int S, class NkbFn>
-__device__ __forceinline__ void mma_loop(const Bars& b, uint8_t* smem, uint32_t tmem, uint32_t idesc,
-                                         bool a_mn, bool b_mn, int total, NkbFn tile_nkb, bool skip_mma) {
-  using L = Smem<BN, S, false>;
+__device__ __forceinline__ void mma_loop(const Bars& b, uint64_t* consume, uint8_t* smem, uint32_t tmem,
+                                         uint32_t idesc, bool a_mn, bool b_mn, int total, NkbFn tile_nkb,
+                                         bool skip_mma) {
+  using L = Smem<BN, S>;
   uint32_t it = 0;
   int local = 0;
   for (int tt = blockIdx.x; tt < total; tt += gridDim.x, ++local) {
@@ -212,11 +316,12 @@ __device__ __forceinline__ void mma_loop(const Bars& b, uint8_t* smem, uint32_t 
     bool ok = true;
     for (int kb = 0; kb < nkb; ++kb, ++it) {
       const int s = it % S;
-      if (!ptx::mbar_wait_or_abort(&b.full[s], (it / S) & 1, kTagFull, b.abort)) {
+      if (!ptx::mbar_wait_or_abort(&consume[s], (it / S) & 1, kTagFull, b.abort)) {
         ok = false;
         break;
       }
       ptx::tc_fence_after();
+      CVMM_STAMP(1, it);
       ptx::fence_proxy_async_smem();
       const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes);
       const uint32_t b_u = a_u + L::a_bytes;
@@ -241,10 +346,12 @@ __device__ __forceinline__ void mma_loop(const Bars& b, uint8_t* smem, uint32_t 
 // ============================================================ row-gathered GEMM
 // flags bit0: A fast path (cp.async), bit1: B fast path (cp.async when not
 // TMA), bit2: C vector stores.
-template <int BN, int S, bool B_KMAJOR, bool B_TMA>
+template <int BN, int S, bool B_KMAJOR, bool B_TMA, bool A_TMA>
 __global__ void __launch_bounds__(kThreads, 1)
-row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b, int flags, int n_n) {
-  using L = Smem<BN, S, false>;
+row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
+                const __grid_constant__ CUtensorMap tmap_a, int flags, int n_n) {
+  static_assert(!A_TMA || B_TMA, "TMA row gathers are used together with TMA weight tiles");
+  using L = Smem<BN, S>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_smem(smem_raw);
   const Bars bar = carve_bars<L, S>(smem);
@@ -253,13 +360,52 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b, int
   const int nkb = (int)((p.K + BK - 1) / BK);
   const int op = p.op_dtype;
   const bool a_fast = flags & 1, b_fast = flags & 2, c_vec = flags & 4;
-  const uint32_t tmem = setup<BN, S>(bar, kProducers + (B_TMA ? 1 : 0));
+  const uint32_t tmem = setup<BN, S>(bar, A_TMA ? 2 : kProducers + (B_TMA ? 1 : 0));
 
   auto entry = [&](int tt) -> int4 {
     return tt < total ? p.tiles[tt / n_n] : make_int4(0, 0, 0, 0);
   };
 
-  if (warp < 4) {
+  if (A_TMA && warp < 4) {
+    // ------------------------------------------------------------ A rows by TMA gather4
+    // Warp 0: lane l gathers rows 4l..4l+3 of every tile, 4 rows x 128 bytes
+    // per instruction, straight into the K-major swizzled A stage.
+    if (warp == 0) {
+      auto rows_of = [&](const int4& en, int (&r)[4]) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int rr = 4 * lane + q;
+          r[q] = rr < en.z ? (int)idx_div(p.a_index[en.y + rr], p.a_div) : -1;
+        }
+      };
+      int4 ent = entry(blockIdx.x);
+      int rows[4], rows_next[4];
+      rows_of(ent, rows);
+      int4 ent_next = entry(blockIdx.x + gridDim.x);
+      uint32_t it = 0;
+      bool aborted = false;
+      for (int tt = blockIdx.x; tt < total && !aborted; tt += gridDim.x) {
+        rows_of(ent_next, rows_next);
+        const int4 ent_after = entry(tt + 2 * gridDim.x);
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % S;
+          if (it >= S && !ptx::mbar_wait_or_abort(&bar.empty[s], ((it / S) - 1) & 1, kTagEmpty, bar.abort)) {
+            aborted = true;
+            break;
+          }
+          const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes);
+          if (lane == 0) ptx::mbar_arrive_expect_tx(&bar.full[s], L::a_bytes);
+          __syncwarp();
+          if (!CVMM_DBG(flags, 512))
+            ptx::tma_gather4(a_u + lane * 512, &tmap_a, &bar.full[s], kb * BK, rows[0], rows[1], rows[2], rows[3]);
+        }
+        ent = ent_next;
+        ent_next = ent_after;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) rows[q] = rows_next[q];
+      }
+    }
+  } else if (warp < 4) {
     // ------------------------------------------------------------ producers
     const int t = threadIdx.x;
     const int ac = t & 7;
@@ -331,6 +477,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b, int
         }
         if (!a_fast || (!B_TMA && !b_fast)) ptx::fence_proxy_async_smem();
         ptx::cp_async_arrive_noinc(&bar.full[s]);
+        if (t == 0) CVMM_STAMP(0, it);
       }
       ent = ent_next;
       ent_next = ent_after;
@@ -342,6 +489,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b, int
     // ------------------------------------------------------------ epilogue
     const int ew = warp - 4;
     const int rr = ew * 32 + lane;
+    const uint32_t stage = ptx::smem_u32(smem + L::staging) + ew * 32 * kStageRowBytes;
     int4 ent = entry(blockIdx.x);
     int64_t crow = rr < ent.z ? p.c_index[ent.y + rr] : -1;
     int4 ent_next = entry(blockIdx.x + gridDim.x);
@@ -352,6 +500,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b, int
       const int a = local & 1;
       if (!ptx::mbar_wait_or_abort(&bar.accf[a], (local >> 1) & 1, kTagAccFull, bar.abort)) break;
       ptx::tc_fence_after();
+      if (rr == 0) CVMM_STAMP(2, local);
       const int64_t n0 = (int64_t)(tt % n_n) * BN;
       const bool row_ok = crow >= 0;
       float wv = 0.f, dot = 0.f;
@@ -366,8 +515,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b, int
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = 0.f;
         }
-        if (!row_ok) continue;
-        if (p.mode == 1) {
+        if (p.mode == 1 && row_ok) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const float av = round_to(v[j], op);
@@ -375,11 +523,12 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b, int
             v[j] = round_to(av * wv, op);
           }
         }
-        store_row32(p.c, p.c_dtype, crow * p.c_ld + nc, v, ncols, c_vec);
+        warp_store_block(p.c, p.c_dtype, row_ok ? crow * p.c_ld + nc : -1, v, ncols, stage, c_vec);
       }
       if (p.mode == 1 && row_ok) atomicAdd(p.gsel + crow, dot);
       ptx::tc_fence_before();
       ptx::mbar_arrive(&bar.acce[a]);
+      if (rr == 0) CVMM_STAMP(3, local);
       ent = ent_next;
       ent_next = ent_after;
       crow = crow_next;
@@ -388,7 +537,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b, int
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = ptx::instr_desc_f16(BM, BN, op == BF16, false, !B_KMAJOR);
-      mma_loop<BN, S>(bar, smem, tmem, idesc, false, !B_KMAJOR, total, [&](int) { return nkb; },
+      mma_loop<BN, S>(bar, bar.full, smem, tmem, idesc, false, !B_KMAJOR, total, [&](int) { return nkb; },
                       CVMM_DBG(flags, 256));
     }
     __syncwarp();
@@ -430,21 +579,21 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b, int
   }
 }
 
-// Multiplies this thread's G chunks of stage `j` by their route weights (kept
-// in `scales`) and rounds to the op dtype: the reference multiplies the bf16
-// grad row by the bf16 weight and rounds the product to bf16 before the dot
-// (cvmm.py:591-599).
+// Multiplies this thread's G chunks of stage `j` by their route weights (from
+// the index ring) and rounds to the op dtype: the reference multiplies the
+// bf16 grad row by the bf16 weight and rounds the product to bf16 before the
+// dot (cvmm.py:591-599).
 template <int BN, int S>
-__device__ __forceinline__ void scale_rows(uint8_t* smem, const float* scales, uint32_t j, int t, int op) {
-  using L = Smem<BN, S, true>;
+__device__ __forceinline__ void scale_rows(uint8_t* smem, const IdxSlot* ring, uint32_t j, int t, int op) {
+  using L = Smem<BN, S>;
   constexpr int GCPR = BN / 8;
-  const int sj = j % S, sl = j % (S + 1);
+  const int sj = j % S;
   const int gc = t % GCPR;
   const uint32_t bj = ptx::smem_u32(smem + sj * L::stage_bytes) + L::a_bytes;
 #pragma unroll
   for (int i = 0; i < BN / 16; ++i) {
     const int kr = t / GCPR + (kProducers / GCPR) * i;
-    const float sc = scales[sl * 64 + kr];
+    const float sc = ring[sj].w[ring[sj].off + kr];
     const uint32_t addr = bj + swz(kr, gc, kAtomRowsBytes);
     uint32_t w4[4];
     ptx::ld_shared_v4(addr, w4[0], w4[1], w4[2], w4[3]);
@@ -464,11 +613,16 @@ __device__ __forceinline__ void scale_rows(uint8_t* smem, const float* scales, u
 // over many tiles. A unit covering its whole expert writes grad_w; chunks of
 // a split expert write partial slots that seg_reduce adds in a fixed order.
 // Both operands are gathered rows: A = x^T (MN-major, rows = routes), B = the
-// (weight-scaled) grad rows (MN-major).
+// (weight-scaled) grad rows (MN-major). Warp 9 runs up to S stages ahead of
+// the producers, resolving each stage's 64 route rows (x row, grad row, route
+// weight) into the shared-memory index ring, so the producers never wait on
+// index loads.
 // flags bit0: X fast path, bit1: G fast path, bit2: out vector stores.
-template <int BN, int S, bool WEIGHTED>
-__global__ void __launch_bounds__(kThreads, 1) seg_gemm_kernel(const SegGemm p, int flags, int n_m, int n_n) {
-  using L = Smem<BN, S, WEIGHTED>;
+template <int BN, int S, bool WEIGHTED, bool G_TMA>
+__global__ void __launch_bounds__(kThreads, 1)
+seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_g,
+                int flags, int n_m, int n_n) {
+  using L = Smem<BN, S>;
   constexpr int GCPR = BN / 8;    // G tile: 16-byte chunks per route row
   constexpr int GROWS = BN / 16;  // G rows per producer thread per stage
   // The weighted variant scales G in shared memory after it lands, so its
@@ -477,20 +631,110 @@ __global__ void __launch_bounds__(kThreads, 1) seg_gemm_kernel(const SegGemm p, 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_smem(smem_raw);
   const Bars bar = carve_bars<L, S>(smem);
-  float* scales = reinterpret_cast<float*>(smem + L::scales);
+  IdxSlot* ring = reinterpret_cast<IdxSlot*>(smem + L::ring);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per_unit = n_m * n_n;
   const int total = *p.n_units * per_unit;
   const int op = p.op_dtype;
   const bool x_fast = flags & 1, g_fast = flags & 2, o_vec = flags & 4;
-  const uint32_t tmem = setup<BN, S>(bar, kProducers);
+  constexpr int kTransform = kProducers - 32;  // warps 1-3 scale weighted grad rows
+  const uint32_t tmem = G_TMA ? setup<BN, S>(bar, 1, WEIGHTED ? kProducers : 32, kTransform)
+                              : setup<BN, S>(bar, kProducers);
 
   auto entry = [&](int tt) -> int4 {
     return tt < total ? p.units[tt / per_unit] : make_int4(0, 0, -1, 0);
   };
   auto nkb_of = [&](const int4& u) -> int { return (int)((u.w - u.y + BK - 1) / BK); };
 
-  if (warp < 4) {
+  if (G_TMA && warp == 0) {
+    // ------------------------------------------------------------ gathers by TMA
+    // Per stage: 64 route rows of x (the m slice) and of the grad (the n slice),
+    // 4 rows per gather4, into the MN-major swizzled stages (route = k row).
+    uint32_t it = 0;
+    bool aborted = false;
+    for (int tt = blockIdx.x; tt < total && !aborted; tt += gridDim.x) {
+      const int4 u = entry(tt);
+      const int rem = tt % per_unit;
+      const int m0 = (rem / n_n) * BM, n0 = (rem % n_n) * BN;
+      const int nkb = nkb_of(u);
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % S;
+        if ((it >= S && !ptx::mbar_wait_or_abort(&bar.empty[s], ((it / S) - 1) & 1, kTagEmpty, bar.abort)) ||
+            !ptx::mbar_wait_or_abort(&bar.idxf[s], (it / S) & 1, kTagFull, bar.abort)) {
+          aborted = true;
+          break;
+        }
+        const IdxSlot& slot = ring[s];
+        const int off = slot.off;
+        const int64_t rb = u.y + (int64_t)kb * BK;
+        const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes), b_u = a_u + L::a_bytes;
+        if (lane == 0) ptx::mbar_arrive_expect_tx(&bar.full[s], L::a_bytes + L::b_bytes);
+        __syncwarp();
+        {
+          const int atom = lane >> 4, grp = lane & 15;
+          int r[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int kr = 4 * grp + q;
+            r[q] = rb + kr < u.w ? slot.x[off + kr] : -1;
+          }
+          ptx::tma_gather4(a_u + atom * kAtomRowsBytes + grp * 512, &tmap_x, &bar.full[s], m0 + 64 * atom, r[0],
+                           r[1], r[2], r[3]);
+        }
+#pragma unroll
+        for (int gi = lane; gi < BN / 4; gi += 32) {
+          const int atom = gi >> 4, grp = gi & 15;
+          int r[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int kr = 4 * grp + q;
+            r[q] = rb + kr < u.w ? slot.g[off + kr] : -1;
+          }
+          ptx::tma_gather4(b_u + atom * kAtomRowsBytes + grp * 512, &tmap_g, &bar.full[s], n0 + 64 * atom, r[0],
+                           r[1], r[2], r[3]);
+        }
+        ptx::mbar_arrive(&bar.idxe[s]);
+        if (lane == 0) CVMM_STAMP(0, it);
+      }
+    }
+  } else if (G_TMA && warp < 4) {
+    // ------------------------------------------------------------ transform (weighted)
+    if (WEIGHTED) {
+      const int tx = threadIdx.x - 32;
+      constexpr int CPR = BN / 8;
+      uint32_t it = 0;
+      bool aborted = false;
+      for (int tt = blockIdx.x; tt < total && !aborted; tt += gridDim.x) {
+        const int nkb = nkb_of(entry(tt));
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % S;
+          if (!ptx::mbar_wait_or_abort(&bar.full[s], (it / S) & 1, kTagFull, bar.abort)) {
+            aborted = true;
+            break;
+          }
+          const IdxSlot& slot = ring[s];
+          const uint32_t b_u = ptx::smem_u32(smem + s * L::stage_bytes) + L::a_bytes;
+          for (int c = tx; c < 64 * CPR; c += kTransform) {
+            const int kr = c / CPR, col = c % CPR;
+            const float sc = slot.w[slot.off + kr];
+            const uint32_t addr = b_u + swz(kr, col, kAtomRowsBytes);
+            uint32_t w4[4];
+            ptx::ld_shared_v4(addr, w4[0], w4[1], w4[2], w4[3]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float lo = bits_to_float((uint16_t)(w4[q] & 0xffffu), op) * sc;
+              const float hi = bits_to_float((uint16_t)(w4[q] >> 16), op) * sc;
+              w4[q] = (uint32_t)float_to_bits(lo, op) | ((uint32_t)float_to_bits(hi, op) << 16);
+            }
+            ptx::st_shared_v4(addr, w4[0], w4[1], w4[2], w4[3]);
+          }
+          ptx::fence_proxy_async_smem();
+          ptx::mbar_arrive(&bar.ready[s]);
+          ptx::mbar_arrive(&bar.idxe[s]);
+        }
+      }
+    }
+  } else if (warp < 4) {
     // ------------------------------------------------------------ producers
     const int t = threadIdx.x;
     const char* xbase = static_cast<const char*>(p.x);
@@ -498,97 +742,76 @@ __global__ void __launch_bounds__(kThreads, 1) seg_gemm_kernel(const SegGemm p, 
     const int64_t xsz = dtype_bytes(p.x_dtype), gsz = dtype_bytes(p.g_dtype);
     const int xc = t & 15;    // X tile: 64 route rows x 16 chunks (128 m columns)
     const int gc = t % GCPR;  // G tile: 64 route rows x GCPR chunks
-    // Indices are below 2^31 (checked by the launcher): 32-bit registers.
-    int xi[8], gi[GROWS], wi[GROWS];
-    // Row indices of stage (u, kb) are fetched one stage ahead.
-    auto fetch = [&](const int4& u, int kb) {
-      const int64_t rb = u.y + (int64_t)kb * BK;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int64_t r = rb + (t >> 4) + 8 * i;
-        xi[i] = r < u.w ? (int)p.x_index[r] : -1;
-      }
-#pragma unroll
-      for (int i = 0; i < GROWS; ++i) {
-        const int64_t r = rb + t / GCPR + (kProducers / GCPR) * i;
-        gi[i] = r < u.w ? (int)p.g_index[r] : -1;
-        if (WEIGHTED) wi[i] = r < u.w ? (int)p.w_index[r] : -1;
-      }
-    };
-    int4 u = entry(blockIdx.x);
-    int4 u_next = entry(blockIdx.x + gridDim.x);
-    if ((int)blockIdx.x < total) fetch(u, 0);
     uint32_t it = 0;
     bool aborted = false;
     for (int tt = blockIdx.x; tt < total && !aborted; tt += gridDim.x) {
-      const int4 u_after = entry(tt + 2 * gridDim.x);
+      const int4 u = entry(tt);
       const int rem = tt % per_unit;
       const int64_t m0 = (int64_t)(rem / n_n) * BM, n0 = (int64_t)(rem % n_n) * BN;
       const int nkb = nkb_of(u);
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % S;
-        bool bad = it >= S && !ptx::mbar_wait_or_abort(&bar.empty[s], ((it / S) - 1) & 1, kTagEmpty, bar.abort);
-        if (WEIGHTED) bad = ptx::named_bar_or(1, kProducers, bad);
-        if (bad) {
+        if ((it >= S && !ptx::mbar_wait_or_abort(&bar.empty[s], ((it / S) - 1) & 1, kTagEmpty, bar.abort)) ||
+            !ptx::mbar_wait_or_abort(&bar.idxf[s], (it / S) & 1, kTagFull, bar.abort)) {
           aborted = true;
           break;
         }
-        const char* xrow[8];
-        const char* grow[GROWS];
-        float wsc[GROWS];
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          xrow[i] = xi[i] >= 0 ? xbase + (idx_div(xi[i], p.x_div) * p.x_ld + m0) * xsz : nullptr;
-#pragma unroll
-        for (int i = 0; i < GROWS; ++i) {
-          grow[i] = gi[i] >= 0 ? gbase + (idx_div(gi[i], p.g_div) * p.g_ld + n0) * gsz : nullptr;
-          if (WEIGHTED) wsc[i] = wi[i] >= 0 ? round_to(load_as_float(p.w, p.w_dtype, wi[i]), op) : 0.f;
-        }
-        if (kb + 1 < nkb) fetch(u, kb + 1);
-        else if (tt + (int)gridDim.x < total) fetch(u_next, 0);
+        const IdxSlot& slot = ring[s];
+        const int off = slot.off;
+        const int64_t rb = u.y + (int64_t)kb * BK;
         const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes), b_u = a_u + L::a_bytes;
         if (!CVMM_DBG(flags, 512)) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const int kr = (t >> 4) + 8 * i;
-            load_chunk(a_u + swz(kr, xc, kAtomRowsBytes), xrow[i], xc * 8, p.M - m0, p.x_dtype, 1, op, x_fast, p.x);
+            const int xr = slot.x[off + kr];
+            const char* row = rb + kr < u.w ? xbase + ((int64_t)xr * p.x_ld + m0) * xsz : nullptr;
+            load_chunk(a_u + swz(kr, xc, kAtomRowsBytes), row, xc * 8, p.M - m0, p.x_dtype, 1, op, x_fast, p.x);
           }
         }
+        if (!CVMM_DBG(flags, 1024)) {
 #pragma unroll
-        for (int i = 0; i < GROWS; ++i) {
-          const int kr = t / GCPR + (kProducers / GCPR) * i;
-          if (!CVMM_DBG(flags, 1024))
-            load_chunk(b_u + swz(kr, gc, kAtomRowsBytes), grow[i], gc * 8, p.N - n0, p.g_dtype, 1, op, g_fast, p.g);
-          if (WEIGHTED && gc == 0) scales[(it % (S + 1)) * 64 + kr] = wsc[i];
+          for (int i = 0; i < GROWS; ++i) {
+            const int kr = t / GCPR + (kProducers / GCPR) * i;
+            const int gr = slot.g[off + kr];
+            const char* row = rb + kr < u.w ? gbase + ((int64_t)gr * p.g_ld + n0) * gsz : nullptr;
+            load_chunk(b_u + swz(kr, gc, kAtomRowsBytes), row, gc * 8, p.N - n0, p.g_dtype, 1, op, g_fast, p.g);
+          }
         }
+        if (t == 0) CVMM_STAMP(0, it);
         if (!WEIGHTED) {
           if (!x_fast || !g_fast) ptx::fence_proxy_async_smem();
           ptx::cp_async_arrive_noinc(&bar.full[s]);
+          ptx::mbar_arrive(&bar.idxe[s]);
         } else {
+          // Hand over stage it-LAG: its copies landed; scale it in place.
           ptx::cp_async_commit();
-          ptx::named_bar_sync(1, kProducers);
           if (it >= (uint32_t)LAG) {
+            const uint32_t j = it - LAG;
             ptx::cp_async_wait<LAG>();
-            scale_rows<BN, S>(smem, scales, it - LAG, t, op);
+            scale_rows<BN, S>(smem, ring, j, t, op);
             ptx::fence_proxy_async_smem();
-            ptx::mbar_arrive(&bar.full[(it - LAG) % S]);
+            ptx::mbar_arrive(&bar.full[j % S]);
+            ptx::mbar_arrive(&bar.idxe[j % S]);
           }
         }
       }
-      u = u_next;
-      u_next = u_after;
     }
     ptx::cp_async_wait_all();
     if (WEIGHTED && !aborted) {
       const uint32_t first = it > (uint32_t)LAG ? it - LAG : 0;
-      for (uint32_t j = first; j < it; ++j) scale_rows<BN, S>(smem, scales, j, t, op);
+      for (uint32_t j = first; j < it; ++j) scale_rows<BN, S>(smem, ring, j, t, op);
       ptx::fence_proxy_async_smem();
-      for (uint32_t j = first; j < it; ++j) ptx::mbar_arrive(&bar.full[j % S]);
+      for (uint32_t j = first; j < it; ++j) {
+        ptx::mbar_arrive(&bar.full[j % S]);
+        ptx::mbar_arrive(&bar.idxe[j % S]);
+      }
     }
   } else if (warp < 8) {
     // ------------------------------------------------------------ epilogue
     const int ew = warp - 4;
     const int mr = ew * 32 + lane;
+    const uint32_t stage = ptx::smem_u32(smem + L::staging) + ew * 32 * kStageRowBytes;
     int local = 0;
     for (int tt = blockIdx.x; tt < total; tt += gridDim.x, ++local) {
       const int4 u = entry(tt);
@@ -611,18 +834,46 @@ __global__ void __launch_bounds__(kThreads, 1) seg_gemm_kernel(const SegGemm p, 
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = 0.f;
         }
-        if (m < p.M) store_row32(dst, F32, m * p.N + nc, v, ncols, o_vec);
+        warp_store_block(dst, F32, m < p.M ? m * p.N + nc : -1, v, ncols, stage, o_vec);
       }
       ptx::tc_fence_before();
       ptx::mbar_arrive(&bar.acce[a]);
+      if (mr == 0) CVMM_STAMP(3, local);
     }
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
       const uint32_t idesc = ptx::instr_desc_f16(BM, BN, op == BF16, true, true);
-      mma_loop<BN, S>(bar, smem, tmem, idesc, true, true, total, [&](int tt) { return nkb_of(entry(tt)); },
+      mma_loop<BN, S>(bar, WEIGHTED && G_TMA ? bar.ready : bar.full, smem, tmem, idesc, true, true, total, [&](int tt) { return nkb_of(entry(tt)); },
                       CVMM_DBG(flags, 256));
     }
     __syncwarp();
+  } else {
+    // ------------------------------------------------------------ index warp
+    uint32_t it = 0;
+    bool aborted = false;
+    for (int tt = blockIdx.x; tt < total && !aborted; tt += gridDim.x) {
+      const int4 u = entry(tt);
+      const int nkb = nkb_of(u);
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % S;
+        if (it >= S && !ptx::mbar_wait_or_abort(&bar.idxe[s], ((it / S) - 1) & 1, kTagEmpty, bar.abort)) {
+          aborted = true;
+          break;
+        }
+        if (lane == 0) {
+          const int64_t rb = u.y + (int64_t)kb * BK;
+          const int64_t al = rb & ~(int64_t)3;
+          ring[s].off = (int)(rb - al);
+          constexpr uint32_t kBytes = kRingEntries * 4;
+          ptx::mbar_arrive_expect_tx(&bar.idxf[s], (WEIGHTED ? 3 : 2) * kBytes);
+          ptx::bulk_load(ptx::smem_u32(ring[s].x), p.xrow + al, kBytes, &bar.idxf[s]);
+          ptx::bulk_load(ptx::smem_u32(ring[s].g), p.grow + al, kBytes, &bar.idxf[s]);
+          if (WEIGHTED) ptx::bulk_load(ptx::smem_u32(ring[s].w), p.wsc + al, kBytes, &bar.idxf[s]);
+        }
+        __syncwarp();
+        if (lane == 0) CVMM_STAMP(2, it);
+      }
+    }
   }
   ptx::tc_fence_before();
   __syncthreads();
@@ -687,9 +938,24 @@ static bool make_b_map(CUtensorMap* map, const void* base, int dtype, int64_t co
   return r == CUDA_SUCCESS;
 }
 
+// 2-D TMA map over a row-major [rows, cols] operand for tile::gather4: a box
+// of 64 columns (128 bytes) by one row, 128-byte swizzle.
+static bool make_rows_map(CUtensorMap* map, const void* base, int dtype, int64_t cols, int64_t rows, int64_t ld) {
+  auto fn = encode_fn();
+  if (!fn || !aligned16(base) || (ld * 2) % 16 != 0 || rows <= 0 || cols <= 0 || rows > INT32_MAX) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {64, 1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype == BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 template <int BN, int S, bool BK_MAJOR>
 static int row_launch(const RowGemm& p, int64_t max_tiles, int flags, cudaStream_t stream) {
-  using L = Smem<BN, S, false>;
+  using L = Smem<BN, S>;
   const int n_n = (int)((p.N + BN - 1) / BN);
   CUtensorMap map;
   memset(&map, 0, sizeof(map));
@@ -699,36 +965,66 @@ static int row_launch(const RowGemm& p, int64_t max_tiles, int flags, cudaStream
                    : make_b_map(&map, p.b, p.op_dtype, p.N, p.K, p.n_experts, p.bs_k, p.bs_e, 64);
   }
   if (dbg_flags() & 2048) tma = false;
+  CUtensorMap amap;
+  memset(&amap, 0, sizeof(amap));
+  const bool a_tma = tma && (flags & 1) && (dbg_flags() & 8192) &&
+                     make_rows_map(&amap, p.a, p.op_dtype, p.K, p.a_rows, p.a_ld);
   const int64_t work = max_tiles * n_n;
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(work, sm_count()));
-  if (tma) {
-    auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true>;
+  if (a_tma) {
+    auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true, true>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
-    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, flags, n_n);
+    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, flags, n_n);
+  } else if (tma) {
+    auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true, false>;
+    int rc = set_smem(kern, L::alloc);
+    if (rc) return rc;
+    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, flags, n_n);
   } else {
-    auto kern = row_gemm_kernel<BN, S, BK_MAJOR, false>;
+    auto kern = row_gemm_kernel<BN, S, BK_MAJOR, false, false>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
-    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, flags, n_n);
+    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, flags, n_n);
   }
   return check_launch("row_gemm_umma");
 }
 
 template <int BN, int S, bool W>
 static int seg_launch(const SegGemm& p, int64_t max_units, int flags, cudaStream_t stream) {
-  using L = Smem<BN, S, W>;
-  auto kern = seg_gemm_kernel<BN, S, W>;
-  int rc = set_smem(kern, L::alloc);
-  if (rc) return rc;
+  using L = Smem<BN, S>;
   const int n_m = (int)((p.M + BM - 1) / BM), n_n = (int)((p.N + BN - 1) / BN);
   const int64_t work = max_units * n_m * n_n;
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(work, sm_count()));
-  kern<<<grid, kThreads, L::alloc, stream>>>(p, flags, n_m, n_n);
+  CUtensorMap xmap, gmap;
+  memset(&xmap, 0, sizeof(xmap));
+  memset(&gmap, 0, sizeof(gmap));
+  // Gathered rows index at most n_routes rows of x and of the grad.
+  const bool gt = (flags & 3) == 3 && !(dbg_flags() & 4096) &&
+                  make_rows_map(&xmap, p.x, p.op_dtype, p.M, p.n_routes, p.x_ld) &&
+                  make_rows_map(&gmap, p.g, p.op_dtype, p.N, p.n_routes, p.g_ld);
+  if (gt) {
+    auto kern = seg_gemm_kernel<BN, S, W, true>;
+    int rc = set_smem(kern, L::alloc);
+    if (rc) return rc;
+    kern<<<grid, kThreads, L::alloc, stream>>>(p, xmap, gmap, flags, n_m, n_n);
+  } else {
+    auto kern = seg_gemm_kernel<BN, S, W, false>;
+    int rc = set_smem(kern, L::alloc);
+    if (rc) return rc;
+    kern<<<grid, kThreads, L::alloc, stream>>>(p, xmap, gmap, flags, n_m, n_n);
+  }
   return check_launch("seg_gemm_umma");
 }
 
 }  // namespace umma
+
+#ifdef CVMM_TRACE
+extern "C" int cvmm_debug_set_trace(void* buf) {
+  unsigned long long* q = static_cast<unsigned long long*>(buf);
+  return cudaMemcpyToSymbol(umma::g_trace, &q, sizeof(q)) == cudaSuccess ? 0 : -3;
+}
+#endif
 
 int launch_row_gemm_umma(const RowGemm& p, int64_t max_tiles, cudaStream_t stream) {
   using namespace umma;
@@ -740,14 +1036,11 @@ int launch_row_gemm_umma(const RowGemm& p, int64_t max_tiles, cudaStream_t strea
     flags |= 2;
   if (p.c_ld % 8 == 0 && aligned16(p.c)) flags |= 4;
   if (p.N <= 64) {
-    return b_kmajor ? row_launch<64, 8, true>(p, max_tiles, flags, stream)
-                    : row_launch<64, 8, false>(p, max_tiles, flags, stream);
-  } else if (p.N <= 128) {
-    return b_kmajor ? row_launch<128, 6, true>(p, max_tiles, flags, stream)
-                    : row_launch<128, 6, false>(p, max_tiles, flags, stream);
+    return b_kmajor ? row_launch<64, 7, true>(p, max_tiles, flags, stream)
+                    : row_launch<64, 7, false>(p, max_tiles, flags, stream);
   }
-  return b_kmajor ? row_launch<256, 4, true>(p, max_tiles, flags, stream)
-                  : row_launch<256, 4, false>(p, max_tiles, flags, stream);
+  return b_kmajor ? row_launch<128, 5, true>(p, max_tiles, flags, stream)
+                  : row_launch<128, 5, false>(p, max_tiles, flags, stream);
 }
 
 int launch_seg_gemm_umma(const SegGemm& p, int64_t max_units, cudaStream_t stream) {
@@ -757,9 +1050,9 @@ int launch_seg_gemm_umma(const SegGemm& p, int64_t max_units, cudaStream_t strea
   if (p.g_dtype == p.op_dtype && p.g_ld % 8 == 0 && aligned16(p.g)) flags |= 2;
   if (p.N % 4 == 0 && aligned16(p.out) && aligned16(p.partials)) flags |= 4;
   const bool w = p.w != nullptr;
-  if (p.N <= 64) return w ? seg_launch<64, 8, true>(p, max_units, flags, stream) : seg_launch<64, 8, false>(p, max_units, flags, stream);
-  if (p.N <= 128) return w ? seg_launch<128, 6, true>(p, max_units, flags, stream) : seg_launch<128, 6, false>(p, max_units, flags, stream);
-  return w ? seg_launch<256, 4, true>(p, max_units, flags, stream) : seg_launch<256, 4, false>(p, max_units, flags, stream);
+  if (p.N <= 64) return w ? seg_launch<64, 7, true>(p, max_units, flags, stream) : seg_launch<64, 7, false>(p, max_units, flags, stream);
+  if (p.N <= 128) return w ? seg_launch<128, 5, true>(p, max_units, flags, stream) : seg_launch<128, 5, false>(p, max_units, flags, stream);
+  return w ? seg_launch<256, 3, true>(p, max_units, flags, stream) : seg_launch<256, 3, false>(p, max_units, flags, stream);
 }
 
 }  // namespace cvmm
