@@ -92,7 +92,7 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
 }
 
 // ---------------------------------------------------------------- TMA
-// 3-D tiled tensor load into shared memory, completing on `bar` (no multicast).
+// 3-D tiled tensor load into shared memory, completing on `bar`; this CTA's shared memory only.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint64_t* bar, int c0, int c1,
                                             int c2) {
   asm volatile(
@@ -104,7 +104,7 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
 
 // TMA row gather: rows r0..r3 (64-element box of columns starting at c0) of a
 // 2-D tensor map with a one-row box land as four consecutive 128-byte rows at
-// `dst`, completing on `bar` (no multicast). Out-of-range rows read zeros.
+// `dst`, completing on `bar`; this CTA's shared memory only. Out-of-range rows read zeros.
 __device__ __forceinline__ void tma_gather4(uint32_t dst, const void* tmap, uint64_t* bar, int c0, int r0, int r1,
                                             int r2, int r3) {
   asm volatile(
