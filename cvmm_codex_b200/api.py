@@ -204,12 +204,20 @@ class CVMM(torch.autograd.Function):
         grad_x = grad_keys = grad_w = None
         if w is None:
             g2 = g.reshape(n_routes, g.shape[-1])
+            g_rows, g_idx, g_pad = g2, route, None
+            if op != torch.float32 and g2.dtype == op:
+                # One expert-padded sorted copy of the route grads (the
+                # reference's grouping copy, cvmm.py:1161) lets both GEMMs read
+                # them as dense tensor-core tiles.
+                g_rows, g_pad = ops.sort_rows_padded(g2, route, 1, sel, offsets, n_experts)
+                g_idx = None
             if need_keys:
                 # dW_e = sum_p x[sel_index[p]]^T g[route[p]]  (cvmm.py:1163-1198)
-                grad_keys = ops.backward_w(x, sel_index, 1, g2, route, 1, offsets, n_experts, op)
+                grad_keys = ops.backward_w(x, sel_index, 1, g_rows, g_idx, 1, offsets, n_experts, op,
+                                           g_pad_start=g_pad)
             if need_x:
                 # gx_route[route] = g[route] W_e^T, then summed over k (cvmm.py:1199-1223)
-                gxr = ops.backward_x(g2, route, 1, route, offsets, keys_op, x.dtype, op)
+                gxr = ops.backward_x(g_rows, g_idx, 1, route, offsets, keys_op, x.dtype, op, g_pad_start=g_pad)
                 if x_rows == n_routes:
                     grad_x = gxr.view_as(x)
                 else:

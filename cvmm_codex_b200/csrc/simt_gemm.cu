@@ -124,7 +124,16 @@ __global__ void resolve_route_rows_kernel(SegGemm p, int* __restrict__ xrow, int
   for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < padded; r += (int64_t)gridDim.x * blockDim.x) {
     const bool ok = r < p.n_routes;
     xrow[r] = ok ? (int)idx_div(p.x_index[r], p.x_div) : -1;
-    grow[r] = ok ? (int)idx_div(p.g_index[r], p.g_div) : -1;
+    if (p.g_pad_start) {
+      int64_t lo = 0, hi = p.n_experts - 1;  // expert of sorted position r: first e with offsets[e] > r
+      while (ok && lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (p.offsets[mid] > r) hi = mid; else lo = mid + 1;
+      }
+      grow[r] = ok ? (int)(p.g_pad_start[lo] + r - seg_begin(p.offsets, lo)) : -1;
+    } else {
+      grow[r] = ok ? (int)idx_div(p.g_index[r], p.g_div) : -1;
+    }
     if (p.w) wsc[r] = ok ? round_to(load_as_float(p.w, p.w_dtype, p.w_index[r]), p.op_dtype) : 0.f;
   }
 }
@@ -134,6 +143,63 @@ int resolve_route_rows(const SegGemm& p, int* xrow, int* grow, float* wsc, cudaS
   const int grid = (int)std::min<int64_t>((padded + 255) / 256, 148 * 8);
   resolve_route_rows_kernel<<<grid, 256, 0, stream>>>(p, xrow, grow, wsc, padded);
   return check_launch("resolve_route_rows");
+}
+
+// pad_start[e] = sum over e' < e of round_up(count(e'), pad): one CTA scan.
+__global__ void __launch_bounds__(1024)
+pad_starts_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int64_t pad, int* __restrict__ pad_start) {
+  __shared__ int warp_tot[32];
+  const int t = threadIdx.x;
+  const int64_t per = (n_experts + blockDim.x - 1) / blockDim.x;
+  const int64_t e0 = min((int64_t)t * per, n_experts), e1 = min(e0 + per, n_experts);
+  int tot = 0;
+  for (int64_t e = e0; e < e1; ++e) tot += (int)((offsets[e] - seg_begin(offsets, e) + pad - 1) / pad * pad);
+  int run = block_exclusive_scan(tot, warp_tot);
+  for (int64_t e = e0; e < e1; ++e) {
+    pad_start[e] = run;
+    run += (int)((offsets[e] - seg_begin(offsets, e) + pad - 1) / pad * pad);
+  }
+}
+
+int pad_starts(const int64_t* offsets, int64_t n_experts, int64_t pad, int* pad_start, cudaStream_t stream) {
+  pad_starts_kernel<<<1, 1024, 0, stream>>>(offsets, n_experts, pad, pad_start);
+  return check_launch("pad_starts");
+}
+
+// One warp per sorted route row: dst[pad_start[e] + p - seg_begin(e)] = src[index[p] / div].
+__global__ void sort_rows_padded_kernel(const char* __restrict__ src, int esz, int64_t src_ld,
+                                        const int64_t* __restrict__ index, int64_t div,
+                                        const int32_t* __restrict__ sorted_sel, const int64_t* __restrict__ offsets,
+                                        const int* __restrict__ pad_start, int64_t n_routes, int64_t cols,
+                                        char* __restrict__ dst, bool vec) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t p = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); p < n_routes; p += warps) {
+    const int64_t e = sorted_sel[p];
+    const int64_t q = pad_start[e] + p - seg_begin(offsets, e);
+    const char* from = src + idx_div(index[p], div) * src_ld * esz;
+    char* to = dst + q * cols * esz;
+    const int64_t bytes = cols * esz;
+    if (vec) {
+      for (int64_t b = lane * 16; b < bytes; b += 32 * 16)
+        *reinterpret_cast<uint4*>(to + b) = *reinterpret_cast<const uint4*>(from + b);
+    } else {
+      for (int64_t b = lane; b < bytes; b += 32) to[b] = from[b];
+    }
+  }
+}
+
+int sort_rows_padded(const void* src, int dtype, int64_t src_ld, const int64_t* index, int64_t div,
+                     const int32_t* sorted_sel, const int64_t* offsets, const int* pad_start, int64_t n_routes,
+                     int64_t cols, void* dst, cudaStream_t stream) {
+  const int esz = dtype_bytes(dtype);
+  const bool vec = ((cols * esz) % 16 == 0) && ((src_ld * esz) % 16 == 0) && (((uintptr_t)src & 15u) == 0) &&
+                   (((uintptr_t)dst & 15u) == 0);
+  const int64_t blocks = std::min<int64_t>((n_routes + 7) / 8, 148 * 16);
+  sort_rows_padded_kernel<<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, stream>>>(
+      static_cast<const char*>(src), esz, src_ld, index, div, sorted_sel, offsets, pad_start, n_routes, cols,
+      static_cast<char*>(dst), vec);
+  return check_launch("sort_rows_padded");
 }
 
 // grad_w[e] = sum over the expert's partial slots in chunk order (split

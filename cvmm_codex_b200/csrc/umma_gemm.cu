@@ -201,6 +201,19 @@ __device__ __forceinline__ void store_row32(void* c, int c_dtype, int64_t off, c
     if (j < ncols) store_from_float(c, c_dtype, off + j, v[j]);
 }
 
+// Two 32-column TMEM loads behind one wait (halves the load-latency stalls).
+__device__ __forceinline__ void load_acc64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r0[32], r1[32];
+  ptx::tmem_ld_32x32b_x32(taddr, r0);
+  ptx::tmem_ld_32x32b_x32(taddr + 32, r1);
+  ptx::tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    v[j] = __uint_as_float(r0[j]);
+    v[32 + j] = __uint_as_float(r1[j]);
+  }
+}
+
 __device__ __forceinline__ void load_acc32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   ptx::tmem_ld_32x32b_x32(taddr, r);
@@ -365,6 +378,13 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
   auto entry = [&](int tt) -> int4 {
     return tt < total ? p.tiles[tt / n_n] : make_int4(0, 0, 0, 0);
   };
+  // A row (before a_div) of tile row rr: gathered index, or the row of the
+  // expert-padded sorted layout.
+  auto a_row_of = [&](const int4& en, int rr) -> int {
+    if (p.a_pad_start) return p.a_pad_start[en.x] + (int)(en.y - seg_begin(p.offsets, en.x)) + rr;
+    return (int)p.a_index[en.y + rr];
+  };
+  const bool a_dense = flags & 32;
 
   if (A_TMA && warp < 4) {
     // ------------------------------------------------------------ A rows by TMA gather4
@@ -375,7 +395,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int rr = 4 * lane + q;
-          r[q] = rr < en.z ? (int)idx_div(p.a_index[en.y + rr], p.a_div) : -1;
+          r[q] = rr < en.z ? (int)idx_div(a_row_of(en, rr), p.a_div) : -1;
         }
       };
       int4 ent = entry(blockIdx.x);
@@ -396,8 +416,12 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
           const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes);
           if (lane == 0) ptx::mbar_arrive_expect_tx(&bar.full[s], L::a_bytes);
           __syncwarp();
-          if (!CVMM_DBG(flags, 512))
+          if (a_dense) {
+            // Expert-padded sorted rows: the 128-row A tile is one dense box.
+            if (lane == 0) ptx::tma_load_2d(a_u, &tmap_a, &bar.full[s], kb * BK, rows[0]);
+          } else if (!CVMM_DBG(flags, 512)) {
             ptx::tma_gather4(a_u + lane * 512, &tmap_a, &bar.full[s], kb * BK, rows[0], rows[1], rows[2], rows[3]);
+          }
         }
         ent = ent_next;
         ent_next = ent_after;
@@ -420,7 +444,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int rr = (t >> 3) + 16 * i;
-      idx[i] = rr < ent.z ? (int)p.a_index[ent.y + rr] : -1;
+      idx[i] = rr < ent.z ? a_row_of(ent, rr) : -1;
     }
     int4 ent_next = entry(blockIdx.x + gridDim.x);
     uint32_t it = 0;
@@ -429,7 +453,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int rr = (t >> 3) + 16 * i;
-        idx_next[i] = rr < ent_next.z ? (int)p.a_index[ent_next.y + rr] : -1;
+        idx_next[i] = rr < ent_next.z ? a_row_of(ent_next, rr) : -1;
       }
       const int4 ent_after = entry(tt + 2 * gridDim.x);
       const int64_t e = ent.x;
@@ -505,25 +529,30 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
       const bool row_ok = crow >= 0;
       float wv = 0.f, dot = 0.f;
       if (p.mode == 1 && row_ok) wv = round_to(load_as_float(p.w, p.w_dtype, crow), op);
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        const int64_t nc = n0 + ch * 32;
-        if (nc >= p.N) break;
-        const int ncols = (int)imin64(32, p.N - nc);
-        float v[32];
-        load_acc32(tmem + ((uint32_t)(ew * 32) << 16) + a * BN + ch * 32, v);
-        if (nkb == 0) {
+      for (int ch = 0; ch < BN / 64; ++ch) {
+        if (n0 + ch * 64 >= p.N) break;
+        float v2[64];
+        load_acc64(tmem + ((uint32_t)(ew * 32) << 16) + a * BN + ch * 64, v2);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0.f;
-        }
-        if (p.mode == 1 && row_ok) {
+        for (int h = 0; h < 2; ++h) {
+          const int64_t nc = n0 + ch * 64 + h * 32;
+          if (nc >= p.N) break;
+          const int ncols = (int)imin64(32, p.N - nc);
+          float* v = v2 + 32 * h;
+          if (nkb == 0) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float av = round_to(v[j], op);
-            if (j < ncols) dot = fmaf(av, load_as_float(p.x, p.x_dtype, crow * p.x_ld + nc + j), dot);
-            v[j] = round_to(av * wv, op);
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
           }
+          if (p.mode == 1 && row_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float av = round_to(v[j], op);
+              if (j < ncols) dot = fmaf(av, load_as_float(p.x, p.x_dtype, crow * p.x_ld + nc + j), dot);
+              v[j] = round_to(av * wv, op);
+            }
+          }
+          warp_store_block(p.c, p.c_dtype, row_ok ? crow * p.c_ld + nc : -1, v, ncols, stage, c_vec);
         }
-        warp_store_block(p.c, p.c_dtype, row_ok ? crow * p.c_ld + nc : -1, v, ncols, stage, c_vec);
       }
       if (p.mode == 1 && row_ok) atomicAdd(p.gsel + crow, dot);
       ptx::tc_fence_before();
@@ -652,11 +681,14 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
     // 4 rows per gather4, into the MN-major swizzled stages (route = k row).
     uint32_t it = 0;
     bool aborted = false;
+    const bool g_dense = flags & 32;
     for (int tt = blockIdx.x; tt < total && !aborted; tt += gridDim.x) {
       const int4 u = entry(tt);
       const int rem = tt % per_unit;
       const int m0 = (rem / n_n) * BM, n0 = (rem % n_n) * BN;
       const int nkb = nkb_of(u);
+      const int g_pstart = g_dense ? p.g_pad_start[u.x] : 0;
+      const int64_t g_sbeg = g_dense ? seg_begin(p.offsets, u.x) : 0;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % S;
         if ((it >= S && !ptx::mbar_wait_or_abort(&bar.empty[s], ((it / S) - 1) & 1, kTagEmpty, bar.abort)) ||
@@ -669,6 +701,13 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
         const int64_t rb = u.y + (int64_t)kb * BK;
         const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes), b_u = a_u + L::a_bytes;
         if (lane == 0) ptx::mbar_arrive_expect_tx(&bar.full[s], L::a_bytes + L::b_bytes);
+        if (g_dense) {
+          // Expert-padded sorted grad rows: the stage's 64 route rows are one
+          // dense box per 64 columns. Units are whole multiples of 64 routes
+          // except an expert's last one, whose tail rows are padding zeros.
+          const int prow = g_pstart + (int)(rb - g_sbeg);
+          if (lane < BN / 64) ptx::tma_load_2d(b_u + lane * kAtomRowsBytes, &tmap_g, &bar.full[s], n0 + 64 * lane, prow);
+        }
         __syncwarp();
         {
           const int atom = lane >> 4, grp = lane & 15;
@@ -682,7 +721,7 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
                            r[1], r[2], r[3]);
         }
 #pragma unroll
-        for (int gi = lane; gi < BN / 4; gi += 32) {
+        for (int gi = lane; gi < (g_dense ? 0 : BN / 4); gi += 32) {
           const int atom = gi >> 4, grp = gi & 15;
           int r[4];
 #pragma unroll
@@ -824,17 +863,22 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
       const int64_t m = m0 + mr;
       float* dst = u.z < 0 ? p.out + e * p.M * p.N : p.partials + (int64_t)u.z * p.M * p.N;
       const bool empty_unit = nkb_of(u) == 0;
-      for (int ch = 0; ch < BN / 32; ++ch) {
-        const int64_t nc = n0 + ch * 32;
-        if (nc >= p.N) break;
-        const int ncols = (int)imin64(32, p.N - nc);
-        float v[32];
-        load_acc32(tmem + ((uint32_t)(ew * 32) << 16) + a * BN + ch * 32, v);
-        if (empty_unit) {
+      for (int ch = 0; ch < BN / 64; ++ch) {
+        if (n0 + ch * 64 >= p.N) break;
+        float v2[64];
+        load_acc64(tmem + ((uint32_t)(ew * 32) << 16) + a * BN + ch * 64, v2);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        for (int h = 0; h < 2; ++h) {
+          const int64_t nc = n0 + ch * 64 + h * 32;
+          if (nc >= p.N) break;
+          const int ncols = (int)imin64(32, p.N - nc);
+          float* v = v2 + 32 * h;
+          if (empty_unit) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          }
+          warp_store_block(dst, F32, m < p.M ? m * p.N + nc : -1, v, ncols, stage, o_vec);
         }
-        warp_store_block(dst, F32, m < p.M ? m * p.N + nc : -1, v, ncols, stage, o_vec);
       }
       ptx::tc_fence_before();
       ptx::mbar_arrive(&bar.acce[a]);
@@ -940,12 +984,13 @@ static bool make_b_map(CUtensorMap* map, const void* base, int dtype, int64_t co
 
 // 2-D TMA map over a row-major [rows, cols] operand for tile::gather4: a box
 // of 64 columns (128 bytes) by one row, 128-byte swizzle.
-static bool make_rows_map(CUtensorMap* map, const void* base, int dtype, int64_t cols, int64_t rows, int64_t ld) {
+static bool make_rows_map(CUtensorMap* map, const void* base, int dtype, int64_t cols, int64_t rows, int64_t ld,
+                          int box_rows = 1) {
   auto fn = encode_fn();
   if (!fn || !aligned16(base) || (ld * 2) % 16 != 0 || rows <= 0 || cols <= 0 || rows > INT32_MAX) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-  cuuint32_t box[2] = {64, 1};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, dtype == BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -967,8 +1012,13 @@ static int row_launch(const RowGemm& p, int64_t max_tiles, int flags, cudaStream
   if (dbg_flags() & 2048) tma = false;
   CUtensorMap amap;
   memset(&amap, 0, sizeof(amap));
-  const bool a_tma = tma && (flags & 1) && (dbg_flags() & 8192) &&
-                     make_rows_map(&amap, p.a, p.op_dtype, p.K, p.a_rows, p.a_ld);
+  // Dense A tiles (expert-padded sorted layout) always go through TMA; row
+  // gathers stay on cp.async, which measured faster than gather4 here.
+  const bool a_dense = tma && (flags & 1) && p.a_pad_start != nullptr &&
+                       make_rows_map(&amap, p.a, p.op_dtype, p.K, p.a_rows, p.a_ld, BM);
+  const bool a_tma = a_dense || (tma && (flags & 1) && (dbg_flags() & 8192) &&
+                                 make_rows_map(&amap, p.a, p.op_dtype, p.K, p.a_rows, p.a_ld));
+  if (a_dense) flags |= 32;
   const int64_t work = max_tiles * n_n;
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(work, sm_count()));
   if (a_tma) {
@@ -999,10 +1049,15 @@ static int seg_launch(const SegGemm& p, int64_t max_units, int flags, cudaStream
   CUtensorMap xmap, gmap;
   memset(&xmap, 0, sizeof(xmap));
   memset(&gmap, 0, sizeof(gmap));
-  // Gathered rows index at most n_routes rows of x and of the grad.
+  // Gathered rows index at most n_routes rows of x and of the grad; the
+  // expert-padded sorted grad has n_routes + 128 * n_experts rows and is read
+  // as dense 64-row boxes.
+  const bool g_dense = p.g_pad_start != nullptr;
+  const int64_t g_rows = g_dense ? p.n_routes + 128 * p.n_experts : p.n_routes;
   const bool gt = (flags & 3) == 3 && !(dbg_flags() & 4096) &&
                   make_rows_map(&xmap, p.x, p.op_dtype, p.M, p.n_routes, p.x_ld) &&
-                  make_rows_map(&gmap, p.g, p.op_dtype, p.N, p.n_routes, p.g_ld);
+                  make_rows_map(&gmap, p.g, p.op_dtype, p.N, g_rows, p.g_ld, g_dense ? 64 : 1);
+  if (gt && g_dense) flags |= 32;
   if (gt) {
     auto kern = seg_gemm_kernel<BN, S, W, true>;
     int rc = set_smem(kern, L::alloc);

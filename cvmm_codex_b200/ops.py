@@ -19,7 +19,7 @@ from ._lib import check, dtype_code, ptr
 KERNELS_PER_CALL = {
     "cvmm_sel_prepare": 10, "cvmm_expert_offsets": 1, "cvmm_forward": 2, "cvmm_backward_x": 2,
     "cvmm_backward_w": 3, "cvmm_weighted_combine": 1, "cvmm_sum_routes": 1,
-    "cvmm_weighted_token_backward": 1, "cvmm_cast": 1,
+    "cvmm_weighted_token_backward": 1, "cvmm_cast": 1, "cvmm_sort_rows_padded": 2,
 }
 
 
@@ -212,15 +212,16 @@ def sum_routes(src: torch.Tensor, top_k: int, out_dtype: torch.dtype) -> torch.T
     return out
 
 
-def backward_x(g: torch.Tensor, g_index: torch.Tensor, g_div: int, out_index: torch.Tensor,
+def backward_x(g: torch.Tensor, g_index: Optional[torch.Tensor], g_div: int, out_index: torch.Tensor,
                offsets: torch.Tensor, keys: torch.Tensor, out_dtype: torch.dtype,
                op_dtype: torch.dtype, w: Optional[torch.Tensor] = None,
-               x: Optional[torch.Tensor] = None):
+               x: Optional[torch.Tensor] = None, g_pad_start: Optional[torch.Tensor] = None):
     """Route gradients a_p = g[g_index[p] // g_div] @ keys[e_p]^T stored at out_index[p].
 
     Plain (w is None): returns out [R, d_in]. Weighted route-shaped input (w and x
     given): returns (grad_x [R, d_in], grad_sel fp32 [R]) with the reference's
-    fused rounding (cvmm.py:1073-1105)."""
+    fused rounding (cvmm.py:1073-1105). With g_pad_start, g is the expert-padded
+    sorted layout from sort_rows_padded and g_index is unused."""
     _require_cuda(g, g_index, out_index, offsets, keys, w, x)
     lib = _lib.load()
     g2 = _rows(g)
@@ -245,15 +246,16 @@ def backward_x(g: torch.Tensor, g_index: torch.Tensor, g_div: int, out_index: to
                                  ptr(w2), dtype_code(w2.dtype) if w2 is not None else 0,
                                  ptr(x2), dtype_code(x2.dtype) if x2 is not None else 0,
                                  x2.stride(0) if x2 is not None else 0, ptr(gsel),
-                                 dtype_code(op_dtype), ptr(ws), ws.numel(), stream)
+                                 dtype_code(op_dtype), ptr(g_pad_start), ptr(ws), ws.numel(), stream)
     check(rc, "cvmm_backward_x")
     return out if mode == 0 else (out, gsel)
 
 
 def backward_w(x: torch.Tensor, x_index: torch.Tensor, x_div: int, g: torch.Tensor,
-               g_index: torch.Tensor, g_div: int, offsets: torch.Tensor, n_experts: int,
+               g_index: Optional[torch.Tensor], g_div: int, offsets: torch.Tensor, n_experts: int,
                op_dtype: torch.dtype, w: Optional[torch.Tensor] = None,
-               w_index: Optional[torch.Tensor] = None) -> torch.Tensor:
+               w_index: Optional[torch.Tensor] = None,
+               g_pad_start: Optional[torch.Tensor] = None) -> torch.Tensor:
     """fp32 grad_keys[e] = sum_{p in seg e} x[x_index[p]//x_div]^T (w-scaled) g[g_index[p]//g_div]
     (reference grouped grad-W kernels, cvmm.py:424-604)."""
     _require_cuda(x, x_index, g, g_index, offsets, w, w_index)
@@ -270,9 +272,34 @@ def backward_w(x: torch.Tensor, x_index: torch.Tensor, x_div: int, g: torch.Tens
                                  ptr(g2), dtype_code(g2.dtype), g2.stride(0), ptr(g_index), int(g_div),
                                  ptr(w2), dtype_code(w2.dtype) if w2 is not None else 0, ptr(w_index),
                                  ptr(offsets), n_routes, int(n_experts), M, N, ptr(out),
-                                 dtype_code(op_dtype), ptr(ws), ws.numel(), stream)
+                                 dtype_code(op_dtype), ptr(g_pad_start), ptr(ws), ws.numel(), stream)
     check(rc, "cvmm_backward_w")
     return out
+
+
+PAD_ROWS = 128
+
+
+def sort_rows_padded(src: torch.Tensor, index: torch.Tensor, div: int, sorted_sel: torch.Tensor,
+                     offsets: torch.Tensor, n_experts: int, pad: int = PAD_ROWS):
+    """Expert-padded sorted copy of route rows (the reference's grouping copy,
+    cvmm.py:338-360): returns (dst [n_routes + n_experts*pad, cols], pad_start int32 [E])."""
+    _require_cuda(src, index, sorted_sel, offsets)
+    lib = _lib.load()
+    s2 = _rows(src)
+    n_routes = index.numel()
+    cols = s2.shape[1]
+    ss = sorted_sel.reshape(-1)
+    if ss.dtype != torch.int32:
+        ss = ss.to(torch.int32)
+    dst = torch.empty((n_routes + int(n_experts) * pad, cols), dtype=s2.dtype, device=s2.device)
+    pstart = torch.empty(int(n_experts), dtype=torch.int32, device=s2.device)
+    with _Device(s2.device) as stream:
+        rc = _invoke("cvmm_sort_rows_padded", lib.cvmm_sort_rows_padded, ptr(s2), dtype_code(s2.dtype), s2.stride(0),
+                     ptr(index), int(div), ptr(ss), ptr(offsets), n_routes, int(n_experts), cols, pad,
+                     ptr(dst), ptr(pstart), stream)
+    check(rc, "cvmm_sort_rows_padded")
+    return dst, pstart
 
 
 def weighted_token_backward(route_grad: torch.Tensor, w: torch.Tensor, x: torch.Tensor,

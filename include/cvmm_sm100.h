@@ -52,7 +52,7 @@ typedef struct CUstream_st* cvmm_stream_t; /* == cudaStream_t */
 #define CVMM_DEV_BAD_INDEX 2
 
 /* ABI version of this header; bumped on any signature change. */
-int cvmm_abi_version(void);
+int cvmm_abi_version(void);  /* 2 */
 
 /* Message for the last failed call on the calling host thread. */
 const char* cvmm_last_error(void);
@@ -142,6 +142,10 @@ int cvmm_weighted_combine(const void* y, int y_dtype, const void* w, int w_dtype
  * cvmm_weighted_route_bwd_x_kernel (cvmm.py:1008-1105, launcher 1386-1433).
  * For every sorted position p with expert e:
  *   a_p = op(g[g_index[p] / g_div]) . op(keys[e])^T          (fp32 acc)
+ * With g_pad_start != NULL, g is the expert-padded sorted layout made by
+ * cvmm_sort_rows_padded (pad 128): the g row of sorted position p is
+ * g_pad_start[e] + p - seg_begin(e) and g_index / g_div are ignored
+ * (bf16/fp16 op_dtype only).
  *   mode 0: out[out_index[p]] = cast_out(a_p)
  *   mode 1 (weighted, route-shaped x):
  *           out[out_index[p]]  = cast_out( op(op(a_p) * op(w[out_index[p]])) )
@@ -156,8 +160,8 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
                     int64_t k_dim, int64_t n_dim, int64_t ks_e, int64_t ks_k, int64_t ks_n,
                     void* out, int out_dtype, int64_t out_ld, int mode, const void* w,
                     int w_dtype, const void* x, int x_dtype, int64_t x_ld, float* gsel,
-                    int op_dtype, void* workspace, size_t workspace_bytes,
-                    cvmm_stream_t stream);
+                    int op_dtype, const int32_t* g_pad_start, void* workspace,
+                    size_t workspace_bytes, cvmm_stream_t stream);
 
 /* Backward grad-weight. Replaces cvmm_grouped_bwd_w_gather_x_kernel /
  * cvmm_grouped_bwd_w_kernel / cvmm_grouped_bwd_w_weighted_kernel
@@ -166,6 +170,9 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
  *   s_p = 1, or with w != NULL: the g row is first multiplied by op(w[w_index[p]])
  *   and rounded to op_dtype (cvmm.py:591-599).
  * grad_w: [n_experts, m_dim, n_dim] fp32, fully written (empty experts get 0).
+ * With g_pad_start != NULL, g is the expert-padded sorted layout of
+ * cvmm_sort_rows_padded (pad 128) and g_index / g_div are ignored (bf16/fp16
+ * op_dtype only).
  * Long expert segments are split over several CTAs (split-K); their partial
  * sums live in the workspace (cvmm_gemm_workspace_size with k_dim = m_dim)
  * and are added in a fixed order, so results are deterministic. */
@@ -174,8 +181,25 @@ int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_i
                     const int64_t* g_index, int64_t g_div, const void* w, int w_dtype,
                     const int64_t* w_index, const int64_t* offsets, int64_t n_routes,
                     int64_t n_experts, int64_t m_dim, int64_t n_dim, float* grad_w,
-                    int op_dtype, void* workspace, size_t workspace_bytes,
-                    cvmm_stream_t stream);
+                    int op_dtype, const int32_t* g_pad_start, void* workspace,
+                    size_t workspace_bytes, cvmm_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Expert-padded sorted copy of route rows. Replaces the reference's grouping
+ * copy cvmm_group_routes / cvmm_group_routes_kernel (cvmm.py:338-360,
+ * 1123-1138), with every expert's segment padded with zero rows to a multiple
+ * of `pad` rows:
+ *   dst[pad_start[e] + (p - seg_begin(e))] = src[index[p] / div]   for sorted p
+ * pad_start[e] (int32) = sum over e' < e of round_up(count(e'), pad); all other
+ * rows of dst are zero. dst needs n_routes + n_experts * pad rows of `cols`
+ * elements (leading dimension cols). Passing dst and pad_start with pad = 128 as
+ * `g` / `g_pad_start` to cvmm_backward_x / cvmm_backward_w lets their
+ * tensor-core paths read the gradient as dense tiles instead of gathering rows.
+ * ------------------------------------------------------------------------ */
+int cvmm_sort_rows_padded(const void* src, int dtype, int64_t src_ld, const int64_t* index,
+                          int64_t div, const int32_t* sorted_sel, const int64_t* offsets,
+                          int64_t n_routes, int64_t n_experts, int64_t cols, int64_t pad,
+                          void* dst, int32_t* pad_start, cvmm_stream_t stream);
 
 /* Sum over the top-k routes of each token: out[t] = cast( sum_j src[t*top_k+j] ),
  * fp32 accumulate. Replaces grouped_x.view(..., top_k, d).sum(-2) (cvmm.py:1223). */

@@ -106,3 +106,25 @@ def test_cuda_default_sort_agreement_report(capsys):
         b = fsel.sort(stable=True).indices
         rows.append((R, E, bool(torch.equal(a, b))))
     print("cuda default sort == stable:", rows)
+
+
+def test_sort_rows_padded_matches_oracle():
+    """Expert-padded sorted copy of route rows (the grouping copy of cvmm.py:338-360)."""
+    g = torch.Generator().manual_seed(21)
+    R, E, cols, pad = 3000, 11, 136, 128
+    sel = torch.randint(0, E, (R // 3, 3), generator=g)
+    sel[:, 0] = 4  # a long segment
+    src = torch.randn(R, cols, generator=g).bfloat16()
+    s = C.cvmm_prepare_sel2(sel.cuda(), route_input=True)
+    offs = ops.expert_offsets(s.sel, E)
+    dst, pstart = ops.sort_rows_padded(src.cuda(), s.sel_index, 1, s.sel, offs, E, pad)
+    _, ssel, idx, _ = O.prepare_sel2(sel.numpy(), route_input=True)
+    counts = np.bincount(ssel, minlength=E)
+    want_ps = np.concatenate([[0], np.cumsum((counts + pad - 1) // pad * pad)[:-1]]).astype(np.int32)
+    np.testing.assert_array_equal(pstart.cpu().numpy(), want_ps)
+    want = np.zeros((R + E * pad, cols), dtype=np.float32)
+    seg = np.concatenate([[0], np.cumsum(counts)[:-1]])
+    for p_ in range(R):
+        e = ssel[p_]
+        want[want_ps[e] + p_ - seg[e]] = src[idx[p_]].float().numpy()
+    np.testing.assert_array_equal(dst.float().cpu().numpy(), want)
