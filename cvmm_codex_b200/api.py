@@ -111,6 +111,11 @@ cvmm_lowmem_min_top_k = int(os.environ.get("CVMM_LOWMEM_MIN_TOP_K", "32"))
 cvmm_lowmem_chunk_size = int(os.environ.get("CVMM_LOWMEM_CHUNK_SIZE", "0"))
 cvmm_force_gather_x_grad_w = os.environ.get("CVMM_GATHER_X_GRAD_W", "0").lower() in ("1", "true", "yes", "on")
 cvmm_gather_x_grad_w_max_top_k = int(os.environ.get("CVMM_GATHER_X_GRAD_W_MAX_TOP_K", "8"))
+# sm_100a engine knob (no reference counterpart): copy the GEMM operands into
+# the expert-padded sorted layout so the tensor-core kernels read dense tiles.
+# Costs one extra [n_routes + 128 * n_experts, d_in] op-dtype copy of x kept
+# for the backward.
+cvmm_sorted_operands = os.environ.get("CVMM_B200_SORTED_OPERANDS", "1").lower() not in ("0", "false", "no", "off")
 
 
 def create_kernels():
@@ -159,6 +164,13 @@ def _operand(keys: torch.Tensor, op_dtype: torch.dtype) -> torch.Tensor:
     return ops.cast(keys, op_dtype)
 
 
+def _sortable(t: torch.Tensor, op_dtype: torch.dtype) -> bool:
+    """Whether rows of `t` can be copied into the expert-padded sorted layout
+    that the tensor-core kernels read as dense 16-byte-aligned TMA tiles."""
+    return (cvmm_sorted_operands and op_dtype in (torch.bfloat16, torch.float16) and t.is_floating_point()
+            and t.shape[-1] % 8 == 0)
+
+
 class CVMM(torch.autograd.Function):
     """Autograd function with the reference's signature (cvmm.py:1521-1755)."""
 
@@ -172,13 +184,21 @@ class CVMM(torch.autograd.Function):
         n_experts = keys.shape[0]
         offsets = ops.expert_offsets(sel, n_experts)
         keys_op = _operand(keys, op_dtype)
-        res = ops.forward(x, sel_index, offsets, keys_op, out_index, op_dtype, op_dtype)
+        xs = xpad = None
+        if _sortable(x, op_dtype):
+            # Expert-sorted, 128-row padded op-dtype copy of the route rows of x:
+            # the forward and the grad-W read it as dense tiles (the reference's
+            # grouped-x copy, cvmm.py:1123-1138).
+            xs, xpad = ops.sort_rows_padded(x, sel_index, 1, sel, offsets, n_experts, dtype=op_dtype)
+            res = ops.forward(xs, sel_index, offsets, keys_op, out_index, op_dtype, op_dtype, x_pad_start=xpad)
+        else:
+            res = ops.forward(x, sel_index, offsets, keys_op, out_index, op_dtype, op_dtype)
         if reduction_weight is not None:
             res = ops.weighted_combine(res, reduction_weight, op_dtype)
             res = res.view(*reduction_weight.shape[:-1], res.shape[-1])
         else:
             res = res.view(*sel.shape, res.shape[-1])
-        ctx.save_for_backward(x, keys_op, raw_sel, sel, sel_index, out_index, reduction_weight, offsets)
+        ctx.save_for_backward(x, keys_op, raw_sel, sel, sel_index, out_index, reduction_weight, offsets, xs, xpad)
         ctx.op_type = op_dtype
         ctx.keys_type = keys.dtype
         ctx.dtype = op_dtype
@@ -186,7 +206,7 @@ class CVMM(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_output):
-        x, keys_op, raw_sel, sel, sel_index, out_index, w, offsets = ctx.saved_tensors
+        x, keys_op, raw_sel, sel, sel_index, out_index, w, offsets, xs, xpad = ctx.saved_tensors
         need_x = ctx.needs_input_grad[0]
         need_keys = ctx.needs_input_grad[4]
         need_w = len(ctx.needs_input_grad) > 6 and ctx.needs_input_grad[6] and w is not None
@@ -205,16 +225,20 @@ class CVMM(torch.autograd.Function):
         if w is None:
             g2 = g.reshape(n_routes, g.shape[-1])
             g_rows, g_idx, g_pad = g2, route, None
-            if op != torch.float32 and g2.dtype == op:
+            if _sortable(g2, op):
                 # One expert-padded sorted copy of the route grads (the
                 # reference's grouping copy, cvmm.py:1161) lets both GEMMs read
                 # them as dense tensor-core tiles.
-                g_rows, g_pad = ops.sort_rows_padded(g2, route, 1, sel, offsets, n_experts)
+                g_rows, g_pad = ops.sort_rows_padded(g2, route, 1, sel, offsets, n_experts, dtype=op)
                 g_idx = None
             if need_keys:
                 # dW_e = sum_p x[sel_index[p]]^T g[route[p]]  (cvmm.py:1163-1198)
-                grad_keys = ops.backward_w(x, sel_index, 1, g_rows, g_idx, 1, offsets, n_experts, op,
-                                           g_pad_start=g_pad)
+                if xs is not None:
+                    grad_keys = ops.backward_w(xs, None, 1, g_rows, g_idx, 1, offsets, n_experts, op,
+                                               g_pad_start=g_pad, x_pad_start=xpad, n_routes=n_routes)
+                else:
+                    grad_keys = ops.backward_w(x, sel_index, 1, g_rows, g_idx, 1, offsets, n_experts, op,
+                                               g_pad_start=g_pad)
             if need_x:
                 # gx_route[route] = g[route] W_e^T, then summed over k (cvmm.py:1199-1223)
                 gxr = ops.backward_x(g_rows, g_idx, 1, route, offsets, keys_op, x.dtype, op, g_pad_start=g_pad)
@@ -227,8 +251,15 @@ class CVMM(torch.autograd.Function):
             gt = g.reshape(-1, g.shape[-1])  # token grads of the combined output
             if need_keys:
                 # dW_e = sum_p x[sel_index[p]]^T (bf16(w_p) * g[route_p // k])  (cvmm.py:1341-1383)
-                grad_keys = ops.backward_w(x, sel_index, 1, gt, route, k, offsets, n_experts, op,
-                                           w=w, w_index=route)
+                if xs is not None and _sortable(gt, op):
+                    # The weight product is applied (and rounded) in the sorted copy.
+                    gs, gpad = ops.sort_rows_padded(gt, route, k, sel, offsets, n_experts, dtype=op, scale=w)
+                    grad_keys = ops.backward_w(xs, None, 1, gs, None, 1, offsets, n_experts, op,
+                                               g_pad_start=gpad, x_pad_start=xpad, n_routes=n_routes)
+                    del gs
+                else:
+                    grad_keys = ops.backward_w(x, sel_index, 1, gt, route, k, offsets, n_experts, op,
+                                               w=w, w_index=route)
             if need_x or need_w:
                 if out_index is None and tuple(x.shape[:-1]) == tuple(w.shape):
                     # Route-shaped input: fused grad-x + sel-weight grad (cvmm.py:1386-1433)

@@ -212,7 +212,7 @@ using namespace cvmm;
 // ================================================================== C ABI
 extern "C" {
 
-int cvmm_abi_version(void) { return 2; }
+int cvmm_abi_version(void) { return 3; }
 
 const char* cvmm_last_error(void) { return t_err; }
 
@@ -265,10 +265,13 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld, const
                  const int64_t* out_index, const int64_t* offsets, int64_t n_routes,
                  const void* keys, int keys_dtype, int64_t n_experts, int64_t k_dim, int64_t n_dim,
                  int64_t ks_e, int64_t ks_k, int64_t ks_n, void* out, int out_dtype, int64_t out_ld,
-                 int op_dtype, void* workspace, size_t workspace_bytes, cvmm_stream_t stream) {
+                 int op_dtype, const int32_t* x_pad_start, void* workspace, size_t workspace_bytes,
+                 cvmm_stream_t stream) {
   if (!is_float_dtype(x_dtype) || !is_float_dtype(keys_dtype) || !is_float_dtype(out_dtype) ||
       !is_float_dtype(op_dtype))
     return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_forward: unsupported dtype");
+  if (x_pad_start && (op_dtype == F32 || x_dtype != op_dtype))
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: the padded sorted layout needs x_dtype == op_dtype (bf16/fp16)");
   if (n_routes < 0 || n_experts <= 0 || k_dim < 0 || n_dim <= 0 || x_rows < 0 || x_ld < k_dim ||
       out_ld < n_dim)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: bad sizes");
@@ -278,7 +281,8 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld, const
   if (!x || !sel_index || !offsets || !keys || !out)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: null pointer");
   RowGemm p = {};
-  p.a = x; p.a_dtype = x_dtype; p.a_ld = x_ld; p.a_rows = x_rows; p.a_index = sel_index; p.a_div = 1;
+  p.a = x; p.a_dtype = x_dtype; p.a_ld = x_ld; p.a_rows = x_pad_start ? n_routes + n_experts * kPadRows : x_rows;
+  p.a_index = sel_index; p.a_div = 1; p.a_pad_start = x_pad_start;
   p.b = keys; p.b_dtype = keys_dtype; p.bs_e = ks_e; p.bs_k = ks_k; p.bs_n = ks_n;
   p.c = out; p.c_dtype = out_dtype; p.c_ld = out_ld; p.c_index = out_index ? out_index : sel_index;
   p.offsets = offsets; p.n_routes = n_routes; p.n_experts = n_experts; p.K = k_dim; p.N = n_dim;
@@ -332,7 +336,7 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: mode 1 needs w, x and gsel");
   RowGemm p = {};
   // B_e[kk][nn] = keys[e][nn][kk]: contract over n_dim, produce k_dim columns.
-  p.a = g; p.a_dtype = g_dtype; p.a_ld = g_ld; p.a_rows = g_pad_start ? n_routes + n_experts * 128 : n_routes;
+  p.a = g; p.a_dtype = g_dtype; p.a_ld = g_ld; p.a_rows = g_pad_start ? n_routes + n_experts * kPadRows : n_routes;
   p.a_index = g_index; p.a_div = g_pad_start ? 1 : g_div;
   p.b = keys; p.b_dtype = keys_dtype; p.bs_e = ks_e; p.bs_k = ks_n; p.bs_n = ks_k;
   p.c = out; p.c_dtype = out_dtype; p.c_ld = out_ld; p.c_index = out_index;
@@ -346,19 +350,21 @@ int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_i
                     const void* g, int g_dtype, int64_t g_ld, const int64_t* g_index, int64_t g_div,
                     const void* w, int w_dtype, const int64_t* w_index, const int64_t* offsets,
                     int64_t n_routes, int64_t n_experts, int64_t m_dim, int64_t n_dim, float* grad_w,
-                    int op_dtype, const int32_t* g_pad_start, void* workspace, size_t workspace_bytes,
-                    cvmm_stream_t stream) {
+                    int op_dtype, const int32_t* x_pad_start, const int32_t* g_pad_start, void* workspace,
+                    size_t workspace_bytes, cvmm_stream_t stream) {
   if (!is_float_dtype(x_dtype) || !is_float_dtype(g_dtype) || !is_float_dtype(op_dtype) ||
       (w && !is_float_dtype(w_dtype)))
     return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_backward_w: unsupported dtype");
   if (n_routes < 0 || n_experts <= 0 || m_dim <= 0 || n_dim <= 0 || x_div <= 0 || g_div <= 0 ||
       x_ld < m_dim || g_ld < n_dim || n_routes > (int64_t)INT32_MAX)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: bad sizes");
-  if (!grad_w || !offsets || (n_routes > 0 && (!x || !g || !x_index || (!g_index && !g_pad_start))) ||
+  if (!grad_w || !offsets || (n_routes > 0 && (!x || !g || (!x_index && !x_pad_start) || (!g_index && !g_pad_start))) ||
       (w && !w_index))
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: null pointer");
-  if (g_pad_start && op_dtype == F32)
-    return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: the padded sorted gradient layout needs bf16/fp16 op_dtype");
+  if ((g_pad_start && (op_dtype == F32 || g_dtype != op_dtype)) || (x_pad_start && (op_dtype == F32 || x_dtype != op_dtype)))
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: padded sorted operands need operand dtype == op_dtype (bf16/fp16)");
+  if (g_pad_start && w)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: a padded g carries the route weights; pass w = NULL");
   if (n_experts > 65535) return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: too many experts");
   const bool tensor = op_dtype != F32;
   GemmWs ws;
@@ -371,14 +377,16 @@ int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_i
   p.g = g; p.g_dtype = g_dtype; p.g_ld = g_ld; p.g_index = g_index; p.g_div = g_div;
   p.w = w; p.w_dtype = w_dtype; p.w_index = w_index;
   p.offsets = offsets; p.n_routes = n_routes; p.n_experts = n_experts; p.M = m_dim; p.N = n_dim;
-  p.out = grad_w; p.op_dtype = op_dtype; p.g_pad_start = g_pad_start;
+  p.out = grad_w; p.op_dtype = op_dtype; p.x_pad_start = x_pad_start; p.g_pad_start = g_pad_start;
   p.chunk = segw_chunk(n_routes, n_experts, m_dim, n_dim, tensor);
   p.units = static_cast<int4*>(ws.tiles);
   p.n_units = ws.count;
   p.partials = ws.partials;
   rc = build_units(offsets, n_experts, p.chunk, static_cast<int4*>(ws.tiles), ws.count, ws.expert_slots, s);
   if (rc) return rc;
-  if (tensor && n_routes > 0) {
+  // Both operands padded: the GEMM derives every row from its unit and needs
+  // no resolved route rows.
+  if (tensor && n_routes > 0 && !(x_pad_start && g_pad_start)) {
     char* rr = reinterpret_cast<char*>(ws.partials) +
                align_up((size_t)segw_max_slots(n_routes, p.chunk) * m_dim * n_dim * sizeof(float), 256);
     const size_t arr = align_up((size_t)(n_routes + kRouteRowsPad) * 4, 256);
@@ -401,22 +409,22 @@ int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_i
   return seg_reduce(ws.expert_slots, ws.partials, grad_w, n_experts, m_dim * n_dim, s);
 }
 
-int cvmm_sort_rows_padded(const void* src, int dtype, int64_t src_ld, const int64_t* index, int64_t div,
-                          const int32_t* sorted_sel, const int64_t* offsets, int64_t n_routes, int64_t n_experts,
-                          int64_t cols, int64_t pad, void* dst, int32_t* pad_start, cvmm_stream_t stream) {
-  if (!is_float_dtype(dtype)) return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_sort_rows_padded: unsupported dtype");
-  if (n_routes < 0 || n_experts <= 0 || cols <= 0 || pad <= 0 || div <= 0 || src_ld < cols ||
-      n_routes + n_experts * pad > (int64_t)INT32_MAX)
+int cvmm_sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64_t* index, int64_t div,
+                          const void* scale, int scale_dtype, const int32_t* sorted_sel, const int64_t* offsets,
+                          int64_t n_routes, int64_t n_experts, int64_t cols, void* dst, int dst_dtype,
+                          int32_t* pad_start, cvmm_stream_t stream) {
+  if (!is_float_dtype(src_dtype) || !is_float_dtype(dst_dtype) || (scale && !is_float_dtype(scale_dtype)))
+    return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_sort_rows_padded: unsupported dtype");
+  if (n_routes < 0 || n_experts <= 0 || cols <= 0 || div <= 0 || src_ld < cols ||
+      n_routes + n_experts * kPadRows > (int64_t)INT32_MAX)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_sort_rows_padded: bad sizes");
   if (!dst || !pad_start || !offsets || (n_routes > 0 && (!src || !index || !sorted_sel)))
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_sort_rows_padded: null pointer");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(dst, 0, (size_t)(n_routes + n_experts * pad) * cols * dtype_size(dtype), s) != cudaSuccess)
-    return fail_cuda("cvmm_sort_rows_padded: memset");
-  int rc = pad_starts(offsets, n_experts, pad, reinterpret_cast<int*>(pad_start), s);
+  int rc = pad_starts(offsets, n_experts, kPadRows, reinterpret_cast<int*>(pad_start), s);
   if (rc || n_routes == 0) return rc;
-  return sort_rows_padded(src, dtype, src_ld, index, div, sorted_sel, offsets, reinterpret_cast<int*>(pad_start),
-                          n_routes, cols, dst, s);
+  return sort_rows_padded(src, src_dtype, src_ld, index, div, scale, scale_dtype, sorted_sel, offsets,
+                          reinterpret_cast<int*>(pad_start), n_routes, n_experts, cols, dst, dst_dtype, s);
 }
 
 int cvmm_weighted_token_backward(const void* route_grad, int rg_dtype, const void* w, int w_dtype,

@@ -50,6 +50,7 @@ struct SegGemm {
   // Per sorted route, resolved before the GEMM (tensor-core path): x row,
   // grad row (int32) and op-rounded route weight (fp32); padded by
   // kRouteRowsPad entries so 16-byte-aligned bulk copies may run past the end.
+  const int* x_pad_start;  // non-null: x is the expert-padded sorted layout
   const int* g_pad_start;  // non-null: g is the expert-padded sorted layout
   const int* xrow;
   const int* grow;
@@ -57,10 +58,13 @@ struct SegGemm {
 };
 
 constexpr int64_t kRouteRowsPad = 128;
+// Rows each expert segment of the expert-padded sorted layout is padded to.
+constexpr int64_t kPadRows = CVMM_PAD_ROWS;
 int pad_starts(const int64_t* offsets, int64_t n_experts, int64_t pad, int* pad_start, cudaStream_t stream);
-int sort_rows_padded(const void* src, int dtype, int64_t src_ld, const int64_t* index, int64_t div,
-                     const int32_t* sorted_sel, const int64_t* offsets, const int* pad_start, int64_t n_routes,
-                     int64_t cols, void* dst, cudaStream_t stream);
+int sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64_t* index, int64_t div,
+                     const void* scale, int scale_dtype, const int32_t* sorted_sel, const int64_t* offsets,
+                     const int* pad_start, int64_t n_routes, int64_t n_experts, int64_t cols, void* dst,
+                     int dst_dtype, cudaStream_t stream);
 int resolve_route_rows(const SegGemm& p, int* xrow, int* grow, float* wsc, cudaStream_t stream);
 
 __device__ __forceinline__ int64_t seg_begin(const int64_t* offsets, int64_t e) {

@@ -123,17 +123,19 @@ __global__ void resolve_route_rows_kernel(SegGemm p, int* __restrict__ xrow, int
                                           float* __restrict__ wsc, int64_t padded) {
   for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < padded; r += (int64_t)gridDim.x * blockDim.x) {
     const bool ok = r < p.n_routes;
-    xrow[r] = ok ? (int)idx_div(p.x_index[r], p.x_div) : -1;
-    if (p.g_pad_start) {
-      int64_t lo = 0, hi = p.n_experts - 1;  // expert of sorted position r: first e with offsets[e] > r
+    int64_t lo = 0;  // expert of sorted position r (padded layouts): first e with offsets[e] > r
+    if (p.x_pad_start || p.g_pad_start) {
+      int64_t hi = p.n_experts - 1;
       while (ok && lo < hi) {
         const int64_t mid = (lo + hi) >> 1;
         if (p.offsets[mid] > r) hi = mid; else lo = mid + 1;
       }
-      grow[r] = ok ? (int)(p.g_pad_start[lo] + r - seg_begin(p.offsets, lo)) : -1;
-    } else {
-      grow[r] = ok ? (int)idx_div(p.g_index[r], p.g_div) : -1;
     }
+    const int padded_row = ok ? (int)(r - seg_begin(p.offsets, lo)) : 0;
+    if (p.x_pad_start) xrow[r] = ok ? p.x_pad_start[lo] + padded_row : -1;
+    else xrow[r] = ok ? (int)idx_div(p.x_index[r], p.x_div) : -1;
+    if (p.g_pad_start) grow[r] = ok ? p.g_pad_start[lo] + padded_row : -1;
+    else grow[r] = ok ? (int)idx_div(p.g_index[r], p.g_div) : -1;
     if (p.w) wsc[r] = ok ? round_to(load_as_float(p.w, p.w_dtype, p.w_index[r]), p.op_dtype) : 0.f;
   }
 }
@@ -166,39 +168,109 @@ int pad_starts(const int64_t* offsets, int64_t n_experts, int64_t pad, int* pad_
   return check_launch("pad_starts");
 }
 
-// One warp per sorted route row: dst[pad_start[e] + p - seg_begin(e)] = src[index[p] / div].
-__global__ void sort_rows_padded_kernel(const char* __restrict__ src, int esz, int64_t src_ld,
-                                        const int64_t* __restrict__ index, int64_t div,
-                                        const int32_t* __restrict__ sorted_sel, const int64_t* __restrict__ offsets,
-                                        const int* __restrict__ pad_start, int64_t n_routes, int64_t cols,
-                                        char* __restrict__ dst, bool vec) {
+// Eight consecutive elements as fp32 (16-byte aligned source).
+__device__ __forceinline__ void load8(const char* from, int dtype, float (&v)[8]) {
+  if (dtype == F32) {
+    const float4 a = reinterpret_cast<const float4*>(from)[0], b = reinterpret_cast<const float4*>(from)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    return;
+  }
+  const uint4 q = *reinterpret_cast<const uint4*>(from);
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = bits_to_float((uint16_t)(w[i] & 0xffffu), dtype);
+    v[2 * i + 1] = bits_to_float((uint16_t)(w[i] >> 16), dtype);
+  }
+}
+
+__device__ __forceinline__ void store8(char* to, int dtype, const float (&v)[8]) {
+  if (dtype == F32) {
+    reinterpret_cast<float4*>(to)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(to)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    return;
+  }
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    w[i] = (uint32_t)float_to_bits(v[2 * i], dtype) | ((uint32_t)float_to_bits(v[2 * i + 1], dtype) << 16);
+  *reinterpret_cast<uint4*>(to) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// One warp per row of the expert-padded sorted copy. Virtual rows
+// [0, n_routes) are the sorted routes: dst[pad_start[e] + p - seg_begin(e)] =
+// op(src[index[p] / div]) (times op(scale[index[p]]), rounded again); rows
+// [n_routes, n_routes + n_experts * kPadRows) enumerate every expert's
+// candidate padding rows, and those inside the expert's padded segment are
+// zeroed. mode 0: byte copy (same dtype, no scale), 1: 8-element vectors with
+// conversion, 2: scalar elements.
+__global__ void sort_rows_padded_kernel(const char* __restrict__ src, int src_dtype, int64_t src_ld,
+                                        const int64_t* __restrict__ index, int64_t div, const void* __restrict__ scale,
+                                        int scale_dtype, const int32_t* __restrict__ sorted_sel,
+                                        const int64_t* __restrict__ offsets, const int* __restrict__ pad_start,
+                                        int64_t n_routes, int64_t n_experts, int64_t cols, char* __restrict__ dst,
+                                        int dst_dtype, int mode) {
   const int lane = threadIdx.x & 31;
+  const int ssz = dtype_bytes(src_dtype), dsz = dtype_bytes(dst_dtype);
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t p = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); p < n_routes; p += warps) {
-    const int64_t e = sorted_sel[p];
-    const int64_t q = pad_start[e] + p - seg_begin(offsets, e);
-    const char* from = src + idx_div(index[p], div) * src_ld * esz;
-    char* to = dst + q * cols * esz;
-    const int64_t bytes = cols * esz;
-    if (vec) {
-      for (int64_t b = lane * 16; b < bytes; b += 32 * 16)
+  const int64_t total = n_routes + n_experts * kPadRows;
+  for (int64_t v = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); v < total; v += warps) {
+    if (v >= n_routes) {
+      const int64_t e = (v - n_routes) / kPadRows, i = (v - n_routes) % kPadRows;
+      const int64_t cnt = offsets[e] - seg_begin(offsets, e);
+      if (cnt + i >= (cnt + kPadRows - 1) / kPadRows * kPadRows) continue;
+      char* to = dst + (pad_start[e] + cnt + i) * cols * dsz;
+      const int64_t bytes = cols * dsz;
+      if (mode != 2) {
+        for (int64_t b = lane * 16; b < bytes; b += 32 * 16) *reinterpret_cast<uint4*>(to + b) = make_uint4(0, 0, 0, 0);
+      } else {
+        for (int64_t b = lane; b < bytes; b += 32) to[b] = 0;
+      }
+      continue;
+    }
+    const int64_t e = sorted_sel[v];
+    const int64_t q = pad_start[e] + v - seg_begin(offsets, e);
+    const int64_t r = index[v];
+    const char* from = src + idx_div(r, div) * src_ld * ssz;
+    char* to = dst + q * cols * dsz;
+    const float sc = scale ? round_to(load_as_float(scale, scale_dtype, r), dst_dtype) : 1.f;
+    if (mode == 0) {
+      for (int64_t b = lane * 16; b < cols * dsz; b += 32 * 16)
         *reinterpret_cast<uint4*>(to + b) = *reinterpret_cast<const uint4*>(from + b);
+    } else if (mode == 1) {
+      for (int64_t c = lane * 8; c < cols; c += 32 * 8) {
+        float x[8];
+        load8(from + c * ssz, src_dtype, x);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          x[j] = round_to(x[j], dst_dtype);
+          if (scale) x[j] = x[j] * sc;
+        }
+        store8(to + c * dsz, dst_dtype, x);
+      }
     } else {
-      for (int64_t b = lane; b < bytes; b += 32) to[b] = from[b];
+      for (int64_t c = lane; c < cols; c += 32) {
+        float x = round_to(load_as_float(from, src_dtype, c), dst_dtype);
+        if (scale) x = x * sc;
+        store_from_float(to, dst_dtype, c, x);
+      }
     }
   }
 }
 
-int sort_rows_padded(const void* src, int dtype, int64_t src_ld, const int64_t* index, int64_t div,
-                     const int32_t* sorted_sel, const int64_t* offsets, const int* pad_start, int64_t n_routes,
-                     int64_t cols, void* dst, cudaStream_t stream) {
-  const int esz = dtype_bytes(dtype);
-  const bool vec = ((cols * esz) % 16 == 0) && ((src_ld * esz) % 16 == 0) && (((uintptr_t)src & 15u) == 0) &&
-                   (((uintptr_t)dst & 15u) == 0);
-  const int64_t blocks = std::min<int64_t>((n_routes + 7) / 8, 148 * 16);
+int sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64_t* index, int64_t div,
+                     const void* scale, int scale_dtype, const int32_t* sorted_sel, const int64_t* offsets,
+                     const int* pad_start, int64_t n_routes, int64_t n_experts, int64_t cols, void* dst,
+                     int dst_dtype, cudaStream_t stream) {
+  const int ssz = dtype_bytes(src_dtype), dsz = dtype_bytes(dst_dtype);
+  const bool aligned = ((cols * ssz) % 16 == 0) && ((src_ld * ssz) % 16 == 0) && ((cols * dsz) % 16 == 0) &&
+                       (((uintptr_t)src & 15u) == 0) && (((uintptr_t)dst & 15u) == 0) && cols % 8 == 0;
+  const int mode = !aligned ? 2 : (src_dtype == dst_dtype && scale == nullptr ? 0 : 1);
+  const int64_t rows = n_routes + n_experts * kPadRows;
+  const int64_t blocks = std::min<int64_t>((rows + 7) / 8, 148 * 16);
   sort_rows_padded_kernel<<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, stream>>>(
-      static_cast<const char*>(src), esz, src_ld, index, div, sorted_sel, offsets, pad_start, n_routes, cols,
-      static_cast<char*>(dst), vec);
+      static_cast<const char*>(src), src_dtype, src_ld, index, div, scale, scale_dtype, sorted_sel, offsets, pad_start,
+      n_routes, n_experts, cols, static_cast<char*>(dst), dst_dtype, mode);
   return check_launch("sort_rows_padded");
 }
 

@@ -49,7 +49,8 @@ constexpr int kThreads = 320;
 constexpr uint32_t kAtomRowsBytes = 64 * 128;  // one 64-row x 128-byte MN-major atom column
 
 // Development-only knobs (compiled in with -DCVMM_TRACE; absent from the
-// shipped library): bit 8 skips the MMAs, bit 9 / bit 10 skip the A / B loads.
+// shipped library): bit 8 skips the MMAs, bit 9 / bit 10 skip the A / B loads,
+// bit 14 skips the grad-W epilogue stores.
 #ifdef CVMM_TRACE
 #define CVMM_DBG(flags, bit) (((flags) & (bit)) != 0)
 #else
@@ -681,35 +682,46 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
     // 4 rows per gather4, into the MN-major swizzled stages (route = k row).
     uint32_t it = 0;
     bool aborted = false;
-    const bool g_dense = flags & 32;
+    const bool g_dense = flags & 32, x_dense = flags & 64, ring_on = !(g_dense && x_dense);
     for (int tt = blockIdx.x; tt < total && !aborted; tt += gridDim.x) {
       const int4 u = entry(tt);
       const int rem = tt % per_unit;
       const int m0 = (rem / n_n) * BM, n0 = (rem % n_n) * BN;
       const int nkb = nkb_of(u);
+      const int64_t sbeg = (g_dense || x_dense) ? seg_begin(p.offsets, u.x) : 0;
       const int g_pstart = g_dense ? p.g_pad_start[u.x] : 0;
-      const int64_t g_sbeg = g_dense ? seg_begin(p.offsets, u.x) : 0;
+      const int x_pstart = x_dense ? p.x_pad_start[u.x] : 0;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % S;
         if ((it >= S && !ptx::mbar_wait_or_abort(&bar.empty[s], ((it / S) - 1) & 1, kTagEmpty, bar.abort)) ||
-            !ptx::mbar_wait_or_abort(&bar.idxf[s], (it / S) & 1, kTagFull, bar.abort)) {
+            (ring_on && !ptx::mbar_wait_or_abort(&bar.idxf[s], (it / S) & 1, kTagFull, bar.abort))) {
           aborted = true;
           break;
         }
         const IdxSlot& slot = ring[s];
-        const int off = slot.off;
+        const int off = ring_on ? slot.off : 0;
         const int64_t rb = u.y + (int64_t)kb * BK;
         const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes), b_u = a_u + L::a_bytes;
-        if (lane == 0) ptx::mbar_arrive_expect_tx(&bar.full[s], L::a_bytes + L::b_bytes);
-        if (g_dense) {
+        const bool skip_x = CVMM_DBG(flags, 512), skip_g = CVMM_DBG(flags, 1024);
+        if (lane == 0) {
+          const uint32_t tx = (skip_x ? 0u : L::a_bytes) + (skip_g ? 0u : L::b_bytes);
+          if (tx) ptx::mbar_arrive_expect_tx(&bar.full[s], tx);
+          else ptx::mbar_arrive(&bar.full[s]);
+        }
+        if (g_dense && !skip_g) {
           // Expert-padded sorted grad rows: the stage's 64 route rows are one
           // dense box per 64 columns. Units are whole multiples of 64 routes
           // except an expert's last one, whose tail rows are padding zeros.
-          const int prow = g_pstart + (int)(rb - g_sbeg);
+          const int prow = g_pstart + (int)(rb - sbeg);
           if (lane < BN / 64) ptx::tma_load_2d(b_u + lane * kAtomRowsBytes, &tmap_g, &bar.full[s], n0 + 64 * lane, prow);
         }
+        if (x_dense && !skip_x) {
+          // Expert-padded sorted x rows: one dense 64-row box per 64 m columns.
+          const int prow = x_pstart + (int)(rb - sbeg);
+          if (lane < BM / 64) ptx::tma_load_2d(a_u + lane * kAtomRowsBytes, &tmap_x, &bar.full[s], m0 + 64 * lane, prow);
+        }
         __syncwarp();
-        {
+        if (!skip_x && !x_dense) {
           const int atom = lane >> 4, grp = lane & 15;
           int r[4];
 #pragma unroll
@@ -721,7 +733,7 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
                            r[1], r[2], r[3]);
         }
 #pragma unroll
-        for (int gi = lane; gi < (g_dense ? 0 : BN / 4); gi += 32) {
+        for (int gi = lane; gi < (g_dense || skip_g ? 0 : BN / 4); gi += 32) {
           const int atom = gi >> 4, grp = gi & 15;
           int r[4];
 #pragma unroll
@@ -732,7 +744,7 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
           ptx::tma_gather4(b_u + atom * kAtomRowsBytes + grp * 512, &tmap_g, &bar.full[s], n0 + 64 * atom, r[0],
                            r[1], r[2], r[3]);
         }
-        ptx::mbar_arrive(&bar.idxe[s]);
+        if (ring_on) ptx::mbar_arrive(&bar.idxe[s]);
         if (lane == 0) CVMM_STAMP(0, it);
       }
     }
@@ -877,7 +889,7 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = 0.f;
           }
-          warp_store_block(dst, F32, m < p.M ? m * p.N + nc : -1, v, ncols, stage, o_vec);
+          if (!CVMM_DBG(flags, 16384)) warp_store_block(dst, F32, m < p.M ? m * p.N + nc : -1, v, ncols, stage, o_vec);
         }
       }
       ptx::tc_fence_before();
@@ -893,8 +905,9 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
     __syncwarp();
   } else {
     // ------------------------------------------------------------ index warp
+    // (idle when both operands are dense: their rows follow from the unit)
     uint32_t it = 0;
-    bool aborted = false;
+    bool aborted = (flags & 96) == 96;
     for (int tt = blockIdx.x; tt < total && !aborted; tt += gridDim.x) {
       const int4 u = entry(tt);
       const int nkb = nkb_of(u);
@@ -1052,12 +1065,17 @@ static int seg_launch(const SegGemm& p, int64_t max_units, int flags, cudaStream
   // Gathered rows index at most n_routes rows of x and of the grad; the
   // expert-padded sorted grad has n_routes + 128 * n_experts rows and is read
   // as dense 64-row boxes.
-  const bool g_dense = p.g_pad_start != nullptr;
-  const int64_t g_rows = g_dense ? p.n_routes + 128 * p.n_experts : p.n_routes;
+  const bool g_dense = p.g_pad_start != nullptr, x_dense = p.x_pad_start != nullptr;
+  const int64_t padded_rows = p.n_routes + kPadRows * p.n_experts;
   const bool gt = (flags & 3) == 3 && !(dbg_flags() & 4096) &&
-                  make_rows_map(&xmap, p.x, p.op_dtype, p.M, p.n_routes, p.x_ld) &&
-                  make_rows_map(&gmap, p.g, p.op_dtype, p.N, g_rows, p.g_ld, g_dense ? 64 : 1);
+                  make_rows_map(&xmap, p.x, p.op_dtype, p.M, x_dense ? padded_rows : p.n_routes, p.x_ld,
+                                x_dense ? 64 : 1) &&
+                  make_rows_map(&gmap, p.g, p.op_dtype, p.N, g_dense ? padded_rows : p.n_routes, p.g_ld,
+                                g_dense ? 64 : 1);
+  // Without TMA maps the cp.async producers read padded rows through the
+  // resolved route rows like gathered ones.
   if (gt && g_dense) flags |= 32;
+  if (gt && x_dense) flags |= 64;
   if (gt) {
     auto kern = seg_gemm_kernel<BN, S, W, true>;
     int rc = set_smem(kern, L::alloc);

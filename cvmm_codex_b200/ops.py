@@ -18,7 +18,7 @@ from ._lib import check, dtype_code, ptr
 # Kernels each native entry point launches (for launch accounting).
 KERNELS_PER_CALL = {
     "cvmm_sel_prepare": 10, "cvmm_expert_offsets": 1, "cvmm_forward": 2, "cvmm_backward_x": 2,
-    "cvmm_backward_w": 3, "cvmm_weighted_combine": 1, "cvmm_sum_routes": 1,
+    "cvmm_backward_w": 4, "cvmm_weighted_combine": 1, "cvmm_sum_routes": 1,
     "cvmm_weighted_token_backward": 1, "cvmm_cast": 1, "cvmm_sort_rows_padded": 2,
 }
 
@@ -55,7 +55,7 @@ class Recorder:
 _recorder = None
 
 
-def _invoke(name, fn, *args):
+def _invoke(name, fn, *args, kernels=None):
     rec = _recorder
     if rec is None:
         return fn(*args)
@@ -65,7 +65,7 @@ def _invoke(name, fn, *args):
     rc = fn(*args)
     b.record()
     rec.events.setdefault(name, []).append((a, b))
-    rec.launches += KERNELS_PER_CALL.get(name, 1)
+    rec.launches += KERNELS_PER_CALL.get(name, 1) if kernels is None else kernels
     rec.calls += 1
     return rc
 
@@ -158,9 +158,10 @@ def _gemm_ws(lib, n_routes, n_experts, dev, m_dim=0, n_dim=0, op_dtype=torch.bfl
 
 def forward(x: torch.Tensor, sel_index: torch.Tensor, offsets: torch.Tensor, keys: torch.Tensor,
             out_index: Optional[torch.Tensor], out_dtype: torch.dtype,
-            op_dtype: torch.dtype) -> torch.Tensor:
+            op_dtype: torch.dtype, x_pad_start: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Y[row_p] = x[sel_index[p]] @ keys[e_p] for every sorted route p; Y is [R, N]
-    (reference cvmm_triton, cvmm.py:815-867)."""
+    (reference cvmm_triton, cvmm.py:815-867). With x_pad_start, x is the
+    expert-padded sorted layout from sort_rows_padded."""
     _require_cuda(x, sel_index, offsets, keys, out_index)
     lib = _lib.load()
     x2 = _rows(x)
@@ -176,7 +177,7 @@ def forward(x: torch.Tensor, sel_index: torch.Tensor, offsets: torch.Tensor, key
                               ptr(keys), dtype_code(keys.dtype), E, K, N,
                               keys.stride(0), keys.stride(1), keys.stride(2),
                               ptr(out), dtype_code(out_dtype), out.stride(0), dtype_code(op_dtype),
-                              ptr(ws), ws.numel(), stream)
+                              ptr(x_pad_start), ptr(ws), ws.numel(), stream)
     check(rc, "cvmm_forward")
     return out
 
@@ -255,14 +256,18 @@ def backward_w(x: torch.Tensor, x_index: torch.Tensor, x_div: int, g: torch.Tens
                g_index: Optional[torch.Tensor], g_div: int, offsets: torch.Tensor, n_experts: int,
                op_dtype: torch.dtype, w: Optional[torch.Tensor] = None,
                w_index: Optional[torch.Tensor] = None,
-               g_pad_start: Optional[torch.Tensor] = None) -> torch.Tensor:
+               g_pad_start: Optional[torch.Tensor] = None,
+               x_pad_start: Optional[torch.Tensor] = None,
+               n_routes: Optional[int] = None) -> torch.Tensor:
     """fp32 grad_keys[e] = sum_{p in seg e} x[x_index[p]//x_div]^T (w-scaled) g[g_index[p]//g_div]
-    (reference grouped grad-W kernels, cvmm.py:424-604)."""
+    (reference grouped grad-W kernels, cvmm.py:424-604). x_pad_start / g_pad_start:
+    x / g is the expert-padded sorted layout (a padded g already carries the
+    route weights); n_routes is required when x_index is None."""
     _require_cuda(x, x_index, g, g_index, offsets, w, w_index)
     lib = _lib.load()
     x2 = _rows(x)
     g2 = _rows(g)
-    n_routes = x_index.numel()
+    n_routes = x_index.numel() if n_routes is None else int(n_routes)
     M, N = x2.shape[1], g2.shape[1]
     out = torch.empty((int(n_experts), M, N), dtype=torch.float32, device=x.device)
     w2 = None if w is None else w.reshape(-1).contiguous()
@@ -272,19 +277,23 @@ def backward_w(x: torch.Tensor, x_index: torch.Tensor, x_div: int, g: torch.Tens
                                  ptr(g2), dtype_code(g2.dtype), g2.stride(0), ptr(g_index), int(g_div),
                                  ptr(w2), dtype_code(w2.dtype) if w2 is not None else 0, ptr(w_index),
                                  ptr(offsets), n_routes, int(n_experts), M, N, ptr(out),
-                                 dtype_code(op_dtype), ptr(g_pad_start), ptr(ws), ws.numel(), stream)
+                                 dtype_code(op_dtype), ptr(x_pad_start), ptr(g_pad_start), ptr(ws), ws.numel(),
+                                 stream, kernels=3 if (x_pad_start is not None and g_pad_start is not None) else 4)
     check(rc, "cvmm_backward_w")
     return out
 
 
-PAD_ROWS = 128
+PAD_ROWS = 128  # CVMM_PAD_ROWS
 
 
 def sort_rows_padded(src: torch.Tensor, index: torch.Tensor, div: int, sorted_sel: torch.Tensor,
-                     offsets: torch.Tensor, n_experts: int, pad: int = PAD_ROWS):
+                     offsets: torch.Tensor, n_experts: int, dtype: Optional[torch.dtype] = None,
+                     scale: Optional[torch.Tensor] = None):
     """Expert-padded sorted copy of route rows (the reference's grouping copy,
-    cvmm.py:338-360): returns (dst [n_routes + n_experts*pad, cols], pad_start int32 [E])."""
-    _require_cuda(src, index, sorted_sel, offsets)
+    cvmm.py:338-360), rounded to `dtype` (default: src's) and, with `scale`,
+    multiplied by the op-rounded scale[index[p]] and rounded again (cvmm.py:591-599).
+    Returns (dst [n_routes + n_experts*PAD_ROWS, cols], pad_start int32 [E])."""
+    _require_cuda(src, index, sorted_sel, offsets, scale)
     lib = _lib.load()
     s2 = _rows(src)
     n_routes = index.numel()
@@ -292,12 +301,15 @@ def sort_rows_padded(src: torch.Tensor, index: torch.Tensor, div: int, sorted_se
     ss = sorted_sel.reshape(-1)
     if ss.dtype != torch.int32:
         ss = ss.to(torch.int32)
-    dst = torch.empty((n_routes + int(n_experts) * pad, cols), dtype=s2.dtype, device=s2.device)
+    dtype = s2.dtype if dtype is None else dtype
+    sc = None if scale is None else scale.reshape(-1).contiguous()
+    dst = torch.empty((n_routes + int(n_experts) * PAD_ROWS, cols), dtype=dtype, device=s2.device)
     pstart = torch.empty(int(n_experts), dtype=torch.int32, device=s2.device)
     with _Device(s2.device) as stream:
         rc = _invoke("cvmm_sort_rows_padded", lib.cvmm_sort_rows_padded, ptr(s2), dtype_code(s2.dtype), s2.stride(0),
-                     ptr(index), int(div), ptr(ss), ptr(offsets), n_routes, int(n_experts), cols, pad,
-                     ptr(dst), ptr(pstart), stream)
+                     ptr(index), int(div), ptr(sc), dtype_code(sc.dtype) if sc is not None else 0,
+                     ptr(ss), ptr(offsets), n_routes, int(n_experts), cols,
+                     ptr(dst), dtype_code(dtype), ptr(pstart), stream)
     check(rc, "cvmm_sort_rows_padded")
     return dst, pstart
 

@@ -52,7 +52,7 @@ typedef struct CUstream_st* cvmm_stream_t; /* == cudaStream_t */
 #define CVMM_DEV_BAD_INDEX 2
 
 /* ABI version of this header; bumped on any signature change. */
-int cvmm_abi_version(void);  /* 2 */
+int cvmm_abi_version(void);  /* 3 */
 
 /* Message for the last failed call on the calling host thread. */
 const char* cvmm_last_error(void);
@@ -127,8 +127,14 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld,
                  const int64_t* sel_index, const int64_t* out_index, const int64_t* offsets,
                  int64_t n_routes, const void* keys, int keys_dtype, int64_t n_experts,
                  int64_t k_dim, int64_t n_dim, int64_t ks_e, int64_t ks_k, int64_t ks_n,
-                 void* out, int out_dtype, int64_t out_ld, int op_dtype, void* workspace,
-                 size_t workspace_bytes, cvmm_stream_t stream);
+                 void* out, int out_dtype, int64_t out_ld, int op_dtype,
+                 const int32_t* x_pad_start, void* workspace, size_t workspace_bytes,
+                 cvmm_stream_t stream);
+/* With x_pad_start != NULL, x is the expert-padded sorted layout made by
+ * cvmm_sort_rows_padded: the x row of sorted position p is then
+ * x_pad_start[e] + p - seg_begin(e), x_rows is ignored, and sel_index only
+ * names the output rows (when out_index is NULL). bf16/fp16 op_dtype with
+ * x_dtype == op_dtype only. */
 
 /* Weighted combine of the forward: out[t] = cast( sum_j cast_y(w[t,j]) * y[t*top_k+j] ),
  * fp32 accumulate. Replaces the bmm at cvmm.py:1543-1545. */
@@ -170,9 +176,11 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
  *   s_p = 1, or with w != NULL: the g row is first multiplied by op(w[w_index[p]])
  *   and rounded to op_dtype (cvmm.py:591-599).
  * grad_w: [n_experts, m_dim, n_dim] fp32, fully written (empty experts get 0).
- * With g_pad_start != NULL, g is the expert-padded sorted layout of
- * cvmm_sort_rows_padded (pad 128) and g_index / g_div are ignored (bf16/fp16
- * op_dtype only).
+ * x_pad_start / g_pad_start != NULL: x / g is the expert-padded sorted
+ * layout of cvmm_sort_rows_padded and x_index, x_div / g_index, g_div are
+ * ignored (bf16/fp16 op_dtype, operand dtype == op_dtype). A padded g must
+ * already carry the route weights (cvmm_sort_rows_padded's `scale`): w must
+ * then be NULL.
  * Long expert segments are split over several CTAs (split-K); their partial
  * sums live in the workspace (cvmm_gemm_workspace_size with k_dim = m_dim)
  * and are added in a fixed order, so results are deterministic. */
@@ -181,25 +189,30 @@ int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_i
                     const int64_t* g_index, int64_t g_div, const void* w, int w_dtype,
                     const int64_t* w_index, const int64_t* offsets, int64_t n_routes,
                     int64_t n_experts, int64_t m_dim, int64_t n_dim, float* grad_w,
-                    int op_dtype, const int32_t* g_pad_start, void* workspace,
-                    size_t workspace_bytes, cvmm_stream_t stream);
+                    int op_dtype, const int32_t* x_pad_start, const int32_t* g_pad_start,
+                    void* workspace, size_t workspace_bytes, cvmm_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Expert-padded sorted copy of route rows. Replaces the reference's grouping
  * copy cvmm_group_routes / cvmm_group_routes_kernel (cvmm.py:338-360,
  * 1123-1138), with every expert's segment padded with zero rows to a multiple
- * of `pad` rows:
- *   dst[pad_start[e] + (p - seg_begin(e))] = src[index[p] / div]   for sorted p
- * pad_start[e] (int32) = sum over e' < e of round_up(count(e'), pad); all other
- * rows of dst are zero. dst needs n_routes + n_experts * pad rows of `cols`
- * elements (leading dimension cols). Passing dst and pad_start with pad = 128 as
- * `g` / `g_pad_start` to cvmm_backward_x / cvmm_backward_w lets their
- * tensor-core paths read the gradient as dense tiles instead of gathering rows.
+ * of CVMM_PAD_ROWS rows so that the GEMMs read it as dense tensor-core tiles:
+ *   dst[pad_start[e] + (p - seg_begin(e))] = op(src[index[p] / div])
+ *       or, with scale != NULL, op( op(src[index[p] / div]) * op(scale[index[p]]) )
+ * where op() rounds to dst_dtype (the weighted grad-W operand rounding of
+ * cvmm.py:591-599). pad_start[e] (int32) = sum over e' < e of
+ * round_up(count(e'), CVMM_PAD_ROWS); the padding rows of every segment are
+ * zero. dst holds n_routes + n_experts * CVMM_PAD_ROWS rows of `cols`
+ * elements (leading dimension cols); rows past the last segment are not
+ * written. Pass dst / pad_start as x / x_pad_start or g / g_pad_start of
+ * cvmm_forward, cvmm_backward_x and cvmm_backward_w.
  * ------------------------------------------------------------------------ */
-int cvmm_sort_rows_padded(const void* src, int dtype, int64_t src_ld, const int64_t* index,
-                          int64_t div, const int32_t* sorted_sel, const int64_t* offsets,
-                          int64_t n_routes, int64_t n_experts, int64_t cols, int64_t pad,
-                          void* dst, int32_t* pad_start, cvmm_stream_t stream);
+#define CVMM_PAD_ROWS 128
+int cvmm_sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64_t* index,
+                          int64_t div, const void* scale, int scale_dtype,
+                          const int32_t* sorted_sel, const int64_t* offsets, int64_t n_routes,
+                          int64_t n_experts, int64_t cols, void* dst, int dst_dtype,
+                          int32_t* pad_start, cvmm_stream_t stream);
 
 /* Sum over the top-k routes of each token: out[t] = cast( sum_j src[t*top_k+j] ),
  * fp32 accumulate. Replaces grouped_x.view(..., top_k, d).sum(-2) (cvmm.py:1223). */

@@ -108,23 +108,43 @@ def test_cuda_default_sort_agreement_report(capsys):
     print("cuda default sort == stable:", rows)
 
 
-def test_sort_rows_padded_matches_oracle():
-    """Expert-padded sorted copy of route rows (the grouping copy of cvmm.py:338-360)."""
+@pytest.mark.parametrize("src_dtype,dst_dtype,scaled", [
+    (torch.bfloat16, torch.bfloat16, False),
+    (torch.float32, torch.bfloat16, False),
+    (torch.bfloat16, torch.bfloat16, True),
+    (torch.float32, torch.float16, True),
+])
+def test_sort_rows_padded_matches_oracle(src_dtype, dst_dtype, scaled):
+    """Expert-padded sorted copy of route rows (the grouping copy of cvmm.py:338-360),
+    with the op-dtype rounding and the weighted-grad product rounding of cvmm.py:591-599."""
     g = torch.Generator().manual_seed(21)
-    R, E, cols, pad = 3000, 11, 136, 128
-    sel = torch.randint(0, E, (R // 3, 3), generator=g)
+    R, E, cols, pad, k = 3000, 11, 136, 128, 3
+    sel = torch.randint(0, E, (R // k, k), generator=g)
     sel[:, 0] = 4  # a long segment
-    src = torch.randn(R, cols, generator=g).bfloat16()
+    sel[:, 1] = torch.where(sel[:, 1] == 7, 8, sel[:, 1])  # expert 7 empty unless drawn in column 2
+    src = torch.randn(R // k, cols, generator=g).to(src_dtype)
+    w = torch.rand(R // k, k, generator=g) if scaled else None
     s = C.cvmm_prepare_sel2(sel.cuda(), route_input=True)
     offs = ops.expert_offsets(s.sel, E)
-    dst, pstart = ops.sort_rows_padded(src.cuda(), s.sel_index, 1, s.sel, offs, E, pad)
+    # NaN-fill a block the caching allocator hands out again, so unwritten padding would show
+    junk = torch.full(((R + E * pad) * cols * 4,), float("nan"), device="cuda")
+    del junk
+    dst, pstart = ops.sort_rows_padded(src.cuda(), s.sel_index, k, s.sel, offs, E, dtype=dst_dtype,
+                                       scale=None if w is None else w.cuda())
     _, ssel, idx, _ = O.prepare_sel2(sel.numpy(), route_input=True)
     counts = np.bincount(ssel, minlength=E)
-    want_ps = np.concatenate([[0], np.cumsum((counts + pad - 1) // pad * pad)[:-1]]).astype(np.int32)
+    padded = (counts + pad - 1) // pad * pad
+    want_ps = np.concatenate([[0], np.cumsum(padded)[:-1]]).astype(np.int32)
     np.testing.assert_array_equal(pstart.cpu().numpy(), want_ps)
-    want = np.zeros((R + E * pad, cols), dtype=np.float32)
+    op = {torch.bfloat16: "bfloat16", torch.float16: "float16"}[dst_dtype]
+    want = np.zeros((int(padded.sum()), cols), dtype=np.float64)
     seg = np.concatenate([[0], np.cumsum(counts)[:-1]])
+    srcf = src.float().numpy().astype(np.float64)
     for p_ in range(R):
         e = ssel[p_]
-        want[want_ps[e] + p_ - seg[e]] = src[idx[p_]].float().numpy()
-    np.testing.assert_array_equal(dst.float().cpu().numpy(), want)
+        row = O.round_op(srcf[idx[p_] // k], op)
+        if w is not None:
+            row = O.round_op(row * O.round_op(w.reshape(-1)[idx[p_]].item(), op), op)
+        want[want_ps[e] + p_ - seg[e]] = row
+    got = dst[: int(padded.sum())].float().cpu().numpy()
+    np.testing.assert_array_equal(got, want)
