@@ -8,12 +8,14 @@ gradients are summed with an NCCL all-reduce inside the step.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
-Prints one JSON line (rank 0). Timing: CUDA events on the compute stream around
+Prints one JSON line (rank 0). The step is captured once as a CUDA graph and
+replayed (`--eager` times Python-issued steps instead); every kernel of the
+step runs on every replay. Timing: CUDA events on the compute stream around
 each step, L2 flushed (256 MiB write) before every timed step and outside the
-events, max over ranks. `e2e` repeats the step through the public API with the
-step's inputs copied from pinned host memory and a scalar read back every
-step. `roofline` covers the kernel with the largest share of the step, timed
-with CUDA events around its launches inside the timed steps.
+events, max over ranks. `e2e` repeats the step with the step's inputs copied
+from pinned host memory into the step's input tensors and a scalar read back,
+every step. `roofline` covers the native call with the largest share of the
+step, timed with CUDA events around its launches in eager steps.
 """
 from __future__ import annotations
 
@@ -43,6 +45,7 @@ def parse():
     p.add_argument("--workload", default=DEFAULT_WORKLOAD)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--eager", action="store_true", help="time eager steps instead of CUDA-graph replays")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--also", default="ff_down_1024_weighted",
                    help="comma-separated extra workloads reported under 'also' (N=1 only)")
@@ -145,7 +148,35 @@ def build_step(w, d, world):
     return step
 
 
-def time_steps(step, d, steps, flush, recorder=None):
+class GraphedStep:
+    """The step captured once as a CUDA graph and replayed: every kernel of the
+    step (selector prep, GEMMs, copies, reductions, the NCCL all-reduce when
+    N > 1) runs on each replay; only the host's per-launch work is gone. Inputs
+    are the captured tensors d["sel"], d["grad_out"], x, keys, weights, which
+    the e2e loop overwrites in place before each replay."""
+
+    def __init__(self, step, d):
+        self.d = d
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                step(d["sel"], d["grad_out"])
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = step(d["sel"], d["grad_out"])
+        torch.cuda.synchronize()
+
+    def __call__(self, sel=None, grad_out=None):
+        self.graph.replay()
+        return self.out
+
+
+def time_steps(run, d, steps, flush, recorder=None):
+    """Device time of `steps` steps (ms, summed), each bracketed by CUDA events
+    on the current stream with the L2 flushed before it, outside the events."""
     times = []
     for _ in range(steps):
         flush.zero_()
@@ -154,22 +185,21 @@ def time_steps(step, d, steps, flush, recorder=None):
         a.record()
         if recorder is not None:
             with recorder:
-                step(d["sel"], d["grad_out"])
+                run(d["sel"], d["grad_out"])
         else:
-            step(d["sel"], d["grad_out"])
+            run(d["sel"], d["grad_out"])
         b.record()
         times.append((a, b))
     torch.cuda.synchronize()
     return sum(a.elapsed_time(b) for a, b in times)
 
 
-def time_e2e(step, d, steps, flush):
+def time_e2e(run, d, steps, flush):
     """Public-API step with host inputs: H2D of x/sel/grad_out (and weights) from
-    pinned memory, the step, and a D2H read of a scalar result, every step."""
+    pinned memory into the step's input tensors, the step, and a D2H read of a
+    scalar result, every step."""
     host = {k: (None if v is None else v.detach().cpu().pin_memory()) for k, v in d.items() if k != "keys"}
-    dev = {k: (None if v is None else torch.empty_like(v, device="cuda")) for k, v in host.items()}
     res_h = torch.empty((), dtype=torch.float32).pin_memory()
-    x_param = d["x"]
     h2d = sum(v.numel() * v.element_size() for v in host.values() if v is not None)
     total = 0.0
     for i in range(steps + 1):
@@ -177,14 +207,11 @@ def time_e2e(step, d, steps, flush):
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record()
-        for k, v in host.items():
-            if v is not None:
-                dev[k].copy_(v, non_blocking=True)
         with torch.no_grad():
-            x_param.copy_(dev["x"])
-            if d["weights"] is not None:
-                d["weights"].copy_(dev["weights"])
-        out = step(dev["sel"], dev["grad_out"])
+            for k, v in host.items():
+                if v is not None:
+                    d[k].copy_(v, non_blocking=True)
+        out = run(d["sel"], d["grad_out"])
         res_h.copy_(out.detach()[..., 0].float().sum(), non_blocking=True)
         b.record()
         torch.cuda.synchronize()
@@ -208,14 +235,26 @@ def run_ours(args, rank, world, local_rank):
         d = make_inputs(w, "cuda", seed=rank)
         step = build_step(w, d, world)
         rec = ops.Recorder()
+        for _ in range(max(args.warmup, 3)):
+            step(d["sel"], d["grad_out"])
+        # Per-call device times and launch counts: eager steps with CUDA events
+        # around every native call (the roofline's kernel durations).
+        time_steps(step, d, max(3, min(args.steps, 10)), flush, rec)
+        run, graphed = step, False
+        if not args.eager:
+            try:
+                run, graphed = GraphedStep(step, d), True
+            except Exception as exc:  # capture unsupported here: time the eager step
+                print(f"CUDA graph capture failed ({exc!r}); timing eager steps", file=sys.stderr)
+                torch.cuda.synchronize()
         with ClockSampler(local_rank) as clk:
             for _ in range(max(args.warmup, 3)):
-                step(d["sel"], d["grad_out"])
+                run(d["sel"], d["grad_out"])
             torch.cuda.synchronize()
             if world > 1:
                 dist.barrier()
             torch.cuda.synchronize()
-            total_ms = time_steps(step, d, args.steps, flush, rec)
+            total_ms = time_steps(run, d, args.steps, flush)
         if world > 1:
             t = torch.tensor([total_ms], device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -224,9 +263,9 @@ def run_ours(args, rank, world, local_rank):
         ms = total_ms / args.steps
         flops = w.flops() * world
         res = {"w": w, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "clocks": clk.summary(),
-               "launches": rec.launches // args.steps, "per_call": rec.summary()}
+               "launches": rec.launches // max(rec.steps, 1), "per_call": rec.summary(), "graphed": graphed}
         if with_e2e:
-            e_ms, bi, bo = time_e2e(step, d, max(3, args.steps // 5), flush)
+            e_ms, bi, bo = time_e2e(run, d, max(3, args.steps // 5), flush)
             if world > 1:
                 t = torch.tensor([e_ms], device="cuda")
                 dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -248,6 +287,7 @@ def run_ours(args, rank, world, local_rank):
                    "experts": w.E, "top_k": w.k, "weighted": w.weighted, "route_input": w.route_input,
                    "global_tokens": w.T * world, "parallelism": f"token-sharded dp{world}",
                    "l2": "flushed (256 MiB write) before every timed step",
+                   "cuda_graph": main["graphed"],
                    "flops_per_step_per_gpu": w.flops(),
                    "pct_bf16_peak_sustained": round(100 * main["tflops"] / world / pk["bf16_tflops_sustained"], 2)},
         "clocks": main["clocks"],

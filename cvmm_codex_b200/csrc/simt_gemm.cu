@@ -197,62 +197,117 @@ __device__ __forceinline__ void store8(char* to, int dtype, const float (&v)[8])
   *reinterpret_cast<uint4*>(to) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// One warp per row of the expert-padded sorted copy. Virtual rows
-// [0, n_routes) are the sorted routes: dst[pad_start[e] + p - seg_begin(e)] =
-// op(src[index[p] / div]) (times op(scale[index[p]]), rounded again); rows
-// [n_routes, n_routes + n_experts * kPadRows) enumerate every expert's
-// candidate padding rows, and those inside the expert's padded segment are
-// zeroed. mode 0: byte copy (same dtype, no scale), 1: 8-element vectors with
-// conversion, 2: scalar elements.
-__global__ void sort_rows_padded_kernel(const char* __restrict__ src, int src_dtype, int64_t src_ld,
-                                        const int64_t* __restrict__ index, int64_t div, const void* __restrict__ scale,
-                                        int scale_dtype, const int32_t* __restrict__ sorted_sel,
-                                        const int64_t* __restrict__ offsets, const int* __restrict__ pad_start,
-                                        int64_t n_routes, int64_t n_experts, int64_t cols, char* __restrict__ dst,
-                                        int dst_dtype, int mode) {
-  const int lane = threadIdx.x & 31;
-  const int ssz = dtype_bytes(src_dtype), dsz = dtype_bytes(dst_dtype);
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+// Expert-padded sorted copy. Virtual rows [0, n_routes) are the sorted routes:
+// dst[pad_start[e] + p - seg_begin(e)] = op(src[index[p] / div]) (times
+// op(scale[index[p]]), rounded again); rows [n_routes, n_routes + n_experts *
+// kPadRows) enumerate every expert's candidate padding rows, and those inside
+// the expert's padded segment are zeroed.
+// Each CTA owns 32 consecutive virtual rows: lane l of warp 0 resolves row
+// l's source, destination and scale (one round of index loads for all 32
+// rows, in parallel), then the CTA's 256 threads stream the rows' chunks
+// with kSortBatch loads in flight per thread before converting and storing.
+// MODE 0: 16-byte copy (same dtype, no scale), 1: 8-element vectors with
+// conversion (and scale), 2: scalar elements.
+constexpr int kSortBatch = 8;
+
+struct SortRowMeta {
+  long long src;  // source element offset of the row, -1: zero row
+  long long dst;  // destination element offset, -1: no row
+  float scale;
+  int pad;
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(256) sort_rows_padded_kernel(
+    const char* __restrict__ src, int src_dtype, int64_t src_ld, const int64_t* __restrict__ index, int64_t div,
+    const void* __restrict__ scale, int scale_dtype, const int32_t* __restrict__ sorted_sel,
+    const int64_t* __restrict__ offsets, const int* __restrict__ pad_start, int64_t n_routes, int64_t n_experts,
+    int64_t cols, char* __restrict__ dst, int dst_dtype) {
+  __shared__ SortRowMeta meta[32];
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int64_t v0 = blockIdx.x * (int64_t)32;
   const int64_t total = n_routes + n_experts * kPadRows;
-  for (int64_t v = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); v < total; v += warps) {
-    if (v >= n_routes) {
+  if (tid < 32) {
+    const int64_t v = v0 + lane;
+    SortRowMeta m = {-1, -1, 1.f, 0};
+    if (v < n_routes) {
+      const int64_t r = index[v];
+      const int64_t e = sorted_sel[v];
+      m.src = idx_div(r, div) * src_ld;
+      m.dst = (pad_start[e] + v - seg_begin(offsets, e)) * cols;
+      if (scale) m.scale = round_to(load_as_float(scale, scale_dtype, r), dst_dtype);
+    } else if (v < total) {
       const int64_t e = (v - n_routes) / kPadRows, i = (v - n_routes) % kPadRows;
       const int64_t cnt = offsets[e] - seg_begin(offsets, e);
-      if (cnt + i >= (cnt + kPadRows - 1) / kPadRows * kPadRows) continue;
-      char* to = dst + (pad_start[e] + cnt + i) * cols * dsz;
-      const int64_t bytes = cols * dsz;
-      if (mode != 2) {
-        for (int64_t b = lane * 16; b < bytes; b += 32 * 16) *reinterpret_cast<uint4*>(to + b) = make_uint4(0, 0, 0, 0);
-      } else {
-        for (int64_t b = lane; b < bytes; b += 32) to[b] = 0;
-      }
-      continue;
+      if (cnt + i < (cnt + kPadRows - 1) / kPadRows * kPadRows) m.dst = (pad_start[e] + cnt + i) * cols;
     }
-    const int64_t e = sorted_sel[v];
-    const int64_t q = pad_start[e] + v - seg_begin(offsets, e);
-    const int64_t r = index[v];
-    const char* from = src + idx_div(r, div) * src_ld * ssz;
-    char* to = dst + q * cols * dsz;
-    const float sc = scale ? round_to(load_as_float(scale, scale_dtype, r), dst_dtype) : 1.f;
-    if (mode == 0) {
-      for (int64_t b = lane * 16; b < cols * dsz; b += 32 * 16)
-        *reinterpret_cast<uint4*>(to + b) = *reinterpret_cast<const uint4*>(from + b);
-    } else if (mode == 1) {
-      for (int64_t c = lane * 8; c < cols; c += 32 * 8) {
-        float x[8];
-        load8(from + c * ssz, src_dtype, x);
+    meta[lane] = m;
+  }
+  __syncthreads();
+  const int ssz = dtype_bytes(src_dtype), dsz = dtype_bytes(dst_dtype);
+  if (MODE == 2) {
+    for (int rr = tid >> 5; rr < 32; rr += blockDim.x >> 5) {
+      const SortRowMeta m = meta[rr];
+      if (m.dst < 0) continue;
+      for (int64_t c = lane; c < cols; c += 32) {
+        float x = m.src < 0 ? 0.f : round_to(load_as_float(src, src_dtype, m.src + c), dst_dtype);
+        if (scale && m.src >= 0) x = x * m.scale;
+        store_from_float(dst, dst_dtype, m.dst + c, x);
+      }
+    }
+    return;
+  }
+  // Work items: (row, 8-element chunk) pairs; MODE 0 moves 16-byte chunks.
+  const int64_t per_row = MODE == 0 ? cols * dsz / 16 : cols / 8;
+  const int64_t items = 32 * per_row;
+  const uint32_t pr = (uint32_t)per_row;  // items < 2^32: 32-bit row / chunk split
+  constexpr int kBatch = MODE == 0 ? kSortBatch : kSortBatch / 2;
+  for (int64_t base = 0; base < items; base += (int64_t)blockDim.x * kBatch) {
+    if (MODE == 0) {
+      uint4 buf[kSortBatch];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          x[j] = round_to(x[j], dst_dtype);
-          if (scale) x[j] = x[j] * sc;
+      for (int u = 0; u < kSortBatch; ++u) {
+        const int64_t it = base + tid + (int64_t)blockDim.x * u;
+        buf[u] = make_uint4(0, 0, 0, 0);
+        if (it < items) {
+          const SortRowMeta& m = meta[(uint32_t)it / pr];
+          if (m.dst >= 0 && m.src >= 0)
+            buf[u] = reinterpret_cast<const uint4*>(src + m.src * ssz)[(uint32_t)it % pr];
         }
-        store8(to + c * dsz, dst_dtype, x);
+      }
+#pragma unroll
+      for (int u = 0; u < kSortBatch; ++u) {
+        const int64_t it = base + tid + (int64_t)blockDim.x * u;
+        if (it < items) {
+          const SortRowMeta& m = meta[(uint32_t)it / pr];
+          if (m.dst >= 0) reinterpret_cast<uint4*>(dst + m.dst * dsz)[(uint32_t)it % pr] = buf[u];
+        }
       }
     } else {
-      for (int64_t c = lane; c < cols; c += 32) {
-        float x = round_to(load_as_float(from, src_dtype, c), dst_dtype);
-        if (scale) x = x * sc;
-        store_from_float(to, dst_dtype, c, x);
+      constexpr int B = kBatch;
+      float x[B][8];
+#pragma unroll
+      for (int u = 0; u < B; ++u) {
+        const int64_t it = base + tid + (int64_t)blockDim.x * u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) x[u][j] = 0.f;
+        if (it < items) {
+          const SortRowMeta& m = meta[(uint32_t)it / pr];
+          if (m.dst >= 0 && m.src >= 0) load8(src + (m.src + ((uint32_t)it % pr) * 8) * ssz, src_dtype, x[u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < B; ++u) {
+        const int64_t it = base + tid + (int64_t)blockDim.x * u;
+        if (it >= items) continue;
+        const SortRowMeta& m = meta[(uint32_t)it / pr];
+        if (m.dst < 0) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          x[u][j] = round_to(x[u][j], dst_dtype);
+          if (scale) x[u][j] = x[u][j] * m.scale;
+        }
+        store8(dst + (m.dst + ((uint32_t)it % pr) * 8) * dsz, dst_dtype, x[u]);
       }
     }
   }
@@ -265,12 +320,22 @@ int sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64
   const int ssz = dtype_bytes(src_dtype), dsz = dtype_bytes(dst_dtype);
   const bool aligned = ((cols * ssz) % 16 == 0) && ((src_ld * ssz) % 16 == 0) && ((cols * dsz) % 16 == 0) &&
                        (((uintptr_t)src & 15u) == 0) && (((uintptr_t)dst & 15u) == 0) && cols % 8 == 0;
-  const int mode = !aligned ? 2 : (src_dtype == dst_dtype && scale == nullptr ? 0 : 1);
   const int64_t rows = n_routes + n_experts * kPadRows;
-  const int64_t blocks = std::min<int64_t>((rows + 7) / 8, 148 * 16);
-  sort_rows_padded_kernel<<<(unsigned)std::max<int64_t>(blocks, 1), 256, 0, stream>>>(
-      static_cast<const char*>(src), src_dtype, src_ld, index, div, scale, scale_dtype, sorted_sel, offsets, pad_start,
-      n_routes, n_experts, cols, static_cast<char*>(dst), dst_dtype, mode);
+  const unsigned grid = (unsigned)std::max<int64_t>((rows + 31) / 32, 1);
+  const char* s = static_cast<const char*>(src);
+  char* d = static_cast<char*>(dst);
+  if (aligned && src_dtype == dst_dtype && scale == nullptr)
+    sort_rows_padded_kernel<0><<<grid, 256, 0, stream>>>(s, src_dtype, src_ld, index, div, scale, scale_dtype,
+                                                         sorted_sel, offsets, pad_start, n_routes, n_experts, cols, d,
+                                                         dst_dtype);
+  else if (aligned)
+    sort_rows_padded_kernel<1><<<grid, 256, 0, stream>>>(s, src_dtype, src_ld, index, div, scale, scale_dtype,
+                                                         sorted_sel, offsets, pad_start, n_routes, n_experts, cols, d,
+                                                         dst_dtype);
+  else
+    sort_rows_padded_kernel<2><<<grid, 256, 0, stream>>>(s, src_dtype, src_ld, index, div, scale, scale_dtype,
+                                                         sorted_sel, offsets, pad_start, n_routes, n_experts, cols, d,
+                                                         dst_dtype);
   return check_launch("sort_rows_padded");
 }
 

@@ -32,9 +32,11 @@ class Recorder:
         self.events = {}
         self.launches = 0
         self.calls = 0
+        self.steps = 0  # times the recorder was entered
 
     def __enter__(self):
         global _recorder
+        self.steps += 1
         self._prev = _recorder
         _recorder = self
         return self
