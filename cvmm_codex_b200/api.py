@@ -190,13 +190,20 @@ class CVMM(torch.autograd.Function):
             # the forward and the grad-W read it as dense tiles (the reference's
             # grouped-x copy, cvmm.py:1123-1138).
             xs, xpad = ops.sort_rows_padded(x, sel_index, 1, sel, offsets, n_experts, dtype=op_dtype)
-            res = ops.forward(xs, sel_index, offsets, keys_op, out_index, op_dtype, op_dtype, x_pad_start=xpad)
-        else:
-            res = ops.forward(x, sel_index, offsets, keys_op, out_index, op_dtype, op_dtype)
+        a = x if xs is None else xs
         if reduction_weight is not None:
-            res = ops.weighted_combine(res, reduction_weight, op_dtype)
+            rows = out_pad = None
+            if xs is not None and keys.shape[-1] % 8 == 0:
+                # Route outputs stay in the padded sorted layout (dense TMA tile
+                # stores); the weighted combine gathers them per token.
+                out_pad = xpad
+                rows = ops.padded_route_rows(out_index if out_index is not None else sel_index, sel, offsets, xpad)
+            y = ops.forward(a, sel_index, offsets, keys_op, out_index, op_dtype, op_dtype, x_pad_start=xpad,
+                            out_pad_start=out_pad)
+            res = ops.weighted_combine(y, reduction_weight, op_dtype, y_rows=rows)
             res = res.view(*reduction_weight.shape[:-1], res.shape[-1])
         else:
+            res = ops.forward(a, sel_index, offsets, keys_op, out_index, op_dtype, op_dtype, x_pad_start=xpad)
             res = res.view(*sel.shape, res.shape[-1])
         ctx.save_for_backward(x, keys_op, raw_sel, sel, sel_index, out_index, reduction_weight, offsets, xs, xpad)
         ctx.op_type = op_dtype
@@ -241,10 +248,18 @@ class CVMM(torch.autograd.Function):
                                                g_pad_start=g_pad)
             if need_x:
                 # gx_route[route] = g[route] W_e^T, then summed over k (cvmm.py:1199-1223)
-                gxr = ops.backward_x(g_rows, g_idx, 1, route, offsets, keys_op, x.dtype, op, g_pad_start=g_pad)
                 if x_rows == n_routes:
+                    gxr = ops.backward_x(g_rows, g_idx, 1, route, offsets, keys_op, x.dtype, op, g_pad_start=g_pad)
                     grad_x = gxr.view_as(x)
+                elif g_pad is not None and x.dtype == op and x.shape[-1] % 8 == 0:
+                    # Route grads stay in the padded sorted layout (dense TMA
+                    # tile stores); the k-sum gathers them per token.
+                    gxs = ops.backward_x(g_rows, None, 1, None, offsets, keys_op, x.dtype, op, g_pad_start=g_pad,
+                                         out_pad_start=g_pad, n_routes=n_routes)
+                    rows = ops.padded_route_rows(route, sel, offsets, g_pad)
+                    grad_x = ops.sum_routes(gxs, n_routes // x_rows, x.dtype, src_rows=rows).view_as(x)
                 else:
+                    gxr = ops.backward_x(g_rows, g_idx, 1, route, offsets, keys_op, x.dtype, op, g_pad_start=g_pad)
                     grad_x = ops.sum_routes(gxr, n_routes // x_rows, x.dtype).view_as(x)
         else:
             k = w.shape[-1]

@@ -30,45 +30,75 @@ int check_launch(const char* where) {
 }
 
 // ------------------------------------------------------------------ small kernels
-// out[t][n] = sum_j wj * src[t*k + j][n], wj = round(w[t*k+j], src dtype) or 1.
-// Each thread produces 8 consecutive columns; rows are read with 16-byte loads
-// when the layout allows (vec), which is the case for every hot shape.
-__global__ void combine_kernel(const void* __restrict__ src, int s_dtype, const void* __restrict__ w,
-                               int w_dtype, void* __restrict__ out, int o_dtype, int64_t T,
-                               int64_t k, int64_t N, bool vec) {
+// out[t][n] = sum_j wj * src[row(t*k + j)][n], wj = round(w[t*k+j], src dtype)
+// or 1, row(r) = rows[r] (expert-padded sorted source) or r. One thread per 8
+// consecutive columns of one token; VEC: 16-bit rows read and written with
+// 16-byte accesses, up to kCombineBatch route rows in flight per thread.
+// Routes are added in ascending j (the reference's sum / bmm order).
+constexpr int kCombineBatch = 8;
+
+template <bool VEC>
+__global__ void __launch_bounds__(256) combine_kernel(const void* __restrict__ src, int s_dtype,
+                                                      const void* __restrict__ w, int w_dtype,
+                                                      const int32_t* __restrict__ rows, void* __restrict__ out,
+                                                      int o_dtype, int64_t T, int64_t k, int64_t N) {
   const int64_t groups = (N + 7) / 8;
-  const int64_t total = T * groups;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = i / groups, n0 = (i % groups) * 8;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int64_t j = 0; j < k; ++j) {
-      const int64_t r = t * k + j;
-      const float wj = w ? round_to(load_as_float(w, w_dtype, r), s_dtype) : 1.f;
-      if (vec && s_dtype != F32) {
-        const uint4 q = *reinterpret_cast<const uint4*>(static_cast<const char*>(src) + (r * N + n0) * 2);
-        const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= T * groups) return;
+  const int64_t t = i / groups, n0 = (i - t * groups) * 8;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int64_t j0 = 0; j0 < k; j0 += kCombineBatch) {
+    if (VEC) {
+      uint4 q[kCombineBatch];
+      float wj[kCombineBatch];
+#pragma unroll
+      for (int u = 0; u < kCombineBatch; ++u) {
+        const int64_t j = j0 + u;
+        if (j < k) {
+          const int64_t r = t * k + j;
+          const int64_t row = rows ? rows[r] : r;
+          wj[u] = w ? round_to(load_as_float(w, w_dtype, r), s_dtype) : 1.f;
+          q[u] = *reinterpret_cast<const uint4*>(static_cast<const char*>(src) + (row * N + n0) * 2);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kCombineBatch; ++u) {
+        if (j0 + u >= k) break;
+        const uint32_t wd[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          acc[2 * c] = fmaf(wj, bits_to_float((uint16_t)(wd[c] & 0xffffu), s_dtype), acc[2 * c]);
-          acc[2 * c + 1] = fmaf(wj, bits_to_float((uint16_t)(wd[c] >> 16), s_dtype), acc[2 * c + 1]);
+          acc[2 * c] = fmaf(wj[u], bits_to_float((uint16_t)(wd[c] & 0xffffu), s_dtype), acc[2 * c]);
+          acc[2 * c + 1] = fmaf(wj[u], bits_to_float((uint16_t)(wd[c] >> 16), s_dtype), acc[2 * c + 1]);
         }
-      } else {
-        for (int c = 0; c < 8 && n0 + c < N; ++c)
-          acc[c] = fmaf(wj, load_as_float(src, s_dtype, r * N + n0 + c), acc[c]);
+      }
+    } else {
+      for (int64_t j = j0; j < k && j < j0 + kCombineBatch; ++j) {
+        const int64_t r = t * k + j;
+        const int64_t row = rows ? rows[r] : r;
+        const float wj = w ? round_to(load_as_float(w, w_dtype, r), s_dtype) : 1.f;
+        for (int c = 0; c < 8 && n0 + c < N; ++c) acc[c] = fmaf(wj, load_as_float(src, s_dtype, row * N + n0 + c), acc[c]);
       }
     }
-    if (vec && o_dtype != F32) {
-      uint32_t wd[4];
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        wd[c] = (uint32_t)float_to_bits(acc[2 * c], o_dtype) |
-                ((uint32_t)float_to_bits(acc[2 * c + 1], o_dtype) << 16);
-      *reinterpret_cast<uint4*>(static_cast<char*>(out) + (t * N + n0) * 2) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
-    } else {
-      for (int c = 0; c < 8 && n0 + c < N; ++c) store_from_float(out, o_dtype, t * N + n0 + c, acc[c]);
-    }
   }
+  if (VEC) {
+    uint32_t wd[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      wd[c] = (uint32_t)float_to_bits(acc[2 * c], o_dtype) | ((uint32_t)float_to_bits(acc[2 * c + 1], o_dtype) << 16);
+    *reinterpret_cast<uint4*>(static_cast<char*>(out) + (t * N + n0) * 2) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  } else {
+    for (int c = 0; c < 8 && n0 + c < N; ++c) store_from_float(out, o_dtype, t * N + n0 + c, acc[c]);
+  }
+}
+
+// rows[route[v]] = pad_start[e] + v - seg_begin(e) for every sorted position v.
+__global__ void padded_route_rows_kernel(const int64_t* __restrict__ route, const int32_t* __restrict__ sorted_sel,
+                                         const int64_t* __restrict__ offsets, const int32_t* __restrict__ pad_start,
+                                         int64_t n_routes, int32_t* __restrict__ rows) {
+  const int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (v >= n_routes) return;
+  const int64_t e = sorted_sel[v];
+  rows[route[v]] = (int32_t)(pad_start[e] + v - seg_begin(offsets, e));
 }
 
 // One CTA per token: grad_x[t] = sum_j w'[t,j] rg[t,j,:],  gsel[t,j] = <rg[t,j,:], x[t,:]>.
@@ -212,7 +242,7 @@ using namespace cvmm;
 // ================================================================== C ABI
 extern "C" {
 
-int cvmm_abi_version(void) { return 3; }
+int cvmm_abi_version(void) { return 4; }
 
 const char* cvmm_last_error(void) { return t_err; }
 
@@ -265,13 +295,15 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld, const
                  const int64_t* out_index, const int64_t* offsets, int64_t n_routes,
                  const void* keys, int keys_dtype, int64_t n_experts, int64_t k_dim, int64_t n_dim,
                  int64_t ks_e, int64_t ks_k, int64_t ks_n, void* out, int out_dtype, int64_t out_ld,
-                 int op_dtype, const int32_t* x_pad_start, void* workspace, size_t workspace_bytes,
-                 cvmm_stream_t stream) {
+                 int op_dtype, const int32_t* x_pad_start, const int32_t* out_pad_start, void* workspace,
+                 size_t workspace_bytes, cvmm_stream_t stream) {
   if (!is_float_dtype(x_dtype) || !is_float_dtype(keys_dtype) || !is_float_dtype(out_dtype) ||
       !is_float_dtype(op_dtype))
     return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_forward: unsupported dtype");
   if (x_pad_start && (op_dtype == F32 || x_dtype != op_dtype))
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: the padded sorted layout needs x_dtype == op_dtype (bf16/fp16)");
+  if (out_pad_start && op_dtype == F32)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: a padded sorted output needs a bf16/fp16 op_dtype");
   if (n_routes < 0 || n_experts <= 0 || k_dim < 0 || n_dim <= 0 || x_rows < 0 || x_ld < k_dim ||
       out_ld < n_dim)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: bad sizes");
@@ -285,6 +317,7 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld, const
   p.a_index = sel_index; p.a_div = 1; p.a_pad_start = x_pad_start;
   p.b = keys; p.b_dtype = keys_dtype; p.bs_e = ks_e; p.bs_k = ks_k; p.bs_n = ks_n;
   p.c = out; p.c_dtype = out_dtype; p.c_ld = out_ld; p.c_index = out_index ? out_index : sel_index;
+  p.c_pad_start = out_pad_start;
   p.offsets = offsets; p.n_routes = n_routes; p.n_experts = n_experts; p.K = k_dim; p.N = n_dim;
   p.mode = 0; p.op_dtype = op_dtype;
   return run_row_gemm(p, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), "cvmm_forward");
@@ -292,7 +325,7 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld, const
 
 int cvmm_weighted_combine(const void* y, int y_dtype, const void* w, int w_dtype, void* out,
                           int out_dtype, int64_t n_tokens, int64_t top_k, int64_t n_dim,
-                          cvmm_stream_t stream) {
+                          const int32_t* y_rows, cvmm_stream_t stream) {
   if (!is_float_dtype(y_dtype) || (w && !is_float_dtype(w_dtype)) || !is_float_dtype(out_dtype))
     return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_weighted_combine: unsupported dtype");
   if (n_tokens < 0 || top_k <= 0 || n_dim <= 0)
@@ -301,15 +334,32 @@ int cvmm_weighted_combine(const void* y, int y_dtype, const void* w, int w_dtype
   if (!y || !out) return fail(CVMM_ERR_INVALID_ARG, "cvmm_weighted_combine: null pointer");
   const bool vec = n_dim % 8 == 0 && y_dtype != F32 && out_dtype != F32 && al16(y) && al16(out);
   const int64_t work = n_tokens * ((n_dim + 7) / 8);
-  combine_kernel<<<grid_for(work, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      y, y_dtype, w, w_dtype, out, out_dtype, n_tokens, top_k, n_dim, vec);
+  const unsigned grid = (unsigned)((work + 255) / 256);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (vec)
+    combine_kernel<true><<<grid, 256, 0, s>>>(y, y_dtype, w, w_dtype, y_rows, out, out_dtype, n_tokens, top_k, n_dim);
+  else
+    combine_kernel<false><<<grid, 256, 0, s>>>(y, y_dtype, w, w_dtype, y_rows, out, out_dtype, n_tokens, top_k, n_dim);
   return check_launch("cvmm_weighted_combine");
 }
 
 int cvmm_sum_routes(const void* src, int src_dtype, void* out, int out_dtype, int64_t n_tokens,
-                    int64_t top_k, int64_t d, cvmm_stream_t stream) {
-  return cvmm_weighted_combine(src, src_dtype, nullptr, CVMM_F32, out, out_dtype, n_tokens, top_k, d,
+                    int64_t top_k, int64_t d, const int32_t* src_rows, cvmm_stream_t stream) {
+  return cvmm_weighted_combine(src, src_dtype, nullptr, CVMM_F32, out, out_dtype, n_tokens, top_k, d, src_rows,
                                stream);
+}
+
+int cvmm_padded_route_rows(const int64_t* route, const int32_t* sorted_sel, const int64_t* offsets,
+                           const int32_t* pad_start, int64_t n_routes, int64_t n_experts, int32_t* rows,
+                           cvmm_stream_t stream) {
+  if (n_routes < 0 || n_experts <= 0 || n_routes + n_experts * kPadRows > (int64_t)INT32_MAX)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_padded_route_rows: bad sizes");
+  if (n_routes == 0) return CVMM_OK;
+  if (!route || !sorted_sel || !offsets || !pad_start || !rows)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_padded_route_rows: null pointer");
+  padded_route_rows_kernel<<<(unsigned)((n_routes + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      route, sorted_sel, offsets, pad_start, n_routes, rows);
+  return check_launch("cvmm_padded_route_rows");
 }
 
 int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_index, int64_t g_div,
@@ -317,8 +367,8 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
                     const void* keys, int keys_dtype, int64_t n_experts, int64_t k_dim, int64_t n_dim,
                     int64_t ks_e, int64_t ks_k, int64_t ks_n, void* out, int out_dtype, int64_t out_ld,
                     int mode, const void* w, int w_dtype, const void* x, int x_dtype, int64_t x_ld,
-                    float* gsel, int op_dtype, const int32_t* g_pad_start, void* workspace,
-                    size_t workspace_bytes, cvmm_stream_t stream) {
+                    float* gsel, int op_dtype, const int32_t* g_pad_start, const int32_t* out_pad_start,
+                    void* workspace, size_t workspace_bytes, cvmm_stream_t stream) {
   if (!is_float_dtype(g_dtype) || !is_float_dtype(keys_dtype) || !is_float_dtype(out_dtype) ||
       !is_float_dtype(op_dtype))
     return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_backward_x: unsupported dtype");
@@ -328,8 +378,10 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: bad sizes");
   if (n_routes == 0) return CVMM_OK;
   if (n_routes > (int64_t)INT32_MAX) return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: too many routes");
-  if (!g || (!g_index && !g_pad_start) || !out_index || !offsets || !keys || !out)
+  if (!g || (!g_index && !g_pad_start) || (!out_index && !out_pad_start) || !offsets || !keys || !out)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: null pointer");
+  if (out_pad_start && (mode != 0 || op_dtype == F32))
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: a padded sorted output needs mode 0 and a bf16/fp16 op_dtype");
   if (g_pad_start && op_dtype == F32)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: the padded sorted gradient layout needs bf16/fp16 op_dtype");
   if (mode == 1 && (!w || !x || !gsel || !is_float_dtype(w_dtype) || !is_float_dtype(x_dtype) || x_ld < k_dim))
@@ -342,7 +394,7 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
   p.c = out; p.c_dtype = out_dtype; p.c_ld = out_ld; p.c_index = out_index;
   p.offsets = offsets; p.n_routes = n_routes; p.n_experts = n_experts; p.K = n_dim; p.N = k_dim;
   p.mode = mode; p.w = w; p.w_dtype = w_dtype; p.x = x; p.x_dtype = x_dtype; p.x_ld = x_ld;
-  p.gsel = gsel; p.op_dtype = op_dtype; p.a_pad_start = g_pad_start;
+  p.gsel = gsel; p.op_dtype = op_dtype; p.a_pad_start = g_pad_start; p.c_pad_start = out_pad_start;
   return run_row_gemm(p, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), "cvmm_backward_x");
 }
 

@@ -28,6 +28,7 @@ struct RowGemm {
   int op_dtype;
   const int4* tiles;   // (expert, first sorted position, rows, 0) per M tile
   const int* a_pad_start;  // non-null: A is the expert-padded sorted layout (row = pad_start[e] + p - seg_begin(e))
+  const int* c_pad_start;  // non-null: C is the expert-padded sorted layout (16-bit, mode 0; c_index unused)
   const int* n_tiles;  // number of valid entries in `tiles`
 };
 

@@ -50,7 +50,7 @@ constexpr uint32_t kAtomRowsBytes = 64 * 128;  // one 64-row x 128-byte MN-major
 
 // Development-only knobs (compiled in with -DCVMM_TRACE; absent from the
 // shipped library): bit 8 skips the MMAs, bit 9 / bit 10 skip the A / B loads,
-// bit 14 skips the grad-W epilogue stores.
+// bit 14 skips the epilogue stores.
 #ifdef CVMM_TRACE
 #define CVMM_DBG(flags, bit) (((flags) & (bit)) != 0)
 #else
@@ -77,12 +77,17 @@ enum : int { kTagEmpty = 1, kTagFull = 2, kTagAccFull = 3, kTagAccEmpty = 4, kTa
 // Shared-memory plan of one CTA (offsets from a 1024-byte aligned base):
 //   S operand stages (A tile 16 KiB + B tile BN x 128 B);
 //   barriers: full[S] empty[S] acc_full[2] acc_empty[2] drain idx_full[S] idx_empty[S] ready[S];
-//   epilogue staging: per epilogue warp a 32 x 32 block (rows of 144 B; the
-//   16-byte pad spreads the rows over the shared-memory banks);
+//   epilogue staging (32 KiB, 1024-byte aligned): per epilogue warp either a
+//   32 x 32 block (rows of 144 B; the 16-byte pad spreads the rows over the
+//   shared-memory banks) or two 32-row x 128-byte boxes in the 128-byte
+//   swizzle that TMA stores read;
 //   index ring (grad-W): S slots of the stage's x rows, grad rows and route
 //   weights, bulk-copied from a 16-byte aligned start 0-3 entries before the
 //   stage's first route (`off`).
 constexpr uint32_t kStageRowBytes = 144;
+constexpr uint32_t kStoreBox = 32 * 128;                  // one 32-row x 64-column 16-bit TMA store box
+constexpr uint32_t kStagingBytes = 4 * 2 * kStoreBox;     // >= 4 * 32 * kStageRowBytes
+static_assert(kStagingBytes >= 4 * 32 * kStageRowBytes, "staging too small");
 constexpr int kRingEntries = 72;
 struct IdxSlot {
   int x[kRingEntries];
@@ -99,12 +104,12 @@ struct Smem {
   static constexpr uint32_t stage_bytes = a_bytes + b_bytes;
   static constexpr uint32_t bars = S * stage_bytes;
   static constexpr uint32_t misc = bars + (5 * S + 5) * 8;  // tmem slot, abort flag
-  static constexpr uint32_t staging = (misc + 16 + 127) / 128 * 128;  // 16-byte vector stores, bulk copies
-  static constexpr uint32_t ring = staging + 4 * 32 * kStageRowBytes;
+  static constexpr uint32_t staging = (misc + 16 + 1023) / 1024 * 1024;  // swizzled TMA store boxes
+  static constexpr uint32_t ring = staging + kStagingBytes;
   static constexpr uint32_t used = ring + S * (uint32_t)sizeof(IdxSlot);
   static constexpr uint32_t alloc = used + 1024;  // slack to align the base
   static_assert(alloc <= 232448, "shared memory plan exceeds 227 KiB");
-  static_assert(staging % 128 == 0 && kStageRowBytes % 16 == 0 && ring % 16 == 0, "misaligned smem region");
+  static_assert(staging % 1024 == 0 && kStageRowBytes % 16 == 0 && ring % 16 == 0, "misaligned smem region");
 };
 
 struct Bars {
@@ -363,7 +368,8 @@ __device__ __forceinline__ void mma_loop(const Bars& b, uint64_t* consume, uint8
 template <int BN, int S, bool B_KMAJOR, bool B_TMA, bool A_TMA>
 __global__ void __launch_bounds__(kThreads, 1)
 row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
-                const __grid_constant__ CUtensorMap tmap_a, int flags, int n_n) {
+                const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_c, int flags,
+                int n_n) {
   static_assert(!A_TMA || B_TMA, "TMA row gathers are used together with TMA weight tiles");
   using L = Smem<BN, S>;
   extern __shared__ uint8_t smem_raw[];
@@ -415,9 +421,13 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
             break;
           }
           const uint32_t a_u = ptx::smem_u32(smem + s * L::stage_bytes);
-          if (lane == 0) ptx::mbar_arrive_expect_tx(&bar.full[s], L::a_bytes);
+          if (lane == 0) {
+            if (CVMM_DBG(flags, 512)) ptx::mbar_arrive(&bar.full[s]);
+            else ptx::mbar_arrive_expect_tx(&bar.full[s], L::a_bytes);
+          }
           __syncwarp();
-          if (a_dense) {
+          if (CVMM_DBG(flags, 512)) {
+          } else if (a_dense) {
             // Expert-padded sorted rows: the 128-row A tile is one dense box.
             if (lane == 0) ptx::tma_load_2d(a_u, &tmap_a, &bar.full[s], kb * BK, rows[0]);
           } else if (!CVMM_DBG(flags, 512)) {
@@ -515,12 +525,20 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
     const int ew = warp - 4;
     const int rr = ew * 32 + lane;
     const uint32_t stage = ptx::smem_u32(smem + L::staging) + ew * 32 * kStageRowBytes;
+    // Dense C (expert-padded sorted output): each 32-row x 64-column block is
+    // written to one of the warp's two swizzled boxes and stored by TMA.
+    const bool c_dense = flags & 128;
+    const uint32_t cbox = ptx::smem_u32(smem + L::staging) + ew * 2 * kStoreBox;
+    int cbuf = 0;
+    auto crow_of = [&](const int4& en) -> int64_t {
+      return (c_dense || rr >= en.z) ? -1 : p.c_index[en.y + rr];
+    };
     int4 ent = entry(blockIdx.x);
-    int64_t crow = rr < ent.z ? p.c_index[ent.y + rr] : -1;
+    int64_t crow = crow_of(ent);
     int4 ent_next = entry(blockIdx.x + gridDim.x);
     int local = 0;
     for (int tt = blockIdx.x; tt < total; tt += gridDim.x, ++local) {
-      const int64_t crow_next = rr < ent_next.z ? p.c_index[ent_next.y + rr] : -1;
+      const int64_t crow_next = crow_of(ent_next);
       const int4 ent_after = entry(tt + 2 * gridDim.x);
       const int a = local & 1;
       if (!ptx::mbar_wait_or_abort(&bar.accf[a], (local >> 1) & 1, kTagAccFull, bar.abort)) break;
@@ -530,10 +548,38 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
       const bool row_ok = crow >= 0;
       float wv = 0.f, dot = 0.f;
       if (p.mode == 1 && row_ok) wv = round_to(load_as_float(p.w, p.w_dtype, crow), op);
+      const int prow0 = c_dense ? p.c_pad_start[ent.x] + (int)(ent.y - seg_begin(p.offsets, ent.x)) + ew * 32 : 0;
       for (int ch = 0; ch < BN / 64; ++ch) {
         if (n0 + ch * 64 >= p.N) break;
         float v2[64];
         load_acc64(tmem + ((uint32_t)(ew * 32) << 16) + a * BN + ch * 64, v2);
+        if (c_dense) {
+          if (nkb == 0) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) v2[j] = 0.f;
+          }
+          // The store issued from this box two blocks ago must have read it.
+          if (lane == 0) ptx::bulk_wait_read<1>();
+          __syncwarp();
+          const uint32_t box = cbox + cbuf * kStoreBox;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              w4[i] = (uint32_t)float_to_bits(v2[8 * q + 2 * i], p.c_dtype) |
+                      ((uint32_t)float_to_bits(v2[8 * q + 2 * i + 1], p.c_dtype) << 16);
+            ptx::st_shared_v4(box + lane * 128 + ((uint32_t)(q ^ (lane & 7)) << 4), w4[0], w4[1], w4[2], w4[3]);
+          }
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && !CVMM_DBG(flags, 16384)) {
+            ptx::tma_store_2d(&tmap_c, box, (int)(n0 + ch * 64), prow0);
+            ptx::bulk_commit();
+          }
+          cbuf ^= 1;
+          continue;
+        }
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int64_t nc = n0 + ch * 64 + h * 32;
@@ -552,7 +598,8 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
               v[j] = round_to(av * wv, op);
             }
           }
-          warp_store_block(p.c, p.c_dtype, row_ok ? crow * p.c_ld + nc : -1, v, ncols, stage, c_vec);
+          if (!CVMM_DBG(flags, 16384))
+            warp_store_block(p.c, p.c_dtype, row_ok ? crow * p.c_ld + nc : -1, v, ncols, stage, c_vec);
         }
       }
       if (p.mode == 1 && row_ok) atomicAdd(p.gsel + crow, dot);
@@ -563,6 +610,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
       ent_next = ent_after;
       crow = crow_next;
     }
+    if (c_dense && lane == 0) ptx::bulk_wait_all();
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -588,6 +636,10 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
           break;
         }
         const uint32_t b_u = ptx::smem_u32(smem + s * L::stage_bytes) + L::a_bytes;
+        if (CVMM_DBG(flags, 1024)) {
+          ptx::mbar_arrive(&bar.full[s]);
+          continue;
+        }
         ptx::mbar_arrive_expect_tx(&bar.full[s], L::b_bytes);
         if (B_KMAJOR) {
           ptx::tma_load_3d(b_u, &tmap_b, &bar.full[s], kb * BK, n0, e);
@@ -1032,23 +1084,33 @@ static int row_launch(const RowGemm& p, int64_t max_tiles, int flags, cudaStream
   const bool a_tma = a_dense || (tma && (flags & 1) && (dbg_flags() & 8192) &&
                                  make_rows_map(&amap, p.a, p.op_dtype, p.K, p.a_rows, p.a_ld));
   if (a_dense) flags |= 32;
+  // Dense C: expert-padded sorted 16-bit output written by 32-row TMA boxes.
+  CUtensorMap cmap;
+  memset(&cmap, 0, sizeof(cmap));
+  if (p.c_pad_start) {
+    if (p.mode != 0 || (p.c_dtype != BF16 && p.c_dtype != F16) ||
+        !make_rows_map(&cmap, p.c, p.c_dtype, p.N, p.n_routes + kPadRows * p.n_experts, p.c_ld, 32))
+      return fail(CVMM_ERR_INVALID_ARG,
+                  "padded sorted output needs mode 0, a bf16/fp16 out_dtype and 16-byte aligned rows");
+    flags |= 128;
+  }
   const int64_t work = max_tiles * n_n;
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(work, sm_count()));
   if (a_tma) {
     auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true, true>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
-    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, flags, n_n);
+    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, cmap, flags, n_n);
   } else if (tma) {
     auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true, false>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
-    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, flags, n_n);
+    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, cmap, flags, n_n);
   } else {
     auto kern = row_gemm_kernel<BN, S, BK_MAJOR, false, false>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
-    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, flags, n_n);
+    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, cmap, flags, n_n);
   }
   return check_launch("row_gemm_umma");
 }

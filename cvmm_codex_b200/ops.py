@@ -160,10 +160,12 @@ def _gemm_ws(lib, n_routes, n_experts, dev, m_dim=0, n_dim=0, op_dtype=torch.bfl
 
 def forward(x: torch.Tensor, sel_index: torch.Tensor, offsets: torch.Tensor, keys: torch.Tensor,
             out_index: Optional[torch.Tensor], out_dtype: torch.dtype,
-            op_dtype: torch.dtype, x_pad_start: Optional[torch.Tensor] = None) -> torch.Tensor:
+            op_dtype: torch.dtype, x_pad_start: Optional[torch.Tensor] = None,
+            out_pad_start: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Y[row_p] = x[sel_index[p]] @ keys[e_p] for every sorted route p; Y is [R, N]
     (reference cvmm_triton, cvmm.py:815-867). With x_pad_start, x is the
-    expert-padded sorted layout from sort_rows_padded."""
+    expert-padded sorted layout from sort_rows_padded; with out_pad_start, Y is
+    returned in that layout ([R + E*PAD_ROWS, N], read through padded_route_rows)."""
     _require_cuda(x, sel_index, offsets, keys, out_index)
     lib = _lib.load()
     x2 = _rows(x)
@@ -171,7 +173,8 @@ def forward(x: torch.Tensor, sel_index: torch.Tensor, offsets: torch.Tensor, key
     E, K, N = keys.shape
     if x2.shape[1] != K:
         raise ValueError(f"cvmm: x feature size {x2.shape[1]} != keys.shape[1] {K}")
-    out = torch.empty((n_routes, N), dtype=out_dtype, device=x.device)
+    out_rows = n_routes + E * PAD_ROWS if out_pad_start is not None else n_routes
+    out = torch.empty((out_rows, N), dtype=out_dtype, device=x.device)
     ws = _gemm_ws(lib, n_routes, E, x.device)
     with _Device(x.device) as stream:
         rc = _invoke("cvmm_forward", lib.cvmm_forward, ptr(x2), dtype_code(x2.dtype), x2.shape[0], x2.stride(0),
@@ -179,13 +182,15 @@ def forward(x: torch.Tensor, sel_index: torch.Tensor, offsets: torch.Tensor, key
                               ptr(keys), dtype_code(keys.dtype), E, K, N,
                               keys.stride(0), keys.stride(1), keys.stride(2),
                               ptr(out), dtype_code(out_dtype), out.stride(0), dtype_code(op_dtype),
-                              ptr(x_pad_start), ptr(ws), ws.numel(), stream)
+                              ptr(x_pad_start), ptr(out_pad_start), ptr(ws), ws.numel(), stream)
     check(rc, "cvmm_forward")
     return out
 
 
-def weighted_combine(y: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
-    """out[t] = sum_j w[t, j] * y[t*k + j] with w cast to y's dtype (cvmm.py:1543-1545)."""
+def weighted_combine(y: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype,
+                     y_rows: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[t] = sum_j w[t, j] * y[row(t*k + j)] with w cast to y's dtype (cvmm.py:1543-1545);
+    row(r) = y_rows[r] (padded sorted y) or r."""
     _require_cuda(y, w)
     lib = _lib.load()
     k = w.shape[-1]
@@ -196,21 +201,22 @@ def weighted_combine(y: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype) -
     out = torch.empty((T, N), dtype=out_dtype, device=y.device)
     with _Device(y.device) as stream:
         rc = _invoke("cvmm_weighted_combine", lib.cvmm_weighted_combine, ptr(y2), dtype_code(y2.dtype), ptr(w2), dtype_code(w2.dtype),
-                                       ptr(out), dtype_code(out_dtype), T, k, N, stream)
+                                       ptr(out), dtype_code(out_dtype), T, k, N, ptr(y_rows), stream)
     check(rc, "cvmm_weighted_combine")
     return out
 
 
-def sum_routes(src: torch.Tensor, top_k: int, out_dtype: torch.dtype) -> torch.Tensor:
-    """out[t] = sum_j src[t*k + j] (cvmm.py:1223)."""
+def sum_routes(src: torch.Tensor, top_k: int, out_dtype: torch.dtype,
+               src_rows: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[t] = sum_j src[row(t*k + j)] (cvmm.py:1223); row(r) = src_rows[r] or r."""
     lib = _lib.load()
     d = src.shape[-1]
     s2 = src.reshape(-1, d).contiguous()
-    T = s2.shape[0] // top_k
+    T = (s2.shape[0] if src_rows is None else src_rows.numel()) // top_k
     out = torch.empty((T, d), dtype=out_dtype, device=src.device)
     with _Device(src.device) as stream:
         rc = _invoke("cvmm_sum_routes", lib.cvmm_sum_routes, ptr(s2), dtype_code(s2.dtype), ptr(out), dtype_code(out_dtype),
-                                 T, int(top_k), d, stream)
+                                 T, int(top_k), d, ptr(src_rows), stream)
     check(rc, "cvmm_sum_routes")
     return out
 
@@ -218,19 +224,22 @@ def sum_routes(src: torch.Tensor, top_k: int, out_dtype: torch.dtype) -> torch.T
 def backward_x(g: torch.Tensor, g_index: Optional[torch.Tensor], g_div: int, out_index: torch.Tensor,
                offsets: torch.Tensor, keys: torch.Tensor, out_dtype: torch.dtype,
                op_dtype: torch.dtype, w: Optional[torch.Tensor] = None,
-               x: Optional[torch.Tensor] = None, g_pad_start: Optional[torch.Tensor] = None):
+               x: Optional[torch.Tensor] = None, g_pad_start: Optional[torch.Tensor] = None,
+               out_pad_start: Optional[torch.Tensor] = None, n_routes: Optional[int] = None):
     """Route gradients a_p = g[g_index[p] // g_div] @ keys[e_p]^T stored at out_index[p].
 
     Plain (w is None): returns out [R, d_in]. Weighted route-shaped input (w and x
     given): returns (grad_x [R, d_in], grad_sel fp32 [R]) with the reference's
     fused rounding (cvmm.py:1073-1105). With g_pad_start, g is the expert-padded
-    sorted layout from sort_rows_padded and g_index is unused."""
+    sorted layout from sort_rows_padded and g_index is unused; with out_pad_start
+    the output is returned in that layout (out_index may be None, then pass n_routes)."""
     _require_cuda(g, g_index, out_index, offsets, keys, w, x)
     lib = _lib.load()
     g2 = _rows(g)
-    n_routes = out_index.numel()
+    n_routes = out_index.numel() if n_routes is None else int(n_routes)
     E, K, N = keys.shape
-    out = torch.empty((n_routes, K), dtype=out_dtype, device=g.device)
+    out_rows = n_routes + E * PAD_ROWS if out_pad_start is not None else n_routes
+    out = torch.empty((out_rows, K), dtype=out_dtype, device=g.device)
     mode = 0
     gsel = None
     x2 = None
@@ -249,7 +258,7 @@ def backward_x(g: torch.Tensor, g_index: Optional[torch.Tensor], g_div: int, out
                                  ptr(w2), dtype_code(w2.dtype) if w2 is not None else 0,
                                  ptr(x2), dtype_code(x2.dtype) if x2 is not None else 0,
                                  x2.stride(0) if x2 is not None else 0, ptr(gsel),
-                                 dtype_code(op_dtype), ptr(g_pad_start), ptr(ws), ws.numel(), stream)
+                                 dtype_code(op_dtype), ptr(g_pad_start), ptr(out_pad_start), ptr(ws), ws.numel(), stream)
     check(rc, "cvmm_backward_x")
     return out if mode == 0 else (out, gsel)
 
@@ -314,6 +323,24 @@ def sort_rows_padded(src: torch.Tensor, index: torch.Tensor, div: int, sorted_se
                      ptr(dst), dtype_code(dtype), ptr(pstart), stream)
     check(rc, "cvmm_sort_rows_padded")
     return dst, pstart
+
+
+def padded_route_rows(route: torch.Tensor, sorted_sel: torch.Tensor, offsets: torch.Tensor,
+                      pad_start: torch.Tensor) -> torch.Tensor:
+    """rows[route[p]] = pad_start[e] + p - seg_begin(e): where each route's row
+    lives in the expert-padded sorted layout (int32 [n_routes])."""
+    _require_cuda(route, sorted_sel, offsets, pad_start)
+    lib = _lib.load()
+    n = route.numel()
+    ss = sorted_sel.reshape(-1)
+    if ss.dtype != torch.int32:
+        ss = ss.to(torch.int32)
+    rows = torch.empty(n, dtype=torch.int32, device=route.device)
+    with _Device(route.device) as stream:
+        rc = _invoke("cvmm_padded_route_rows", lib.cvmm_padded_route_rows, ptr(route), ptr(ss), ptr(offsets),
+                     ptr(pad_start), n, offsets.numel(), ptr(rows), stream)
+    check(rc, "cvmm_padded_route_rows")
+    return rows
 
 
 def weighted_token_backward(route_grad: torch.Tensor, w: torch.Tensor, x: torch.Tensor,

@@ -52,7 +52,7 @@ typedef struct CUstream_st* cvmm_stream_t; /* == cudaStream_t */
 #define CVMM_DEV_BAD_INDEX 2
 
 /* ABI version of this header; bumped on any signature change. */
-int cvmm_abi_version(void);  /* 3 */
+int cvmm_abi_version(void);  /* 4 */
 
 /* Message for the last failed call on the calling host thread. */
 const char* cvmm_last_error(void);
@@ -128,19 +128,27 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld,
                  int64_t n_routes, const void* keys, int keys_dtype, int64_t n_experts,
                  int64_t k_dim, int64_t n_dim, int64_t ks_e, int64_t ks_k, int64_t ks_n,
                  void* out, int out_dtype, int64_t out_ld, int op_dtype,
-                 const int32_t* x_pad_start, void* workspace, size_t workspace_bytes,
-                 cvmm_stream_t stream);
+                 const int32_t* x_pad_start, const int32_t* out_pad_start, void* workspace,
+                 size_t workspace_bytes, cvmm_stream_t stream);
 /* With x_pad_start != NULL, x is the expert-padded sorted layout made by
  * cvmm_sort_rows_padded: the x row of sorted position p is then
  * x_pad_start[e] + p - seg_begin(e), x_rows is ignored, and sel_index only
  * names the output rows (when out_index is NULL). bf16/fp16 op_dtype with
- * x_dtype == op_dtype only. */
+ * x_dtype == op_dtype only.
+ * With out_pad_start != NULL, out is written in the expert-padded sorted
+ * layout instead (row of sorted position p: out_pad_start[e] + p - seg_begin(e),
+ * n_routes + n_experts * CVMM_PAD_ROWS rows, padding rows included) by dense
+ * tensor-memory-to-TMA stores; out_index is then ignored. bf16/fp16 out_dtype
+ * and op_dtype, 16-byte aligned rows. Read it back per route through
+ * cvmm_padded_route_rows. */
 
 /* Weighted combine of the forward: out[t] = cast( sum_j cast_y(w[t,j]) * y[t*top_k+j] ),
  * fp32 accumulate. Replaces the bmm at cvmm.py:1543-1545. */
 int cvmm_weighted_combine(const void* y, int y_dtype, const void* w, int w_dtype,
                           void* out, int out_dtype, int64_t n_tokens, int64_t top_k,
-                          int64_t n_dim, cvmm_stream_t stream);
+                          int64_t n_dim, const int32_t* y_rows, cvmm_stream_t stream);
+/* y_rows != NULL: the y row of route r is y_rows[r] (e.g. an expert-padded
+ * sorted forward output with the map of cvmm_padded_route_rows); NULL: r. */
 
 /* ------------------------------------------------------------------------
  * Backward grad-input GEMM. Replaces cvmm_grouped_bwd_x_kernel
@@ -166,8 +174,10 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
                     int64_t k_dim, int64_t n_dim, int64_t ks_e, int64_t ks_k, int64_t ks_n,
                     void* out, int out_dtype, int64_t out_ld, int mode, const void* w,
                     int w_dtype, const void* x, int x_dtype, int64_t x_ld, float* gsel,
-                    int op_dtype, const int32_t* g_pad_start, void* workspace,
-                    size_t workspace_bytes, cvmm_stream_t stream);
+                    int op_dtype, const int32_t* g_pad_start, const int32_t* out_pad_start,
+                    void* workspace, size_t workspace_bytes, cvmm_stream_t stream);
+/* out_pad_start != NULL (mode 0 only): out is written in the expert-padded
+ * sorted layout as in cvmm_forward, out_index is ignored. */
 
 /* Backward grad-weight. Replaces cvmm_grouped_bwd_w_gather_x_kernel /
  * cvmm_grouped_bwd_w_kernel / cvmm_grouped_bwd_w_weighted_kernel
@@ -217,7 +227,19 @@ int cvmm_sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const 
 /* Sum over the top-k routes of each token: out[t] = cast( sum_j src[t*top_k+j] ),
  * fp32 accumulate. Replaces grouped_x.view(..., top_k, d).sum(-2) (cvmm.py:1223). */
 int cvmm_sum_routes(const void* src, int src_dtype, void* out, int out_dtype,
-                    int64_t n_tokens, int64_t top_k, int64_t d, cvmm_stream_t stream);
+                    int64_t n_tokens, int64_t top_k, int64_t d, const int32_t* src_rows,
+                    cvmm_stream_t stream);
+/* src_rows != NULL: the src row of route r is src_rows[r]; NULL: r. */
+
+/* Route -> row map of the expert-padded sorted layout:
+ *   rows[route[p]] = pad_start[e] + p - seg_begin(e)   for sorted p,
+ * with route[p] the route id of sorted position p (out_index, or sel_index
+ * for route-indexed selectors). Lets cvmm_sum_routes / cvmm_weighted_combine
+ * read outputs written with out_pad_start. No reference counterpart: the
+ * reference scatters outputs straight to route order (cvmm.py:213-218). */
+int cvmm_padded_route_rows(const int64_t* route, const int32_t* sorted_sel, const int64_t* offsets,
+                           const int32_t* pad_start, int64_t n_routes, int64_t n_experts,
+                           int32_t* rows, cvmm_stream_t stream);
 
 /* Token-input weighted backward tail (cvmm.py:1737-1746):
  *   grad_x[t]      = cast( sum_j cast_r(w[t,j]) * route_grad[t,j] )       (if grad_x)
