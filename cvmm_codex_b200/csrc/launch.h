@@ -33,10 +33,13 @@ inline size_t dtype_size(int d) {
 }
 
 // Entry points implemented across the .cu files.
-size_t sel_prepare_workspace_size(int64_t n);
+// min_chunk: fewest routes per radix-sort warp chunk (128 by default; the
+// allocation-free entry uses 1024 to keep its static scratch small).
+constexpr int64_t kSelMinChunk = 128;
+size_t sel_prepare_workspace_size(int64_t n, int64_t min_chunk = kSelMinChunk);
 int sel_prepare(const void* sel, int sel_dtype, int64_t n, int64_t top_k, int route_input,
                 int32_t* raw_sel, int32_t* sorted_sel, int64_t* sel_index, int64_t* out_index,
-                void* workspace, size_t ws_bytes, cudaStream_t stream);
+                void* workspace, size_t ws_bytes, cudaStream_t stream, int64_t min_chunk = kSelMinChunk);
 int expert_offsets(const int32_t* sorted, int64_t n, int64_t n_experts, int64_t* offsets,
                    cudaStream_t stream);
 

@@ -9,7 +9,8 @@
 // general sort we run an LSD radix sort with 11-bit digits over the biased key
 // range actually present (max - min). For every realistic expert count
 // (< 2048 experts) that is ONE pass of histogram -> scan -> scatter. Each warp
-// owns a chunk of 1024 consecutive routes; the scatter ranks equal digits
+// owns a chunk of consecutive routes (128 or more, at most 2048 chunks, so
+// that even 64k routes spread over ~128 CTAs); the scatter ranks equal digits
 // inside a warp with __match_any_sync, which keeps the sort stable without any
 // cross-warp ordering inside a CTA. Extra passes (keys spread over > 2048
 // values) are launched unconditionally but exit on the device when the key
@@ -23,7 +24,7 @@ namespace sel {
 
 constexpr int kDigitBits = 11;
 constexpr int kBins = 1 << kDigitBits;  // 2048
-constexpr int kChunk = 1024;            // routes per warp
+constexpr int64_t kMaxChunks = 2048;    // bounds the single-CTA scan to kBins * kMaxChunks counts
 constexpr int kWarpsPerCta = 4;
 constexpr int kMaxPasses = 3;           // 33 bits >= 32-bit key range
 
@@ -78,7 +79,7 @@ __device__ __forceinline__ unsigned int digit_of(int32_t key, unsigned int mn, i
 // counts layout: counts[bin * n_chunks + chunk] so that one exclusive scan in
 // memory order yields every (bin, chunk) base position.
 __global__ void __launch_bounds__(kWarpsPerCta * 32)
-hist_kernel(const int32_t* __restrict__ keys, int64_t n, int64_t n_chunks,
+hist_kernel(const int32_t* __restrict__ keys, int64_t n, int64_t n_chunks, int64_t chunk_len,
             const Header* __restrict__ h, int shift, int* __restrict__ counts) {
   if (!pass_needed(h, shift)) return;
   __shared__ int hist[kWarpsPerCta][kBins];
@@ -90,32 +91,56 @@ hist_kernel(const int32_t* __restrict__ keys, int64_t n, int64_t n_chunks,
   for (int b = lane; b < nb; b += 32) my[b] = 0;
   __syncwarp();
   if (chunk < n_chunks) {
-    const int64_t beg = chunk * kChunk;
-    const int64_t end = min(beg + kChunk, n);
+    const int64_t beg = chunk * chunk_len;
+    const int64_t end = min(beg + chunk_len, n);
     for (int64_t i = beg + lane; i < end; i += 32) atomicAdd(&my[digit_of(keys[i], mn, shift)], 1);
     __syncwarp();
     for (int b = lane; b < nb; b += 32) counts[(int64_t)b * n_chunks + chunk] = my[b];
   }
 }
 
-// Single-CTA exclusive scan over nb * n_chunks counts, in place.
+// Single-CTA exclusive scan over nb * n_chunks counts, in place. Thread t
+// owns a contiguous, 16-byte aligned slice; it reads the slice in batches of
+// kScanBatch counts with int4 loads all in flight (the slice sum), the CTA
+// scans the 1024 slice sums, and the slice is rewritten the same way.
+constexpr int kScanBatch = 32;
+
+__device__ __forceinline__ void scan_load(const int* __restrict__ c, int64_t i, int64_t end, int (&v)[kScanBatch]) {
+#pragma unroll
+  for (int q = 0; q < kScanBatch / 4; ++q) {
+    const int64_t k = i + 4 * q;
+    if (k + 3 < end) {
+      const int4 x = *reinterpret_cast<const int4*>(c + k);
+      v[4 * q] = x.x; v[4 * q + 1] = x.y; v[4 * q + 2] = x.z; v[4 * q + 3] = x.w;
+    } else {
+#pragma unroll
+      for (int r = 0; r < 4; ++r) v[4 * q + r] = k + r < end ? c[k + r] : 0;
+    }
+  }
+}
+
 __global__ void __launch_bounds__(1024)
 scan_kernel(int* __restrict__ counts, int64_t n_chunks, const Header* __restrict__ h, int shift) {
   if (!pass_needed(h, shift)) return;
   const int64_t total = (int64_t)n_bins(h, shift) * n_chunks;
   const int t = threadIdx.x;
-  const int64_t per = (total + blockDim.x - 1) / blockDim.x;
+  const int64_t per = ((total + blockDim.x - 1) / blockDim.x + 3) & ~(int64_t)3;
   const int64_t beg = min((int64_t)t * per, total), end = min(beg + per, total);
+  int v[kScanBatch];
   int local = 0;
-  for (int64_t i = beg; i < end; ++i) local += counts[i];
+  for (int64_t b = beg; b < end; b += kScanBatch) {
+    scan_load(counts, b, end, v);
+#pragma unroll
+    for (int j = 0; j < kScanBatch; ++j) local += v[j];
+  }
   __shared__ int warp_sums[32];
-  int v = local;
+  int x = local;
   const int lane = t & 31, warp = t >> 5;
   for (int o = 1; o < 32; o <<= 1) {
-    int y = __shfl_up_sync(0xffffffffu, v, o);
-    if (lane >= o) v += y;
+    int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
   }
-  if (lane == 31) warp_sums[warp] = v;
+  if (lane == 31) warp_sums[warp] = x;
   __syncthreads();
   if (warp == 0) {
     int s = lane < (int)(blockDim.x >> 5) ? warp_sums[lane] : 0;
@@ -126,18 +151,33 @@ scan_kernel(int* __restrict__ counts, int64_t n_chunks, const Header* __restrict
     warp_sums[lane] = s;  // inclusive over warps
   }
   __syncthreads();
-  int run = v - local + (warp > 0 ? warp_sums[warp - 1] : 0);  // exclusive prefix
-  for (int64_t i = beg; i < end; ++i) {
-    int c = counts[i];
-    counts[i] = run;
-    run += c;
+  int run = x - local + (warp > 0 ? warp_sums[warp - 1] : 0);  // exclusive prefix
+  for (int64_t b = beg; b < end; b += kScanBatch) {
+    if (per > kScanBatch) scan_load(counts, b, end, v);  // else v still holds the slice
+#pragma unroll
+    for (int j = 0; j < kScanBatch; ++j) {
+      const int c = v[j];
+      v[j] = run;
+      run += c;
+    }
+#pragma unroll
+    for (int q = 0; q < kScanBatch / 4; ++q) {
+      const int64_t k = b + 4 * q;
+      if (k + 3 < end) {
+        *reinterpret_cast<int4*>(counts + k) = make_int4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+          if (k + r < end) counts[k + r] = v[4 * q + r];
+      }
+    }
   }
 }
 
 // Stable scatter. Pass 0 reads keys = raw_sel with implicit values = route id.
 __global__ void __launch_bounds__(kWarpsPerCta * 32)
 scatter_kernel(const int32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_in,
-               int64_t n, int64_t n_chunks, const Header* __restrict__ h, int shift,
+               int64_t n, int64_t n_chunks, int64_t chunk_len, const Header* __restrict__ h, int shift,
                const int* __restrict__ base, int32_t* __restrict__ keys_out,
                int32_t* __restrict__ vals_out, int32_t* __restrict__ sorted_sel,
                int64_t* __restrict__ sel_index, int64_t* __restrict__ out_index,
@@ -153,8 +193,8 @@ scatter_kernel(const int32_t* __restrict__ keys_in, const int32_t* __restrict__ 
   int* my = ctr[warp];
   for (int b = lane; b < nb; b += 32) my[b] = base[(int64_t)b * n_chunks + chunk];
   __syncwarp();
-  const int64_t beg = chunk * kChunk;
-  const int64_t end = min(beg + kChunk, n);
+  const int64_t beg = chunk * chunk_len;
+  const int64_t end = min(beg + chunk_len, n);
   const unsigned int lt_mask = (1u << lane) - 1u;
   for (int64_t i0 = beg; i0 < end; i0 += 32) {
     const int64_t i = i0 + lane;
@@ -185,24 +225,39 @@ scatter_kernel(const int32_t* __restrict__ keys_in, const int32_t* __restrict__ 
   }
 }
 
-// offsets[e] = #sorted keys <= e (upper bound), the reference's inclusive
-// end offsets (cvmm.py:315-335).
+// offsets[e] = #sorted keys <= e, the reference's inclusive end offsets
+// (cvmm.py:315-335). One thread per sorted position i writes the experts in
+// [sorted[i], sorted[i+1]) (clipped to [0, n_experts)) with i + 1; thread -1
+// (i.e. position 0's extra work) writes the experts below sorted[0] with 0, and
+// the last position the experts from sorted[n-1] on with n. Every expert is
+// written exactly once, with no search.
 __global__ void offsets_kernel(const int32_t* __restrict__ sorted, int64_t n, int64_t n_experts,
                                int64_t* __restrict__ offsets) {
-  int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (e >= n_experts) return;
-  int64_t lo = 0, hi = n;
-  while (lo < hi) {
-    int64_t mid = (lo + hi) >> 1;
-    if ((int64_t)sorted[mid] <= e) lo = mid + 1; else hi = mid;
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (n == 0) {
+    if (i < n_experts) offsets[i] = 0;
+    return;
   }
-  offsets[e] = lo;
+  if (i >= n) return;
+  const int64_t a = sorted[i];
+  if (i == 0)
+    for (int64_t e = 0; e < min(a, n_experts); ++e) offsets[e] = 0;
+  const int64_t b = i + 1 < n ? (int64_t)sorted[i + 1] : n_experts;
+  for (int64_t e = max(a, (int64_t)0); e < min(b, n_experts); ++e) offsets[e] = i + 1;
 }
 
 }  // namespace sel
 
-size_t sel_prepare_workspace_size(int64_t n) {
-  const int64_t n_chunks = (n + sel::kChunk - 1) / sel::kChunk;
+namespace sel {
+// Routes per warp chunk: at least min_chunk, a multiple of 32, at most kMaxChunks chunks.
+static int64_t chunk_len(int64_t n, int64_t min_chunk) {
+  int64_t c = std::max<int64_t>(min_chunk, (n + kMaxChunks - 1) / kMaxChunks);
+  return (c + 31) / 32 * 32;
+}
+}  // namespace sel
+
+size_t sel_prepare_workspace_size(int64_t n, int64_t min_chunk) {
+  const int64_t n_chunks = (n + sel::chunk_len(n, min_chunk) - 1) / sel::chunk_len(n, min_chunk);
   size_t bytes = 256;                                             // header
   bytes += align_up((size_t)n_chunks * sel::kBins * sizeof(int), 256);  // counts
   bytes += 4 * align_up((size_t)n * sizeof(int32_t), 256);         // ping-pong keys/vals
@@ -211,7 +266,7 @@ size_t sel_prepare_workspace_size(int64_t n) {
 
 int sel_prepare(const void* sel_ptr, int sel_dtype, int64_t n, int64_t top_k, int route_input,
                 int32_t* raw_sel, int32_t* sorted_sel, int64_t* sel_index, int64_t* out_index,
-                void* workspace, size_t ws_bytes, cudaStream_t stream) {
+                void* workspace, size_t ws_bytes, cudaStream_t stream, int64_t min_chunk) {
   if (n < 0 || top_k <= 0) return fail(CVMM_ERR_INVALID_ARG, "cvmm_sel_prepare: bad n_routes/top_k");
   if (sel_dtype != CVMM_I64 && sel_dtype != CVMM_I32)
     return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_sel_prepare: sel must be int64 or int32");
@@ -219,10 +274,11 @@ int sel_prepare(const void* sel_ptr, int sel_dtype, int64_t n, int64_t top_k, in
   if (!sel_ptr || !raw_sel || !sorted_sel || !sel_index || (!route_input && !out_index))
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_sel_prepare: null pointer");
   if (n > (int64_t)INT32_MAX) return fail(CVMM_ERR_INVALID_ARG, "cvmm_sel_prepare: too many routes");
-  if (!workspace || ws_bytes < sel_prepare_workspace_size(n))
+  if (!workspace || ws_bytes < sel_prepare_workspace_size(n, min_chunk))
     return fail(CVMM_ERR_WORKSPACE, "cvmm_sel_prepare: workspace too small");
 
-  const int64_t n_chunks = (n + sel::kChunk - 1) / sel::kChunk;
+  const int64_t clen = sel::chunk_len(n, min_chunk);
+  const int64_t n_chunks = (n + clen - 1) / clen;
   char* ws = static_cast<char*>(workspace);
   sel::Header* h = reinterpret_cast<sel::Header*>(ws);
   ws += 256;
@@ -245,10 +301,10 @@ int sel_prepare(const void* sel_ptr, int sel_dtype, int64_t n, int64_t top_k, in
     const int shift = p * sel::kDigitBits;
     int32_t* kout = buf[(p & 1) * 2];
     int32_t* vout = buf[(p & 1) * 2 + 1];
-    sel::hist_kernel<<<cta, sel::kWarpsPerCta * 32, 0, stream>>>(kin, n, n_chunks, h, shift, counts);
+    sel::hist_kernel<<<cta, sel::kWarpsPerCta * 32, 0, stream>>>(kin, n, n_chunks, clen, h, shift, counts);
     sel::scan_kernel<<<1, 1024, 0, stream>>>(counts, n_chunks, h, shift);
     sel::scatter_kernel<<<cta, sel::kWarpsPerCta * 32, 0, stream>>>(
-        kin, vin, n, n_chunks, h, shift, counts, kout, vout, sorted_sel, sel_index, out_index,
+        kin, vin, n, n_chunks, clen, h, shift, counts, kout, vout, sorted_sel, sel_index, out_index,
         top_k, route_input);
     kin = kout;
     vin = vout;
@@ -260,8 +316,8 @@ int expert_offsets(const int32_t* sorted, int64_t n, int64_t n_experts, int64_t*
                    cudaStream_t stream) {
   if (n < 0 || n_experts <= 0 || !offsets || (n > 0 && !sorted))
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_expert_offsets: bad arguments");
-  int grid = (int)((n_experts + 255) / 256);
-  sel::offsets_kernel<<<grid, 256, 0, stream>>>(sorted, n, n_experts, offsets);
+  const int64_t work = n > 0 ? n : n_experts;
+  sel::offsets_kernel<<<(unsigned)((work + 255) / 256), 256, 0, stream>>>(sorted, n, n_experts, offsets);
   return check_launch("cvmm_expert_offsets");
 }
 

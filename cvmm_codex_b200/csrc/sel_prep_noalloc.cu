@@ -17,8 +17,10 @@ namespace cvmm {
 // per-chunk histograms and the ping-pong key/value buffers. Every GPU that
 // loads the library keeps this much memory until the process exits.
 constexpr int64_t kNoAllocMaxRoutes = CVMM_NOALLOC_MAX_ROUTES;
+constexpr int64_t kNoAllocChunk = 1024;  // routes per radix-sort warp chunk
 constexpr size_t kNoAllocScratchBytes =
-    256 + ((kNoAllocMaxRoutes + 1023) / 1024) * 2048 * sizeof(int) + 4 * kNoAllocMaxRoutes * sizeof(int32_t);
+    256 + ((kNoAllocMaxRoutes + kNoAllocChunk - 1) / kNoAllocChunk) * 2048 * sizeof(int) +
+    4 * kNoAllocMaxRoutes * sizeof(int32_t);
 
 static __device__ __align__(256) unsigned char g_sel_scratch[kNoAllocScratchBytes];
 
@@ -54,7 +56,7 @@ extern "C" int cvmm_sel_prepare_noalloc(const void* sel, int sel_dtype, int64_t 
     return fail(CVMM_ERR_INVALID_ARG,
                 "cvmm_sel_prepare_noalloc: n_routes exceeds CVMM_NOALLOC_MAX_ROUTES (65536); "
                 "use cvmm_sel_prepare with a caller-provided workspace");
-  if (sel_prepare_workspace_size(n_routes < 0 ? 0 : n_routes) > kNoAllocScratchBytes)
+  if (sel_prepare_workspace_size(n_routes < 0 ? 0 : n_routes, kNoAllocChunk) > kNoAllocScratchBytes)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_sel_prepare_noalloc: scratch too small for n_routes");
   void* scratch = nullptr;
   int rc = scratch_for_current_device(&scratch);
@@ -62,5 +64,5 @@ extern "C" int cvmm_sel_prepare_noalloc(const void* sel, int sel_dtype, int64_t 
   // sel_prepare zeroes the part of the scratch that must start at zero (the
   // key-range header) on every call; the rest is fully written before use.
   return sel_prepare(sel, sel_dtype, n_routes, top_k, route_input, raw_sel, sorted_sel, sel_index, out_index,
-                     scratch, kNoAllocScratchBytes, reinterpret_cast<cudaStream_t>(stream));
+                     scratch, kNoAllocScratchBytes, reinterpret_cast<cudaStream_t>(stream), kNoAllocChunk);
 }
