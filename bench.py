@@ -273,7 +273,7 @@ def run_ours(args, rank, world, local_rank):
             res["e2e"] = {"value": round(flops / (e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                           "ms_per_step": round(e_ms, 4), "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo}
         if with_roofline:
-            res["roofline"] = roofline(w, res["per_call"], args.steps, pk)
+            res["roofline"], res["roofline_calls"] = roofline(w, res["per_call"], rec.steps, pk)
         return res
 
     main = measure(args.workload, not args.no_e2e, True)
@@ -293,7 +293,7 @@ def run_ours(args, rank, world, local_rank):
         "clocks": main["clocks"],
         "gpu_launches": main["launches"] * args.steps,
         "roofline": main["roofline"],
-        "per_call_ms": {k: round(v[1] / max(v[0], 1), 5) for k, v in main["per_call"].items()},
+        "roofline_calls": main["roofline_calls"],
     }
     if "e2e" in main:
         line["e2e"] = main["e2e"]
@@ -310,27 +310,78 @@ def run_ours(args, rank, world, local_rank):
     return line
 
 
-GEMM_CALLS = ("cvmm_forward", "cvmm_backward_x", "cvmm_backward_w")
+def call_work(w, name):
+    """Algorithmic (bytes, flops) of ONE call of native entry point `name` in a
+    step of workload `w`: the bytes the call must move to and from HBM with
+    16-bit activations (inputs read once, outputs written once, the padding of
+    the sorted layout not counted) and its multiply-add FLOPs."""
+    R, T, E, di, do = w.R, w.T, w.E, w.d_in, w.d_out
+    wts = E * di * do
+    gemm = 2.0 * R * di * do
+    if name == "cvmm_sel_prepare":
+        return R * 8 + R * (4 + 4 + 8 + (0 if w.route_input else 8)), 0.0
+    if name == "cvmm_expert_offsets":
+        return R * 4 + E * 8, 0.0
+    if name == "cvmm_cast":
+        return wts * (4 + 2), 0.0
+    if name == "cvmm_sort_rows_padded":  # mean of the x copy and the grad copy
+        x_copy = (R if w.route_input else T) * di * 2 + R * di * 2
+        g_copy = (T * do * 2 + R * 4 if w.weighted else R * do * 2) + R * do * 2
+        return (x_copy + g_copy) / 2, 0.0
+    if name == "cvmm_padded_route_rows":
+        return R * 16, 0.0
+    if name == "cvmm_forward":
+        return R * di * 2 + wts * 2 + R * do * 2, gemm
+    if name == "cvmm_backward_w":
+        return R * di * 2 + R * do * 2 + wts * 4, gemm
+    if name == "cvmm_backward_x":
+        if w.weighted:  # token grads, route weights, route x for the sel-weight grad
+            return T * do * 2 + R * 4 + R * di * 2 + wts * 2 + R * di * 2 + R * 4, gemm
+        return R * do * 2 + wts * 2 + R * di * 2, gemm
+    if name == "cvmm_sum_routes":
+        return R * di * 2 + T * di * 2, 0.0
+    if name == "cvmm_weighted_combine":
+        return R * do * 2 + R * 4 + T * do * 2, 0.0
+    return 0.0, 0.0
+
+
+def dram_traffic(workload, call):
+    """DRAM bytes (read + write) per launch of the call's main kernel from the
+    committed ncu capture summary, or None."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)["workloads"][workload].get(call)
+    except (OSError, KeyError, ValueError):
+        return None
 
 
 def roofline(w, per_call, steps, pk):
-    """Dominant native call of the step; algorithmic FLOPs per launch for the
-    GEMMs (2*R*d_in*d_out), algorithmic bytes for the memory-bound kernels."""
-    name, (calls, total) = max(per_call.items(), key=lambda kv: kv[1][1])
-    avg_ms = total / max(calls, 1)
+    """Per native call: algorithmic bytes and FLOPs over its CUDA-event time;
+    the bound is whichever of HBM (measured copy bandwidth) and the tensor
+    cores (measured sustained bf16) allows the shorter time. Returns the entry
+    of the call with the largest share of the step and the whole table."""
+    table = {}
     step_total = sum(v[1] for v in per_call.values())
-    share = total / step_total if step_total else None
-    if name in GEMM_CALLS:
-        work = 2.0 * w.R * w.d_in * w.d_out
-        achieved = work / (avg_ms * 1e-3) / 1e12
-        peak = pk["bf16_tflops_sustained"]
-        return {"kernel": name, "bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
-                "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
-                "avg_ms": round(avg_ms, 5), "share_of_native_time": round(share, 3) if share else None,
-                "peak_source": pk["source"] + " bf16 sustained"}
-    achieved = 0.0
-    return {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-            "frac": None, "traffic": None, "avg_ms": round(avg_ms, 5)}
+    for name, (calls, total) in per_call.items():
+        avg_ms = total / max(calls, 1)
+        nbytes, flops = call_work(w, name)
+        t_hbm = nbytes / (pk["hbm_gbs"] * 1e9)
+        t_tc = flops / (pk["bf16_tflops_sustained"] * 1e12)
+        if flops and t_tc >= t_hbm:
+            ach, peak, unit, bound = flops / (avg_ms * 1e-3) / 1e12, pk["bf16_tflops_sustained"], "TFLOP/s", "tensor"
+        else:
+            ach, peak, unit, bound = nbytes / (avg_ms * 1e-3) / 1e9, pk["hbm_gbs"], "GB/s", "hbm"
+        table[name] = {"bound": bound, "achieved": round(ach, 2), "peak": peak, "unit": unit,
+                       "frac": round(ach / peak, 4), "avg_ms": round(avg_ms, 5), "calls_per_step": calls // max(steps, 1),
+                       "share": round(total / step_total, 3) if step_total else None,
+                       "algorithmic_bytes": int(nbytes), "flops": int(flops)}
+    name = max(per_call, key=lambda k: per_call[k][1])
+    top = dict(table[name])
+    top["kernel"] = name
+    top["traffic"] = dram_traffic(w.name, name)
+    top["peak_source"] = f"{pk['source']} ({'hbm copy' if top['bound'] == 'hbm' else 'bf16 sustained'})"
+    return top, table
 
 
 # ------------------------------------------------------------------ CPU baseline / reference arm
