@@ -51,6 +51,7 @@ SIGNATURES = {
     "cvmm_sort_rows_padded": (_I, [_P, _I, _L, _P, _L, _P, _I, _P, _P, _L, _L, _L, _P, _I, _P, _P]),
     "cvmm_sum_routes": (_I, [_P, _I, _P, _I, _L, _L, _L, _P, _P]),
     "cvmm_padded_route_rows": (_I, [_P, _P, _P, _P, _L, _L, _P, _P]),
+    "cvmm_selftest_wait_timeout": (_I, [_L, _P]),
     "cvmm_weighted_token_backward": (_I, [_P, _I, _P, _I, _P, _I, _P, _I, _P, _L, _L, _L, _P]),
     "cvmm_cast": (_I, [_P, _I, _P, _I, _L, _P]),
 }

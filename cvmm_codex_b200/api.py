@@ -83,9 +83,9 @@ def cvmm_prepare_sel2(sel: Union[torch.Tensor, CVMMSel], w: Optional[torch.Tenso
 
 def get_dtype():
     """Operation dtype: the autocast dtype when autocast is on, else float32 (cvmm.py:30-33)."""
-    if not torch.is_autocast_enabled():
+    if not torch.is_autocast_enabled("cuda"):
         return torch.float32
-    return torch.get_autocast_gpu_dtype()
+    return torch.get_autocast_dtype("cuda")
 
 
 def dtype_to_type_id(dtype: torch.dtype):

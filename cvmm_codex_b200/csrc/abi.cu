@@ -6,6 +6,7 @@
 
 #include "gemm.cuh"
 #include "launch.h"
+#include "ptx.cuh"
 
 namespace cvmm {
 
@@ -89,6 +90,24 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* __restrict__ s
   } else {
     for (int c = 0; c < 8 && n0 + c < N; ++c) store_from_float(out, o_dtype, t * N + n0 + c, acc[c]);
   }
+}
+
+// Self-test of the bounded-wait path every persistent kernel relies on: one
+// thread waits on an mbarrier that nothing ever arrives on, through the same
+// bounded wait as the GEMM roles, so the wait runs out after `limit_ns`, the
+// status word records CVMM_DEV_TIMEOUT at kSelfTestTag and the kernel returns.
+constexpr int kSelfTestTag = 99;
+
+__global__ void wait_timeout_selftest_kernel(uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(&bar, 1);
+    abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) ptx::mbar_wait_or_abort(&bar, 0, kSelfTestTag, &abort_flag, limit_ns);
 }
 
 // rows[route[v]] = pad_start[e] + v - seg_begin(e) for every sorted position v.
@@ -347,6 +366,13 @@ int cvmm_sum_routes(const void* src, int src_dtype, void* out, int out_dtype, in
                     int64_t top_k, int64_t d, const int32_t* src_rows, cvmm_stream_t stream) {
   return cvmm_weighted_combine(src, src_dtype, nullptr, CVMM_F32, out, out_dtype, n_tokens, top_k, d, src_rows,
                                stream);
+}
+
+int cvmm_selftest_wait_timeout(int64_t limit_ns, cvmm_stream_t stream) {
+  if (limit_ns < 1000 || limit_ns > 100000000)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_selftest_wait_timeout: limit must be in [1 us, 100 ms]");
+  wait_timeout_selftest_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>((uint64_t)limit_ns);
+  return check_launch("cvmm_selftest_wait_timeout");
 }
 
 int cvmm_padded_route_rows(const int64_t* route, const int32_t* sorted_sel, const int64_t* offsets,

@@ -74,7 +74,7 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 // `abort` (after its own wait timed out), so an unwinding CTA does not sit
 // out one time limit per remaining wait.
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, int where,
-                                                   volatile int* abort) {
+                                                   volatile int* abort, uint64_t limit_ns = kWaitLimitNs) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
@@ -82,7 +82,7 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
     if (mbar_try_wait(a, parity)) return true;
     if ((it & 255u) == 0u) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         report(CVMM_DEV_TIMEOUT, where, (long long)parity);
         *abort = 1;
         return false;

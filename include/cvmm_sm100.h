@@ -62,6 +62,14 @@ const char* cvmm_last_error(void);
  * where/aux receive the kernel tag and offending value when non-NULL. */
 int cvmm_device_status(int reset, int* where, long long* aux, cvmm_stream_t stream);
 
+/* Failure-path self-test: launches one thread that waits on a barrier nothing
+ * arrives on, through the bounded wait all persistent kernels use, with a limit
+ * of limit_ns (1 us .. 100 ms) instead of the kernels' 2 s. Afterwards
+ * cvmm_device_status reports CVMM_DEV_TIMEOUT with where == 99, and the
+ * context stays usable. No reference counterpart (the reference has no device
+ * failure detection). */
+int cvmm_selftest_wait_timeout(int64_t limit_ns, cvmm_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Selector preparation.
  * Replaces cvmm_prepare_sel2 (cvmm.py:1786-1803) and cvmm_prepare_sel

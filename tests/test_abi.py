@@ -55,6 +55,7 @@ def test_workspace_queries_need_no_device():
     (lambda l: l.cvmm_forward(16, 0, 4, 8, 16, None, 16, 4, 16, 0, 1, 8, 8, 64, 8, 1, 16, 0, 8, 0, None, 16, None, 0, None), -1),
     (lambda l: l.cvmm_backward_x(16, 2, 8, None, 1, None, 16, 4, 16, 2, 1, 8, 8, 64, 8, 1, 16, 2, 8, 1, 16, 0, 16, 2, 8, 16, 2, 16, 16, None, 0, None), -1),
     (lambda l: l.cvmm_padded_route_rows(None, None, None, None, 4, 2, None, None), -1),
+    (lambda l: l.cvmm_selftest_wait_timeout(0, None), -1),
     (lambda l: l.cvmm_cast(None, 0, None, 9, 4, None), -2),
     (lambda l: l.cvmm_expert_offsets(None, 4, 0, None, None), -1),
 ])
