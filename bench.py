@@ -92,6 +92,18 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def wait_first(self, limit_s):
+        t_end = time.perf_counter() + limit_s
+        while self.proc is not None and not self.lines and time.perf_counter() < t_end:
+            time.sleep(0.02)
+
+    def mark(self):
+        """Samples before this point (idle, warm-up) are left out of the summary."""
+        self.start = len(self.lines)
+
+    def since_mark(self):
+        return len(self.lines) - getattr(self, "start", 0)
+
     def __exit__(self, *exc):
         if self.proc is not None:
             self.proc.terminate()
@@ -104,7 +116,7 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[getattr(self, "start", 0):]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -248,13 +260,22 @@ def run_ours(args, rank, world, local_rank):
                 print(f"CUDA graph capture failed ({exc!r}); timing eager steps", file=sys.stderr)
                 torch.cuda.synchronize()
         with ClockSampler(local_rank) as clk:
+            clk.wait_first(5.0)  # nvidia-smi takes a moment to print its first line
             for _ in range(max(args.warmup, 3)):
                 run(d["sel"], d["grad_out"])
             torch.cuda.synchronize()
             if world > 1:
                 dist.barrier()
             torch.cuda.synchronize()
+            clk.mark()
             total_ms = time_steps(run, d, args.steps, flush)
+            # A short timed region may end between two samples: keep the same
+            # replays running (untimed) until the sampler has seen the load.
+            t_end = time.perf_counter() + 1.0
+            while clk.since_mark() < 10 and time.perf_counter() < t_end:
+                for _ in range(20):
+                    run(d["sel"], d["grad_out"])
+                torch.cuda.synchronize()
         if world > 1:
             t = torch.tensor([total_ms], device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -537,20 +537,34 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
     int64_t crow = crow_of(ent);
     int4 ent_next = entry(blockIdx.x + gridDim.x);
     int local = 0;
+    // Mode 1 reads the route's x row for the sel-weight dot product: 64
+    // columns as eight 16-byte loads, issued ahead of the accumulator they
+    // pair with (x_vec: 16-bit x with 16-byte aligned rows).
+    const bool x_vec = p.mode == 1 && (flags & 65536);
+    uint4 xr[8];
+    auto load_x = [&](int64_t row, int64_t col0) {
+      if (!x_vec || row < 0 || col0 + 64 > p.N) return;
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const char*>(p.x) + (row * p.x_ld + col0) * 2);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) xr[q] = src[q];
+    };
     for (int tt = blockIdx.x; tt < total; tt += gridDim.x, ++local) {
       const int64_t crow_next = crow_of(ent_next);
       const int4 ent_after = entry(tt + 2 * gridDim.x);
       const int a = local & 1;
+      const int64_t n0 = (int64_t)(tt % n_n) * BN;
+      load_x(crow, n0);
       if (!ptx::mbar_wait_or_abort(&bar.accf[a], (local >> 1) & 1, kTagAccFull, bar.abort)) break;
       ptx::tc_fence_after();
       if (rr == 0) CVMM_STAMP(2, local);
-      const int64_t n0 = (int64_t)(tt % n_n) * BN;
       const bool row_ok = crow >= 0;
       float wv = 0.f, dot = 0.f;
       if (p.mode == 1 && row_ok) wv = round_to(load_as_float(p.w, p.w_dtype, crow), op);
       const int prow0 = c_dense ? p.c_pad_start[ent.x] + (int)(ent.y - seg_begin(p.offsets, ent.x)) + ew * 32 : 0;
       for (int ch = 0; ch < BN / 64; ++ch) {
         if (n0 + ch * 64 >= p.N) break;
+        if (ch > 0) load_x(crow, n0 + ch * 64);
+        const bool xv_ok = x_vec && n0 + ch * 64 + 64 <= p.N;
         float v2[64];
         load_acc64(tmem + ((uint32_t)(ew * 32) << 16) + a * BN + ch * 64, v2);
         if (c_dense) {
@@ -590,7 +604,18 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = 0.f;
           }
-          if (p.mode == 1 && row_ok) {
+          if (p.mode == 1 && row_ok && xv_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const uint4 q4 = xr[4 * h + (j >> 3)];
+              const int c = (j >> 1) & 3;
+              const uint32_t wd = c == 0 ? q4.x : (c == 1 ? q4.y : (c == 2 ? q4.z : q4.w));
+              const float xval = bits_to_float((uint16_t)((j & 1) ? (wd >> 16) : (wd & 0xffffu)), p.x_dtype);
+              const float av = round_to(v[j], op);
+              dot = fmaf(av, xval, dot);
+              v[j] = round_to(av * wv, op);
+            }
+          } else if (p.mode == 1 && row_ok) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const float av = round_to(v[j], op);
@@ -1170,6 +1195,7 @@ int launch_row_gemm_umma(const RowGemm& p, int64_t max_tiles, cudaStream_t strea
       (b_kmajor ? (p.bs_k == 1 && p.bs_n % 8 == 0) : (p.bs_n == 1 && p.bs_k % 8 == 0)))
     flags |= 2;
   if (p.c_ld % 8 == 0 && aligned16(p.c)) flags |= 4;
+  if (p.mode == 1 && (p.x_dtype == BF16 || p.x_dtype == F16) && p.x_ld % 8 == 0 && aligned16(p.x)) flags |= 65536;
   if (p.N <= 64) {
     return b_kmajor ? row_launch<64, 7, true>(p, max_tiles, flags, stream)
                     : row_launch<64, 7, false>(p, max_tiles, flags, stream);
