@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* __restrict__ s
     uint32_t wd[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c)
-      wd[c] = (uint32_t)float_to_bits(acc[2 * c], o_dtype) | ((uint32_t)float_to_bits(acc[2 * c + 1], o_dtype) << 16);
+      wd[c] = pack2(acc[2 * c], acc[2 * c + 1], o_dtype);
     *reinterpret_cast<uint4*>(static_cast<char*>(out) + (t * N + n0) * 2) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
   } else {
     for (int c = 0; c < 8 && n0 + c < N; ++c) store_from_float(out, o_dtype, t * N + n0 + c, acc[c]);
@@ -168,10 +168,10 @@ __global__ void cast_f32_to_16_vec(const float4* __restrict__ src, uint4* __rest
        i += (int64_t)gridDim.x * blockDim.x) {
     const float4 a = src[2 * i], b = src[2 * i + 1];
     uint4 o;
-    o.x = (uint32_t)float_to_bits(a.x, d_dtype) | ((uint32_t)float_to_bits(a.y, d_dtype) << 16);
-    o.y = (uint32_t)float_to_bits(a.z, d_dtype) | ((uint32_t)float_to_bits(a.w, d_dtype) << 16);
-    o.z = (uint32_t)float_to_bits(b.x, d_dtype) | ((uint32_t)float_to_bits(b.y, d_dtype) << 16);
-    o.w = (uint32_t)float_to_bits(b.z, d_dtype) | ((uint32_t)float_to_bits(b.w, d_dtype) << 16);
+    o.x = pack2(a.x, a.y, d_dtype);
+    o.y = pack2(a.z, a.w, d_dtype);
+    o.z = pack2(b.x, b.y, d_dtype);
+    o.w = pack2(b.z, b.w, d_dtype);
     dst[i] = o;
   }
 }

@@ -53,6 +53,17 @@ __device__ __forceinline__ uint16_t float_to_bits(float v, int dtype) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(v));
 }
 
+// Two values rounded to a 16-bit dtype (round-to-nearest-even) and packed
+// low | high << 16, with one paired conversion instead of two.
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, int dtype) {
+  if (dtype == F16) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+  const __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&b);
+}
+
 __device__ __forceinline__ float bits_to_float(uint16_t b, int dtype) {
   if (dtype == F16) return __half2float(__ushort_as_half(b));
   return __bfloat162float(__ushort_as_bfloat16(b));

@@ -193,7 +193,7 @@ __device__ __forceinline__ void store8(char* to, int dtype, const float (&v)[8])
   uint32_t w[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
-    w[i] = (uint32_t)float_to_bits(v[2 * i], dtype) | ((uint32_t)float_to_bits(v[2 * i + 1], dtype) << 16);
+    w[i] = pack2(v[2 * i], v[2 * i + 1], dtype);
   *reinterpret_cast<uint4*>(to) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 

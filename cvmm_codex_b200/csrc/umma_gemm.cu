@@ -50,7 +50,7 @@ constexpr uint32_t kAtomRowsBytes = 64 * 128;  // one 64-row x 128-byte MN-major
 
 // Development-only knobs (compiled in with -DCVMM_TRACE; absent from the
 // shipped library): bit 8 skips the MMAs, bit 9 / bit 10 skip the A / B loads,
-// bit 14 skips the epilogue stores.
+// bit 14 skips the epilogue stores, bit 15 keeps one epilogue warp group.
 #ifdef CVMM_TRACE
 #define CVMM_DBG(flags, bit) (((flags) & (bit)) != 0)
 #else
@@ -63,7 +63,7 @@ constexpr uint32_t kAtomRowsBytes = 64 * 128;  // one 64-row x 128-byte MN-major
 __device__ unsigned long long* g_trace;
 #define CVMM_STAMP(role, idx)                                                     \
   do {                                                                            \
-    if (g_trace && blockIdx.x == 0 && (idx) < 4096) g_trace[(role) * 4096 + (idx)] = globaltimer_ns(); \
+    if (g_trace && blockIdx.x == 0 && (idx) < 4096) g_trace[(role) * 4096 + (idx)] = clock64(); \
   } while (0)
 #else
 #define CVMM_STAMP(role, idx) \
@@ -77,17 +77,19 @@ enum : int { kTagEmpty = 1, kTagFull = 2, kTagAccFull = 3, kTagAccEmpty = 4, kTa
 // Shared-memory plan of one CTA (offsets from a 1024-byte aligned base):
 //   S operand stages (A tile 16 KiB + B tile BN x 128 B);
 //   barriers: full[S] empty[S] acc_full[2] acc_empty[2] drain idx_full[S] idx_empty[S] ready[S];
-//   epilogue staging (32 KiB, 1024-byte aligned): per epilogue warp either a
+//   epilogue staging (36 KiB, 1024-byte aligned): per epilogue warp either a
 //   32 x 32 block (rows of 144 B; the 16-byte pad spreads the rows over the
-//   shared-memory banks) or two 32-row x 128-byte boxes in the 128-byte
-//   swizzle that TMA stores read;
+//   shared-memory banks) or 32-row x 128-byte boxes in the 128-byte swizzle
+//   that TMA stores read (two per warp with one epilogue warp group, one with two);
 //   index ring (grad-W): S slots of the stage's x rows, grad rows and route
 //   weights, bulk-copied from a 16-byte aligned start 0-3 entries before the
 //   stage's first route (`off`).
 constexpr uint32_t kStageRowBytes = 144;
 constexpr uint32_t kStoreBox = 32 * 128;                  // one 32-row x 64-column 16-bit TMA store box
-constexpr uint32_t kStagingBytes = 4 * 2 * kStoreBox;     // >= 4 * 32 * kStageRowBytes
-static_assert(kStagingBytes >= 4 * 32 * kStageRowBytes, "staging too small");
+// Per epilogue warp: two store boxes (one warp group) or one (two groups), or
+// 32 rows of kStageRowBytes.
+constexpr uint32_t kStagingBytes = 8 * 32 * kStageRowBytes;
+static_assert(kStagingBytes >= 8 * kStoreBox, "staging too small");
 constexpr int kRingEntries = 72;
 struct IdxSlot {
   int x[kRingEntries];
@@ -170,7 +172,7 @@ __device__ __forceinline__ void load_chunk(uint32_t dst, const char* row, int64_
       if (2 * i < rem) lo = load_as_float(row, src_dtype, (col + 2 * i) * col_stride);
       if (2 * i + 1 < rem) hi = load_as_float(row, src_dtype, (col + 2 * i + 1) * col_stride);
     }
-    wds[i] = (uint32_t)float_to_bits(lo, op_dtype) | ((uint32_t)float_to_bits(hi, op_dtype) << 16);
+    wds[i] = pack2(lo, hi, op_dtype);
   }
   ptx::st_shared_v4(dst, wds[0], wds[1], wds[2], wds[3]);
 }
@@ -190,8 +192,7 @@ __device__ __forceinline__ void store_row32(void* c, int c_dtype, int64_t off, c
       uint32_t w[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        w[i] = (uint32_t)float_to_bits(v[q * 8 + 2 * i], c_dtype) |
-               ((uint32_t)float_to_bits(v[q * 8 + 2 * i + 1], c_dtype) << 16);
+        w[i] = pack2(v[q * 8 + 2 * i], v[q * 8 + 2 * i + 1], c_dtype);
       dst[q] = make_uint4(w[0], w[1], w[2], w[3]);
     }
     return;
@@ -265,8 +266,7 @@ __device__ __forceinline__ void warp_store_block(void* c, int c_dtype, int64_t r
       uint32_t w[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        w[i] = (uint32_t)float_to_bits(v[8 * q + 2 * i], c_dtype) |
-               ((uint32_t)float_to_bits(v[8 * q + 2 * i + 1], c_dtype) << 16);
+        w[i] = pack2(v[8 * q + 2 * i], v[8 * q + 2 * i + 1], c_dtype);
       ptx::st_shared_v4(my + 16 * q, w[0], w[1], w[2], w[3]);
     }
     __syncwarp();
@@ -287,7 +287,7 @@ __device__ __forceinline__ void warp_store_block(void* c, int c_dtype, int64_t r
 // Barrier set-up and TMEM allocation (2 accumulator slots of BN columns).
 template <int BN, int S>
 __device__ __forceinline__ uint32_t setup(const Bars& b, int full_count, int idxe_count = kProducers,
-                                          int ready_count = 1) {
+                                          int ready_count = 1, int epi_count = kEpilogue) {
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -296,7 +296,7 @@ __device__ __forceinline__ uint32_t setup(const Bars& b, int full_count, int idx
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&b.accf[a], 1);
-      ptx::mbar_init(&b.acce[a], kEpilogue);
+      ptx::mbar_init(&b.acce[a], epi_count);
     }
     ptx::mbar_init(b.drain, 1);
     for (int s = 0; s < S; ++s) {
@@ -364,13 +364,20 @@ __device__ __forceinline__ void mma_loop(const Bars& b, uint64_t* consume, uint8
 
 // ============================================================ row-gathered GEMM
 // flags bit0: A fast path (cp.async), bit1: B fast path (cp.async when not
-// TMA), bit2: C vector stores.
-template <int BN, int S, bool B_KMAJOR, bool B_TMA, bool A_TMA>
+// TMA), bit2: C vector stores, bit5: dense A (expert-padded layout), bit7:
+// dense C (TMA stores), bit16: 16-byte x loads in the mode-1 epilogue.
+// EPI2 (dense A, BN = 128): warp 9 issues the A box with the B tiles, and
+// warps 0-3 become a second epilogue group: warps 4-7 drain accumulator
+// columns 0-63, warps 0-3 columns 64-127 (warp w reaches TMEM lanes
+// 32*(w%4)..+31), which halves the per-tile epilogue time that otherwise
+// bounds the short-K shapes.
+template <int BN, int S, bool B_KMAJOR, bool B_TMA, bool A_TMA, bool EPI2 = false>
 __global__ void __launch_bounds__(kThreads, 1)
 row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_c, int flags,
                 int n_n) {
   static_assert(!A_TMA || B_TMA, "TMA row gathers are used together with TMA weight tiles");
+  static_assert(!EPI2 || (A_TMA && BN == 128), "two epilogue groups need dense TMA A tiles and BN = 128");
   using L = Smem<BN, S>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_smem(smem_raw);
@@ -380,7 +387,8 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
   const int nkb = (int)((p.K + BK - 1) / BK);
   const int op = p.op_dtype;
   const bool a_fast = flags & 1, b_fast = flags & 2, c_vec = flags & 4;
-  const uint32_t tmem = setup<BN, S>(bar, A_TMA ? 2 : kProducers + (B_TMA ? 1 : 0));
+  const uint32_t tmem = setup<BN, S>(bar, EPI2 ? 1 : (A_TMA ? 2 : kProducers + (B_TMA ? 1 : 0)), kProducers, 1,
+                                     EPI2 ? 2 * kEpilogue : kEpilogue);
 
   auto entry = [&](int tt) -> int4 {
     return tt < total ? p.tiles[tt / n_n] : make_int4(0, 0, 0, 0);
@@ -393,7 +401,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
   };
   const bool a_dense = flags & 32;
 
-  if (A_TMA && warp < 4) {
+  if (!EPI2 && A_TMA && warp < 4) {
     // ------------------------------------------------------------ A rows by TMA gather4
     // Warp 0: lane l gathers rows 4l..4l+3 of every tile, 4 rows x 128 bytes
     // per instruction, straight into the K-major swizzled A stage.
@@ -440,7 +448,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
         for (int q = 0; q < 4; ++q) rows[q] = rows_next[q];
       }
     }
-  } else if (warp < 4) {
+  } else if (!EPI2 && warp < 4) {
     // ------------------------------------------------------------ producers
     const int t = threadIdx.x;
     const int ac = t & 7;
@@ -522,13 +530,16 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
     ptx::cp_async_wait_all();
   } else if (warp < 8) {
     // ------------------------------------------------------------ epilogue
-    const int ew = warp - 4;
+    const int ew = warp & 3;                                // TMEM lane quadrant
+    const int c_lo = EPI2 ? (warp < 4 ? BN / 2 : 0) : 0;    // this warp's accumulator columns
+    const int c_hi = EPI2 ? c_lo + BN / 2 : BN;
+    const bool stamper = warp == 4 && lane == 0;
     const int rr = ew * 32 + lane;
-    const uint32_t stage = ptx::smem_u32(smem + L::staging) + ew * 32 * kStageRowBytes;
+    const uint32_t stage = ptx::smem_u32(smem + L::staging) + (EPI2 ? warp : ew) * 32 * kStageRowBytes;
     // Dense C (expert-padded sorted output): each 32-row x 64-column block is
-    // written to one of the warp's two swizzled boxes and stored by TMA.
+    // written to a swizzled box of the warp and stored by TMA.
     const bool c_dense = flags & 128;
-    const uint32_t cbox = ptx::smem_u32(smem + L::staging) + ew * 2 * kStoreBox;
+    const uint32_t cbox = ptx::smem_u32(smem + L::staging) + (EPI2 ? warp * kStoreBox : ew * 2 * kStoreBox);
     int cbuf = 0;
     auto crow_of = [&](const int4& en) -> int64_t {
       return (c_dense || rr >= en.z) ? -1 : p.c_index[en.y + rr];
@@ -553,44 +564,50 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
       const int4 ent_after = entry(tt + 2 * gridDim.x);
       const int a = local & 1;
       const int64_t n0 = (int64_t)(tt % n_n) * BN;
-      load_x(crow, n0);
+      load_x(crow, n0 + c_lo);
       if (!ptx::mbar_wait_or_abort(&bar.accf[a], (local >> 1) & 1, kTagAccFull, bar.abort)) break;
       ptx::tc_fence_after();
-      if (rr == 0) CVMM_STAMP(2, local);
+      if (stamper) CVMM_STAMP(2, local);
       const bool row_ok = crow >= 0;
       float wv = 0.f, dot = 0.f;
       if (p.mode == 1 && row_ok) wv = round_to(load_as_float(p.w, p.w_dtype, crow), op);
       const int prow0 = c_dense ? p.c_pad_start[ent.x] + (int)(ent.y - seg_begin(p.offsets, ent.x)) + ew * 32 : 0;
-      for (int ch = 0; ch < BN / 64; ++ch) {
+      for (int ch = c_lo / 64; ch < c_hi / 64; ++ch) {
         if (n0 + ch * 64 >= p.N) break;
-        if (ch > 0) load_x(crow, n0 + ch * 64);
+        if (ch > c_lo / 64) load_x(crow, n0 + ch * 64);
         const bool xv_ok = x_vec && n0 + ch * 64 + 64 <= p.N;
         float v2[64];
         load_acc64(tmem + ((uint32_t)(ew * 32) << 16) + a * BN + ch * 64, v2);
+        if (stamper && ch == 0) CVMM_STAMP(4, local);
         if (c_dense) {
           if (nkb == 0) {
 #pragma unroll
             for (int j = 0; j < 64; ++j) v2[j] = 0.f;
           }
-          // The store issued from this box two blocks ago must have read it.
-          if (lane == 0) ptx::bulk_wait_read<1>();
+          // The store issued earlier from this box must have read it (two
+          // boxes per warp: the one before last; one box: the last).
+          if (lane == 0) {
+            if (EPI2) ptx::bulk_wait_read<0>();
+            else ptx::bulk_wait_read<1>();
+          }
           __syncwarp();
-          const uint32_t box = cbox + cbuf * kStoreBox;
+          const uint32_t box = cbox + (EPI2 ? 0u : cbuf * kStoreBox);
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             uint32_t w4[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-              w4[i] = (uint32_t)float_to_bits(v2[8 * q + 2 * i], p.c_dtype) |
-                      ((uint32_t)float_to_bits(v2[8 * q + 2 * i + 1], p.c_dtype) << 16);
+              w4[i] = pack2(v2[8 * q + 2 * i], v2[8 * q + 2 * i + 1], p.c_dtype);
             ptx::st_shared_v4(box + lane * 128 + ((uint32_t)(q ^ (lane & 7)) << 4), w4[0], w4[1], w4[2], w4[3]);
           }
+          if (stamper && ch == 0) CVMM_STAMP(5, local);
           ptx::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0 && !CVMM_DBG(flags, 16384)) {
             ptx::tma_store_2d(&tmap_c, box, (int)(n0 + ch * 64), prow0);
             ptx::bulk_commit();
           }
+          if (stamper) CVMM_STAMP(6 + (ch & 1), local);
           cbuf ^= 1;
           continue;
         }
@@ -630,7 +647,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
       if (p.mode == 1 && row_ok) atomicAdd(p.gsel + crow, dot);
       ptx::tc_fence_before();
       ptx::mbar_arrive(&bar.acce[a]);
-      if (rr == 0) CVMM_STAMP(3, local);
+      if (stamper) CVMM_STAMP(3, local);
       ent = ent_next;
       ent_next = ent_after;
       crow = crow_next;
@@ -647,12 +664,14 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
   } else if (B_TMA && lane == 0) {
     // ------------------------------------------------------------ B tiles by TMA
     ptx::tma_prefetch_desc(&tmap_b);
+    if (EPI2) ptx::tma_prefetch_desc(&tmap_a);
     uint32_t it = 0;
     int4 ent = entry(blockIdx.x);
     for (int tt = blockIdx.x; tt < total; tt += gridDim.x) {
       const int4 ent_next = entry(tt + gridDim.x);
       const int e = ent.x;
       const int n0 = (tt % n_n) * BN;
+      const int a_row0 = EPI2 ? a_row_of(ent, 0) : 0;  // dense A: the tile's first padded row
       bool aborted = false;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % S;
@@ -665,7 +684,8 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
           ptx::mbar_arrive(&bar.full[s]);
           continue;
         }
-        ptx::mbar_arrive_expect_tx(&bar.full[s], L::b_bytes);
+        ptx::mbar_arrive_expect_tx(&bar.full[s], (EPI2 ? L::a_bytes : 0u) + L::b_bytes);
+        if (EPI2) ptx::tma_load_2d(b_u - L::a_bytes, &tmap_a, &bar.full[s], kb * BK, a_row0);
         if (B_KMAJOR) {
           ptx::tma_load_3d(b_u, &tmap_b, &bar.full[s], kb * BK, n0, e);
         } else {
@@ -708,7 +728,7 @@ __device__ __forceinline__ void scale_rows(uint8_t* smem, const IdxSlot* ring, u
     for (int q = 0; q < 4; ++q) {
       const float lo = bits_to_float((uint16_t)(w4[q] & 0xffffu), op) * sc;
       const float hi = bits_to_float((uint16_t)(w4[q] >> 16), op) * sc;
-      w4[q] = (uint32_t)float_to_bits(lo, op) | ((uint32_t)float_to_bits(hi, op) << 16);
+      w4[q] = pack2(lo, hi, op);
     }
     ptx::st_shared_v4(addr, w4[0], w4[1], w4[2], w4[3]);
   }
@@ -852,7 +872,7 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
             for (int q = 0; q < 4; ++q) {
               const float lo = bits_to_float((uint16_t)(w4[q] & 0xffffu), op) * sc;
               const float hi = bits_to_float((uint16_t)(w4[q] >> 16), op) * sc;
-              w4[q] = (uint32_t)float_to_bits(lo, op) | ((uint32_t)float_to_bits(hi, op) << 16);
+              w4[q] = pack2(lo, hi, op);
             }
             ptx::st_shared_v4(addr, w4[0], w4[1], w4[2], w4[3]);
           }
@@ -1121,7 +1141,12 @@ static int row_launch(const RowGemm& p, int64_t max_tiles, int flags, cudaStream
   }
   const int64_t work = max_tiles * n_n;
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(work, sm_count()));
-  if (a_tma) {
+  if (a_dense && BN == 128 && !(dbg_flags() & 32768)) {
+    auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true, true, BN == 128>;
+    int rc = set_smem(kern, L::alloc);
+    if (rc) return rc;
+    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, cmap, flags, n_n);
+  } else if (a_tma) {
     auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true, true>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
