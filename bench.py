@@ -479,18 +479,27 @@ def main():
         if line is not None:
             print(json.dumps(line), flush=True)
         return
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-        torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
-    # The drop-in module prints "New shape:" like the reference; keep stdout
-    # for the one JSON line.
+    # The drop-in module prints "New shape:" like the reference and NCCL prints
+    # its banner from C++: both go to stderr (file-descriptor level) so stdout
+    # carries only the one JSON line.
     import contextlib
-    with contextlib.redirect_stdout(sys.stderr):
-        line = run_ours(args, rank, world, local_rank)
+    sys.stdout.flush()
+    saved_fd = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+            torch.cuda.set_device(local_rank)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local_rank))
+        with contextlib.redirect_stdout(sys.stderr):
+            line = run_ours(args, rank, world, local_rank)
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved_fd, 1)
+        os.close(saved_fd)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
