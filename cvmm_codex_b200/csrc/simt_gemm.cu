@@ -83,32 +83,62 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot) {
 // (slot -1); the chunks of a split expert write consecutive partial slots
 // that seg_reduce_kernel later sums in chunk order, so the result does not
 // depend on scheduling.
+constexpr int kUnitSortMaxExperts = 1024;
+
 __global__ void __launch_bounds__(1024)
 build_units_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int64_t chunk,
                    int4* __restrict__ units, int* __restrict__ n_units, int2* __restrict__ expert_slots) {
   __shared__ int warp_tot[32];
+  __shared__ int tail_len[kUnitSortMaxExperts];  // each expert's tail chunk length (0: none)
   const int t = threadIdx.x;
   const int64_t per = (n_experts + blockDim.x - 1) / blockDim.x;
   const int64_t e0 = min((int64_t)t * per, n_experts), e1 = min(e0 + per, n_experts);
-  int cnt = 0, slots = 0;
+  // Full chunks of every expert come first (in expert order), then the
+  // shorter tail chunks, longest first (for up to kUnitSortMaxExperts
+  // experts; expert order otherwise): CTAs take units round-robin, so this
+  // longest-first order spreads the long units evenly over the CTAs. Slots of
+  // split experts are numbered per expert in chunk order whatever the
+  // emission order, so seg_reduce's fixed summation order is unchanged.
+  const bool sort_tails = n_experts <= kUnitSortMaxExperts;
+  int full = 0, tails = 0, slots = 0;
   for (int64_t e = e0; e < e1; ++e) {
     const int64_t len = offsets[e] - seg_begin(offsets, e);
     const int nch = (int)((len + chunk - 1) / chunk);
-    cnt += nch;
+    full += (int)(len / chunk);
+    tails += (len % chunk) != 0;
     if (nch > 1) slots += nch;
+    if (sort_tails) tail_len[e] = (int)(len % chunk);
   }
-  int pos = block_exclusive_scan(cnt, warp_tot);
+  int fpos = block_exclusive_scan(full, warp_tot);
+  int tpos = block_exclusive_scan(tails, warp_tot);
   int sbase = block_exclusive_scan(slots, warp_tot);
+  __shared__ int full_total;
+  if (t == blockDim.x - 1) full_total = fpos + full;
+  __syncthreads();
+  const int n_full = full_total;
   for (int64_t e = e0; e < e1; ++e) {
     const int64_t b = seg_begin(offsets, e), end = offsets[e];
     const int nch = (int)((end - b + chunk - 1) / chunk);
     expert_slots[e] = make_int2(nch > 1 ? sbase : -1, nch);
     int c = 0;
-    for (int64_t r = b; r < end; r += chunk, ++c)
-      units[pos++] = make_int4((int)e, (int)r, nch > 1 ? sbase + c : -1, (int)min(r + chunk, end));
+    for (int64_t r = b; r < end; r += chunk, ++c) {
+      const int4 u = make_int4((int)e, (int)r, nch > 1 ? sbase + c : -1, (int)min(r + chunk, end));
+      if (r + chunk <= end) {
+        units[fpos++] = u;
+      } else {
+        int rank = tpos;
+        if (sort_tails) {  // tails longer than this one, ties by expert id
+          const int L = (int)(end - r);
+          rank = 0;
+          for (int64_t f = 0; f < n_experts; ++f) rank += tail_len[f] > L || (tail_len[f] == L && f < e);
+        }
+        units[n_full + rank] = u;
+        ++tpos;
+      }
+    }
     if (nch > 1) sbase += nch;
   }
-  if (t == blockDim.x - 1) *n_units = pos;
+  if (t == blockDim.x - 1) *n_units = n_full + tpos;
 }
 
 int build_units(const int64_t* offsets, int64_t n_experts, int64_t chunk, int4* units, int* n_units,

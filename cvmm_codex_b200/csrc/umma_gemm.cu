@@ -969,6 +969,7 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
       if (!ptx::mbar_wait_or_abort(&bar.accf[a], (local >> 1) & 1, kTagAccFull, bar.abort)) break;
       ptx::tc_fence_after();
       const int64_t e = u.x;
+      if (mr == 0) CVMM_STAMP(2, local);
       const int64_t m = m0 + mr;
       float* dst = u.z < 0 ? p.out + e * p.M * p.N : p.partials + (int64_t)u.z * p.M * p.N;
       const bool empty_unit = nkb_of(u) == 0;
