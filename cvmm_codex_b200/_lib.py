@@ -42,7 +42,7 @@ SIGNATURES = {
     "cvmm_expert_offsets": (_I, [_P, _L, _L, _P, _P]),
     "cvmm_gemm_workspace_size": (_S, [_L, _L, _L, _L, _I, _I, _I, _L]),
     "cvmm_forward": (_I, [_P, _I, _L, _L, _P, _P, _P, _L, _P, _I, _L, _L, _L, _L, _L, _L,
-                          _P, _I, _L, _I, _P, _P, _P, _S, _P]),
+                          _P, _I, _L, _I, _P, _P, _P, _P, _S, _P]),
     "cvmm_weighted_combine": (_I, [_P, _I, _P, _I, _P, _I, _L, _L, _L, _P, _P]),
     "cvmm_backward_x": (_I, [_P, _I, _L, _P, _L, _P, _P, _L, _P, _I, _L, _L, _L, _L, _L, _L,
                              _P, _I, _L, _I, _P, _I, _P, _I, _L, _P, _I, _P, _P, _P, _S, _P]),
@@ -50,6 +50,7 @@ SIGNATURES = {
                              _L, _L, _P, _I, _P, _P, _P, _S, _P]),
     "cvmm_sort_rows_padded": (_I, [_P, _I, _L, _P, _L, _P, _I, _P, _P, _L, _L, _L, _P, _I, _P, _P]),
     "cvmm_sum_routes": (_I, [_P, _I, _P, _I, _L, _L, _L, _P, _P]),
+    "cvmm_pad_starts": (_I, [_P, _L, _P, _P]),
     "cvmm_padded_route_rows": (_I, [_P, _P, _P, _P, _L, _L, _P, _P]),
     "cvmm_selftest_wait_timeout": (_I, [_L, _P]),
     "cvmm_weighted_token_backward": (_I, [_P, _I, _P, _I, _P, _I, _P, _I, _P, _L, _L, _L, _P]),
@@ -81,7 +82,7 @@ def load():
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if lib.cvmm_abi_version() != 4:
+        if lib.cvmm_abi_version() != 5:
             raise CvmmLibraryError("libcvmm_sm100.so ABI version mismatch; rebuild it")
         _lib = lib
     return _lib

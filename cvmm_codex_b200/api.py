@@ -185,13 +185,21 @@ class CVMM(torch.autograd.Function):
         offsets = ops.expert_offsets(sel, n_experts)
         keys_op = _operand(keys, op_dtype)
         xs = xpad = None
-        if _sortable(x, op_dtype):
+        if _sortable(x, op_dtype) and reduction_weight is not None:
             # Expert-sorted, 128-row padded op-dtype copy of the route rows of x:
             # the forward and the grad-W read it as dense tiles (the reference's
             # grouped-x copy, cvmm.py:1123-1138).
             xs, xpad = ops.sort_rows_padded(x, sel_index, 1, sel, offsets, n_experts, dtype=op_dtype)
         a = x if xs is None else xs
-        if reduction_weight is not None:
+        if reduction_weight is None and _sortable(x, op_dtype):
+            # The forward gathers x's rows anyway: it writes that sorted padded
+            # copy for the grad-W as it goes, instead of a separate copy pass.
+            xpad = ops.pad_starts(offsets, n_experts)
+            xs = torch.empty((sel_index.numel() + n_experts * ops.PAD_ROWS, x.shape[-1]), dtype=op_dtype,
+                             device=x.device)
+            res = ops.forward(x, sel_index, offsets, keys_op, out_index, op_dtype, op_dtype, x_copy=xs)
+            res = res.view(*sel.shape, res.shape[-1])
+        elif reduction_weight is not None:
             rows = out_pad = None
             if xs is not None and keys.shape[-1] % 8 == 0:
                 # Route outputs stay in the padded sorted layout (dense TMA tile

@@ -261,7 +261,7 @@ using namespace cvmm;
 // ================================================================== C ABI
 extern "C" {
 
-int cvmm_abi_version(void) { return 4; }
+int cvmm_abi_version(void) { return 5; }
 
 const char* cvmm_last_error(void) { return t_err; }
 
@@ -314,8 +314,8 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld, const
                  const int64_t* out_index, const int64_t* offsets, int64_t n_routes,
                  const void* keys, int keys_dtype, int64_t n_experts, int64_t k_dim, int64_t n_dim,
                  int64_t ks_e, int64_t ks_k, int64_t ks_n, void* out, int out_dtype, int64_t out_ld,
-                 int op_dtype, const int32_t* x_pad_start, const int32_t* out_pad_start, void* workspace,
-                 size_t workspace_bytes, cvmm_stream_t stream) {
+                 int op_dtype, const int32_t* x_pad_start, const int32_t* out_pad_start, void* x_copy,
+                 void* workspace, size_t workspace_bytes, cvmm_stream_t stream) {
   if (!is_float_dtype(x_dtype) || !is_float_dtype(keys_dtype) || !is_float_dtype(out_dtype) ||
       !is_float_dtype(op_dtype))
     return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_forward: unsupported dtype");
@@ -323,6 +323,8 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld, const
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: the padded sorted layout needs x_dtype == op_dtype (bf16/fp16)");
   if (out_pad_start && op_dtype == F32)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: a padded sorted output needs a bf16/fp16 op_dtype");
+  if (x_copy && (op_dtype == F32 || x_pad_start))
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: x_copy needs a bf16/fp16 op_dtype and a row-indexed x");
   if (n_routes < 0 || n_experts <= 0 || k_dim < 0 || n_dim <= 0 || x_rows < 0 || x_ld < k_dim ||
       out_ld < n_dim)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward: bad sizes");
@@ -337,6 +339,7 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld, const
   p.b = keys; p.b_dtype = keys_dtype; p.bs_e = ks_e; p.bs_k = ks_k; p.bs_n = ks_n;
   p.c = out; p.c_dtype = out_dtype; p.c_ld = out_ld; p.c_index = out_index ? out_index : sel_index;
   p.c_pad_start = out_pad_start;
+  p.a_copy = x_copy;
   p.offsets = offsets; p.n_routes = n_routes; p.n_experts = n_experts; p.K = k_dim; p.N = n_dim;
   p.mode = 0; p.op_dtype = op_dtype;
   return run_row_gemm(p, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), "cvmm_forward");
@@ -485,6 +488,12 @@ int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_i
   // Sums split experts' partial slots in chunk order and zero-fills experts
   // without routes (the reference writes 0 for them, cvmm.py:476-478).
   return seg_reduce(ws.expert_slots, ws.partials, grad_w, n_experts, m_dim * n_dim, s);
+}
+
+int cvmm_pad_starts(const int64_t* offsets, int64_t n_experts, int32_t* pad_start, cvmm_stream_t stream) {
+  if (n_experts <= 0 || !offsets || !pad_start) return fail(CVMM_ERR_INVALID_ARG, "cvmm_pad_starts: bad arguments");
+  return pad_starts(offsets, n_experts, kPadRows, reinterpret_cast<int*>(pad_start),
+                    reinterpret_cast<cudaStream_t>(stream));
 }
 
 int cvmm_sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64_t* index, int64_t div,

@@ -26,7 +26,10 @@ struct RowGemm {
   const void* x; int x_dtype; int64_t x_ld;
   float* gsel;
   int op_dtype;
-  const int4* tiles;   // (expert, first sorted position, rows, 0) per M tile
+  const int4* tiles;   // (expert, first sorted position, rows, tile index) per M tile; with
+                       // 128-row tiles, tile t covers rows 128 t .. 128 t + 127 of the
+                       // expert-padded sorted layout
+  void* a_copy;        // non-null: also write the op-dtype A tiles there (expert-padded sorted layout)
   const int* a_pad_start;  // non-null: A is the expert-padded sorted layout (row = pad_start[e] + p - seg_begin(e))
   const int* c_pad_start;  // non-null: C is the expert-padded sorted layout (16-bit, mode 0; c_index unused)
   const int* n_tiles;  // number of valid entries in `tiles`

@@ -44,7 +44,7 @@ build_tiles_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int b
   int pos = v - cnt + (warp > 0 ? warp_tot[warp - 1] : 0);
   for (int64_t e = e0; e < e1; ++e) {
     int64_t b = seg_begin(offsets, e), end = offsets[e];
-    for (int64_t r = b; r < end; r += bm) tiles[pos++] = make_int4((int)e, (int)r, (int)min((int64_t)bm, end - r), 0);
+    for (int64_t r = b; r < end; r += bm, ++pos) tiles[pos] = make_int4((int)e, (int)r, (int)min((int64_t)bm, end - r), pos);
   }
   if (t == blockDim.x - 1) *n_tiles = pos;
 }

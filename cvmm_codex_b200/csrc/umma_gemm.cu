@@ -45,6 +45,7 @@ constexpr int BK = 64;              // K per stage: one 128-byte swizzle atom of
 constexpr int kProducers = 128;     // warps 0-3
 constexpr int kEpilogue = 128;      // warps 4-7
 constexpr int kMmaWarp = 8;
+constexpr int kFlagACopy = 1 << 17;  // row GEMM: write the gathered A tiles to RowGemm::a_copy
 constexpr int kThreads = 320;
 constexpr uint32_t kAtomRowsBytes = 64 * 128;  // one 64-row x 128-byte MN-major atom column
 
@@ -287,12 +288,12 @@ __device__ __forceinline__ void warp_store_block(void* c, int c_dtype, int64_t r
 // Barrier set-up and TMEM allocation (2 accumulator slots of BN columns).
 template <int BN, int S>
 __device__ __forceinline__ uint32_t setup(const Bars& b, int full_count, int idxe_count = kProducers,
-                                          int ready_count = 1, int epi_count = kEpilogue) {
+                                          int ready_count = 1, int epi_count = kEpilogue, int empty_count = 1) {
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       ptx::mbar_init(&b.full[s], full_count);
-      ptx::mbar_init(&b.empty[s], 1);
+      ptx::mbar_init(&b.empty[s], empty_count);
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&b.accf[a], 1);
@@ -317,11 +318,17 @@ __device__ __forceinline__ uint32_t setup(const Bars& b, int full_count, int idx
   return *b.tmem_slot;
 }
 
-// MMA issuer shared by both kernels: tile_nkb(t) gives the K stages of tile t.
-template <int BN, int S, class NkbFn>
+// MMA issuer shared by both kernels: tile_nkb(t) gives the K stages of tile t;
+// on_stage(t, kb, s) runs after stage s's MMAs are issued, and on_stage(-1,
+// 0, 0) once after the last.
+struct NoStageHook {
+  __device__ void operator()(int, int, int) const {}
+};
+
+template <int BN, int S, class NkbFn, class StageFn = NoStageHook>
 __device__ __forceinline__ void mma_loop(const Bars& b, uint64_t* consume, uint8_t* smem, uint32_t tmem,
                                          uint32_t idesc, bool a_mn, bool b_mn, int total, NkbFn tile_nkb,
-                                         bool skip_mma) {
+                                         bool skip_mma, StageFn on_stage = StageFn()) {
   using L = Smem<BN, S>;
   uint32_t it = 0;
   int local = 0;
@@ -353,10 +360,12 @@ __device__ __forceinline__ void mma_loop(const Bars& b, uint64_t* consume, uint8
         if (!skip_mma) ptx::mma_f16(d, ad, bd, idesc, (kb | j) != 0 ? 1u : 0u);
       }
       ptx::mma_commit(&b.empty[s]);
+      on_stage(tt, kb, s);
     }
     if (!ok) break;
     ptx::mma_commit(&b.accf[a]);
   }
+  on_stage(-1, 0, 0);
   // Everything issued must finish before TMEM is released.
   ptx::mma_commit(b.drain);
   ptx::mbar_wait(b.drain, 0, kTagDrain);
@@ -388,15 +397,16 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
   const int op = p.op_dtype;
   const bool a_fast = flags & 1, b_fast = flags & 2, c_vec = flags & 4;
   const uint32_t tmem = setup<BN, S>(bar, EPI2 ? 1 : (A_TMA ? 2 : kProducers + (B_TMA ? 1 : 0)), kProducers, 1,
-                                     EPI2 ? 2 * kEpilogue : kEpilogue);
+                                     EPI2 ? 2 * kEpilogue : kEpilogue, (flags & kFlagACopy) ? 2 : 1);
 
   auto entry = [&](int tt) -> int4 {
     return tt < total ? p.tiles[tt / n_n] : make_int4(0, 0, 0, 0);
   };
   // A row (before a_div) of tile row rr: gathered index, or the row of the
   // expert-padded sorted layout.
+  static_assert(BM == kPadRows, "padded rows follow from 128-row tile indices");
   auto a_row_of = [&](const int4& en, int rr) -> int {
-    if (p.a_pad_start) return p.a_pad_start[en.x] + (int)(en.y - seg_begin(p.offsets, en.x)) + rr;
+    if (p.a_pad_start) return (int)kPadRows * en.w + rr;
     return (int)p.a_index[en.y + rr];
   };
   const bool a_dense = flags & 32;
@@ -571,7 +581,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
       const bool row_ok = crow >= 0;
       float wv = 0.f, dot = 0.f;
       if (p.mode == 1 && row_ok) wv = round_to(load_as_float(p.w, p.w_dtype, crow), op);
-      const int prow0 = c_dense ? p.c_pad_start[ent.x] + (int)(ent.y - seg_begin(p.offsets, ent.x)) + ew * 32 : 0;
+      const int prow0 = (int)kPadRows * ent.w + ew * 32;  // dense C: this warp's first padded row
       for (int ch = c_lo / 64; ch < c_hi / 64; ++ch) {
         if (n0 + ch * 64 >= p.N) break;
         if (ch > c_lo / 64) load_x(crow, n0 + ch * 64);
@@ -657,8 +667,41 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = ptx::instr_desc_f16(BM, BN, op == BF16, false, !B_KMAJOR);
-      mma_loop<BN, S>(bar, bar.full, smem, tmem, idesc, false, !B_KMAJOR, total, [&](int) { return nkb; },
-                      CVMM_DBG(flags, 256));
+      if (flags & kFlagACopy) {
+        // Store-back of the gathered A tiles: the stage's A tile (op dtype,
+        // 128-byte swizzle) goes to its padded rows by TMA; the stage is
+        // released (second arrival on `empty`) once that store has read it,
+        // two stages later, so stores overlap the next stages' MMAs.
+        int q0 = -1, q1 = -1;
+        auto store_a = [&](int tt, int kb, int s) {
+          if (tt < 0) {
+            ptx::bulk_wait_read<0>();
+            if (q0 >= 0) ptx::mbar_arrive(&bar.empty[q0]);
+            if (q1 >= 0) ptx::mbar_arrive(&bar.empty[q1]);
+            ptx::bulk_wait_all();
+            return;
+          }
+          if (tt % n_n == 0)
+            ptx::tma_store_2d(&tmap_a, ptx::smem_u32(smem + s * L::stage_bytes), kb * BK,
+                              (int)kPadRows * entry(tt).w);
+          ptx::bulk_commit();
+          if (q1 >= 0) {
+            ptx::bulk_wait_read<2>();
+            ptx::mbar_arrive(&bar.empty[q0]);
+            q0 = q1;
+            q1 = s;
+          } else if (q0 >= 0) {
+            q1 = s;
+          } else {
+            q0 = s;
+          }
+        };
+        mma_loop<BN, S>(bar, bar.full, smem, tmem, idesc, false, !B_KMAJOR, total, [&](int) { return nkb; },
+                        CVMM_DBG(flags, 256), store_a);
+      } else {
+        mma_loop<BN, S>(bar, bar.full, smem, tmem, idesc, false, !B_KMAJOR, total, [&](int) { return nkb; },
+                        CVMM_DBG(flags, 256));
+      }
     }
     __syncwarp();
   } else if (B_TMA && lane == 0) {
@@ -1130,6 +1173,14 @@ static int row_launch(const RowGemm& p, int64_t max_tiles, int flags, cudaStream
   const bool a_tma = a_dense || (tma && (flags & 1) && (dbg_flags() & 8192) &&
                                  make_rows_map(&amap, p.a, p.op_dtype, p.K, p.a_rows, p.a_ld));
   if (a_dense) flags |= 32;
+  // A copy (the forward writing the expert-padded sorted x): gathered A only;
+  // the map over the copy takes tmap_a's place, unused on that path.
+  if (p.a_copy) {
+    if (a_tma ||
+        !make_rows_map(&amap, p.a_copy, p.op_dtype, p.K, p.n_routes + kPadRows * p.n_experts, p.K, BM))
+      return fail(CVMM_ERR_INVALID_ARG, "A copy needs a gathered A operand, 16-bit arithmetic and 16-byte aligned rows");
+    flags |= kFlagACopy;
+  }
   // Dense C: expert-padded sorted 16-bit output written by 32-row TMA boxes.
   CUtensorMap cmap;
   memset(&cmap, 0, sizeof(cmap));

@@ -19,7 +19,7 @@ from ._lib import check, dtype_code, ptr
 KERNELS_PER_CALL = {
     "cvmm_sel_prepare": 10, "cvmm_expert_offsets": 1, "cvmm_forward": 2, "cvmm_backward_x": 2,
     "cvmm_backward_w": 4, "cvmm_weighted_combine": 1, "cvmm_sum_routes": 1,
-    "cvmm_weighted_token_backward": 1, "cvmm_cast": 1, "cvmm_sort_rows_padded": 2,
+    "cvmm_weighted_token_backward": 1, "cvmm_cast": 1, "cvmm_sort_rows_padded": 2, "cvmm_pad_starts": 1,
 }
 
 
@@ -161,11 +161,13 @@ def _gemm_ws(lib, n_routes, n_experts, dev, m_dim=0, n_dim=0, op_dtype=torch.bfl
 def forward(x: torch.Tensor, sel_index: torch.Tensor, offsets: torch.Tensor, keys: torch.Tensor,
             out_index: Optional[torch.Tensor], out_dtype: torch.dtype,
             op_dtype: torch.dtype, x_pad_start: Optional[torch.Tensor] = None,
-            out_pad_start: Optional[torch.Tensor] = None) -> torch.Tensor:
+            out_pad_start: Optional[torch.Tensor] = None, x_copy: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Y[row_p] = x[sel_index[p]] @ keys[e_p] for every sorted route p; Y is [R, N]
     (reference cvmm_triton, cvmm.py:815-867). With x_pad_start, x is the
     expert-padded sorted layout from sort_rows_padded; with out_pad_start, Y is
-    returned in that layout ([R + E*PAD_ROWS, N], read through padded_route_rows)."""
+    returned in that layout ([R + E*PAD_ROWS, N], read through padded_route_rows).
+    With x_copy ([R + E*PAD_ROWS, K], op dtype), the forward also writes the
+    expert-padded sorted copy of the x rows it gathers there."""
     _require_cuda(x, sel_index, offsets, keys, out_index)
     lib = _lib.load()
     x2 = _rows(x)
@@ -182,7 +184,7 @@ def forward(x: torch.Tensor, sel_index: torch.Tensor, offsets: torch.Tensor, key
                               ptr(keys), dtype_code(keys.dtype), E, K, N,
                               keys.stride(0), keys.stride(1), keys.stride(2),
                               ptr(out), dtype_code(out_dtype), out.stride(0), dtype_code(op_dtype),
-                              ptr(x_pad_start), ptr(out_pad_start), ptr(ws), ws.numel(), stream)
+                              ptr(x_pad_start), ptr(out_pad_start), ptr(x_copy), ptr(ws), ws.numel(), stream)
     check(rc, "cvmm_forward")
     return out
 
@@ -295,6 +297,17 @@ def backward_w(x: torch.Tensor, x_index: torch.Tensor, x_div: int, g: torch.Tens
 
 
 PAD_ROWS = 128  # CVMM_PAD_ROWS
+
+
+def pad_starts(offsets: torch.Tensor, n_experts: int) -> torch.Tensor:
+    """pad_start int32 [E] of the expert-padded sorted layout for these offsets."""
+    _require_cuda(offsets)
+    lib = _lib.load()
+    out = torch.empty(int(n_experts), dtype=torch.int32, device=offsets.device)
+    with _Device(offsets.device) as stream:
+        rc = _invoke("cvmm_pad_starts", lib.cvmm_pad_starts, ptr(offsets), int(n_experts), ptr(out), stream)
+    check(rc, "cvmm_pad_starts")
+    return out
 
 
 def sort_rows_padded(src: torch.Tensor, index: torch.Tensor, div: int, sorted_sel: torch.Tensor,

@@ -52,7 +52,7 @@ typedef struct CUstream_st* cvmm_stream_t; /* == cudaStream_t */
 #define CVMM_DEV_BAD_INDEX 2
 
 /* ABI version of this header; bumped on any signature change. */
-int cvmm_abi_version(void);  /* 4 */
+int cvmm_abi_version(void);  /* 5 */
 
 /* Message for the last failed call on the calling host thread. */
 const char* cvmm_last_error(void);
@@ -136,8 +136,8 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld,
                  int64_t n_routes, const void* keys, int keys_dtype, int64_t n_experts,
                  int64_t k_dim, int64_t n_dim, int64_t ks_e, int64_t ks_k, int64_t ks_n,
                  void* out, int out_dtype, int64_t out_ld, int op_dtype,
-                 const int32_t* x_pad_start, const int32_t* out_pad_start, void* workspace,
-                 size_t workspace_bytes, cvmm_stream_t stream);
+                 const int32_t* x_pad_start, const int32_t* out_pad_start, void* x_copy,
+                 void* workspace, size_t workspace_bytes, cvmm_stream_t stream);
 /* With x_pad_start != NULL, x is the expert-padded sorted layout made by
  * cvmm_sort_rows_padded: the x row of sorted position p is then
  * x_pad_start[e] + p - seg_begin(e), x_rows is ignored, and sel_index only
@@ -148,7 +148,13 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld,
  * n_routes + n_experts * CVMM_PAD_ROWS rows, padding rows included) by dense
  * tensor-memory-to-TMA stores; out_index is then ignored. bf16/fp16 out_dtype
  * and op_dtype, 16-byte aligned rows. Read it back per route through
- * cvmm_padded_route_rows. */
+ * cvmm_padded_route_rows.
+ * With x_copy != NULL (row-indexed x, bf16/fp16 op_dtype), the forward also
+ * writes the op_dtype rows it gathers into x_copy in the expert-padded sorted
+ * layout ([n_routes + n_experts * CVMM_PAD_ROWS, k_dim], padding rows zero),
+ * exactly what cvmm_sort_rows_padded would produce; cvmm_pad_starts gives its
+ * pad_start for the grad-W call. This replaces a separate copy pass (the
+ * reference's grouped-x copy, cvmm.py:1123-1138). */
 
 /* Weighted combine of the forward: out[t] = cast( sum_j cast_y(w[t,j]) * y[t*top_k+j] ),
  * fp32 accumulate. Replaces the bmm at cvmm.py:1543-1545. */
@@ -226,6 +232,8 @@ int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_i
  * cvmm_forward, cvmm_backward_x and cvmm_backward_w.
  * ------------------------------------------------------------------------ */
 #define CVMM_PAD_ROWS 128
+/* pad_start[e] of the expert-padded sorted layout for these offsets. */
+int cvmm_pad_starts(const int64_t* offsets, int64_t n_experts, int32_t* pad_start, cvmm_stream_t stream);
 int cvmm_sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64_t* index,
                           int64_t div, const void* scale, int scale_dtype,
                           const int32_t* sorted_sel, const int64_t* offsets, int64_t n_routes,

@@ -148,3 +148,27 @@ def test_sort_rows_padded_matches_oracle(src_dtype, dst_dtype, scaled):
         want[want_ps[e] + p_ - seg[e]] = row
     got = dst[: int(padded.sum())].float().cpu().numpy()
     np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("x_dtype,d_in", [(torch.bfloat16, 256), (torch.float32, 136), (torch.bfloat16, 72)])
+def test_forward_x_copy_equals_sorted_copy(x_dtype, d_in):
+    """The forward's store-back of the rows it gathers (x_copy) is the
+    expert-padded sorted copy that cvmm_sort_rows_padded makes, bit for bit,
+    padding rows included; the forward output is unchanged by it."""
+    g = torch.Generator().manual_seed(8)
+    T, k, E, N = 900, 3, 7, 128
+    sel = torch.randint(0, E, (T, k), generator=g)
+    sel[: T // 2, 1] = 5  # one expert over several tiles
+    x = torch.randn(T, d_in, generator=g).to(x_dtype).cuda()
+    keys = (torch.randn(E, d_in, N, generator=g) / d_in ** 0.5).bfloat16().cuda()
+    s = C.cvmm_prepare_sel2(sel.cuda())
+    offs = ops.expert_offsets(s.sel, E)
+    want, wpad = ops.sort_rows_padded(x, s.sel_index, 1, s.sel, offs, E, dtype=torch.bfloat16)
+    pad = ops.pad_starts(offs, E)
+    assert torch.equal(pad, wpad)
+    xs = torch.full_like(want, float("nan"))
+    y = ops.forward(x, s.sel_index, offs, keys, s.out_index, torch.bfloat16, torch.bfloat16, x_copy=xs)
+    used = int(pad[-1].item()) + (int(offs[-1].item() - (offs[-2].item() if E > 1 else 0)) + 127) // 128 * 128
+    assert torch.equal(xs[:used], want[:used])
+    y_ref = ops.forward(x, s.sel_index, offs, keys, s.out_index, torch.bfloat16, torch.bfloat16)
+    assert torch.equal(y, y_ref)
