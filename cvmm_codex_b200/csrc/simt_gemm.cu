@@ -334,7 +334,8 @@ __global__ void __launch_bounds__(256) sort_rows_padded_kernel(
         if (m.dst < 0) continue;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          x[u][j] = round_to(x[u][j], dst_dtype);
+          // Values already in dst_dtype need no re-rounding (identity).
+          if (src_dtype != dst_dtype) x[u][j] = round_to(x[u][j], dst_dtype);
           if (scale) x[u][j] = x[u][j] * m.scale;
         }
         store8(dst + (m.dst + ((uint32_t)it % pr) * 8) * dsz, dst_dtype, x[u]);
