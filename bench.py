@@ -345,14 +345,21 @@ def call_work(w, name):
         return R * 4 + E * 8, 0.0
     if name == "cvmm_cast":
         return wts * (4 + 2), 0.0
-    if name == "cvmm_sort_rows_padded":  # mean of the x copy and the grad copy
+    if name == "cvmm_sort_rows_padded":
+        # weighted: the x copy and the weight-scaled grad copy (mean of the two
+        # calls); unweighted: the grad copy (the forward writes the x copy)
         x_copy = (R if w.route_input else T) * di * 2 + R * di * 2
         g_copy = (T * do * 2 + R * 4 if w.weighted else R * do * 2) + R * do * 2
-        return (x_copy + g_copy) / 2, 0.0
+        return ((x_copy + g_copy) / 2 if w.weighted else g_copy), 0.0
+    if name == "cvmm_pad_starts":
+        return E * 8 + E * 4, 0.0
     if name == "cvmm_padded_route_rows":
         return R * 16, 0.0
     if name == "cvmm_forward":
-        return R * di * 2 + wts * 2 + R * do * 2, gemm
+        if w.weighted:  # sorted x in, padded route outputs out
+            return R * di * 2 + wts * 2 + R * do * 2, gemm
+        # gathered token rows in, route outputs and the sorted x copy out
+        return (R if w.route_input else T) * di * 2 + wts * 2 + R * do * 2 + R * di * 2, gemm
     if name == "cvmm_backward_w":
         return R * di * 2 + R * do * 2 + wts * 4, gemm
     if name == "cvmm_backward_x":
