@@ -76,26 +76,37 @@ __device__ __forceinline__ unsigned int digit_of(int32_t key, unsigned int mn, i
   return ((bias(key) - mn) >> shift) & (kBins - 1);
 }
 
-// counts layout: counts[bin * n_chunks + chunk] so that one exclusive scan in
-// memory order yields every (bin, chunk) base position.
+// Digit histogram of this CTA's warp chunks, one row per warp, in `hist`.
+__device__ __forceinline__ void cta_histogram(const int32_t* __restrict__ keys, int64_t n, int64_t n_chunks,
+                                              int64_t chunk_len, unsigned int mn, int shift, int nb,
+                                              int (*hist)[kBins]) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t chunk = (int64_t)blockIdx.x * kWarpsPerCta + warp;
+  for (int b = lane; b < nb; b += 32) hist[warp][b] = 0;
+  __syncwarp();
+  if (chunk < n_chunks) {
+    const int64_t beg = chunk * chunk_len;
+    const int64_t end = min(beg + chunk_len, n);
+    for (int64_t i = beg + lane; i < end; i += 32) atomicAdd(&hist[warp][digit_of(keys[i], mn, shift)], 1);
+  }
+  __syncthreads();
+}
+
+// counts layout: counts[bin * n_cta + cta] (one column per CTA of kWarpsPerCta
+// warp chunks), so that one exclusive scan in memory order yields every
+// (bin, CTA) base position; the warps of a CTA are ordered inside the scatter.
 __global__ void __launch_bounds__(kWarpsPerCta * 32)
 hist_kernel(const int32_t* __restrict__ keys, int64_t n, int64_t n_chunks, int64_t chunk_len,
             const Header* __restrict__ h, int shift, int* __restrict__ counts) {
   if (!pass_needed(h, shift)) return;
   __shared__ int hist[kWarpsPerCta][kBins];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t chunk = (int64_t)blockIdx.x * kWarpsPerCta + warp;
   const int nb = n_bins(h, shift);
-  const unsigned int mn = ~h->max_nu;
-  int* my = hist[warp];
-  for (int b = lane; b < nb; b += 32) my[b] = 0;
-  __syncwarp();
-  if (chunk < n_chunks) {
-    const int64_t beg = chunk * chunk_len;
-    const int64_t end = min(beg + chunk_len, n);
-    for (int64_t i = beg + lane; i < end; i += 32) atomicAdd(&my[digit_of(keys[i], mn, shift)], 1);
-    __syncwarp();
-    for (int b = lane; b < nb; b += 32) counts[(int64_t)b * n_chunks + chunk] = my[b];
+  cta_histogram(keys, n, n_chunks, chunk_len, ~h->max_nu, shift, nb, hist);
+  for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+    int c = 0;
+#pragma unroll
+    for (int w = 0; w < kWarpsPerCta; ++w) c += hist[w][b];
+    counts[(int64_t)b * gridDim.x + blockIdx.x] = c;
   }
 }
 
@@ -186,13 +197,24 @@ scatter_kernel(const int32_t* __restrict__ keys_in, const int32_t* __restrict__ 
   __shared__ int ctr[kWarpsPerCta][kBins];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t chunk = (int64_t)blockIdx.x * kWarpsPerCta + warp;
-  if (chunk >= n_chunks) return;
   const int nb = n_bins(h, shift);
   const unsigned int mn = ~h->max_nu;
   const bool last = shift + kDigitBits >= 32 || (key_range(h) >> (shift + kDigitBits)) == 0u;
+  // Each warp's first position per bin: the CTA's base plus the counts of the
+  // CTA's earlier warps (stable: warp chunks are in route order).
+  cta_histogram(keys_in, n, n_chunks, chunk_len, mn, shift, nb, ctr);
+  for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+    int run = base[(int64_t)b * gridDim.x + blockIdx.x];
+#pragma unroll
+    for (int w = 0; w < kWarpsPerCta; ++w) {
+      const int c = ctr[w][b];
+      ctr[w][b] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  if (chunk >= n_chunks) return;
   int* my = ctr[warp];
-  for (int b = lane; b < nb; b += 32) my[b] = base[(int64_t)b * n_chunks + chunk];
-  __syncwarp();
   const int64_t beg = chunk * chunk_len;
   const int64_t end = min(beg + chunk_len, n);
   const unsigned int lt_mask = (1u << lane) - 1u;
@@ -302,7 +324,7 @@ int sel_prepare(const void* sel_ptr, int sel_dtype, int64_t n, int64_t top_k, in
     int32_t* kout = buf[(p & 1) * 2];
     int32_t* vout = buf[(p & 1) * 2 + 1];
     sel::hist_kernel<<<cta, sel::kWarpsPerCta * 32, 0, stream>>>(kin, n, n_chunks, clen, h, shift, counts);
-    sel::scan_kernel<<<1, 1024, 0, stream>>>(counts, n_chunks, h, shift);
+    sel::scan_kernel<<<1, 1024, 0, stream>>>(counts, cta, h, shift);
     sel::scatter_kernel<<<cta, sel::kWarpsPerCta * 32, 0, stream>>>(
         kin, vin, n, n_chunks, clen, h, shift, counts, kout, vout, sorted_sel, sel_index, out_index,
         top_k, route_input);
