@@ -451,7 +451,7 @@ def cpu_baseline(w, budget_s: float):
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    n_tok = max(64, min(w.T, 1024))
+    n_tok = max(64, min(w.T, 2048))
     d = cb.make_sample(w, n_tok)
     cb.step(w, d)  # warm
     t0 = time.perf_counter()
@@ -480,7 +480,7 @@ def run_reference(args, rank):
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    n_tok = max(64, min(w.T, 512))
+    n_tok = max(64, min(w.T, 2048))
     d = cb.make_sample(w, n_tok)
     for _ in range(min(args.warmup, 3)):
         cb.step(w, d)
