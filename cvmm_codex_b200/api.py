@@ -194,7 +194,8 @@ class CVMM(torch.autograd.Function):
         if reduction_weight is None and _sortable(x, op_dtype):
             # The forward gathers x's rows anyway: it writes that sorted padded
             # copy for the grad-W as it goes, instead of a separate copy pass.
-            xpad = ops.pad_starts(offsets, n_experts)
+            # Its pad starts depend only on the offsets; the backward takes them
+            # from the grad copy it makes anyway.
             xs = torch.empty((sel_index.numel() + n_experts * ops.PAD_ROWS, x.shape[-1]), dtype=op_dtype,
                              device=x.device)
             res = ops.forward(x, sel_index, offsets, keys_op, out_index, op_dtype, op_dtype, x_copy=xs)
@@ -246,6 +247,8 @@ class CVMM(torch.autograd.Function):
                 # them as dense tensor-core tiles.
                 g_rows, g_pad = ops.sort_rows_padded(g2, route, 1, sel, offsets, n_experts, dtype=op)
                 g_idx = None
+            if xs is not None and xpad is None:
+                xpad = g_pad if g_pad is not None else ops.pad_starts(offsets, n_experts)
             if need_keys:
                 # dW_e = sum_p x[sel_index[p]]^T g[route[p]]  (cvmm.py:1163-1198)
                 if xs is not None:

@@ -245,11 +245,17 @@ static int run_row_gemm(RowGemm& p, void* ws, size_t ws_bytes, cudaStream_t stre
   if (rc) return rc;
   const bool tensor = p.op_dtype != F32;
   const int bm = tensor ? 128 : 64;
-  int4* tiles = static_cast<int4*>(g.tiles);
-  rc = build_tiles(p.offsets, p.n_experts, bm, tiles, g.count, stream);
-  if (rc) return rc;
-  p.tiles = tiles;
-  p.n_tiles = g.count;
+  if (tensor && p.n_experts <= kRowPlanExperts) {
+    // The tensor-core kernel derives its tile table from the offsets itself.
+    p.tiles = nullptr;
+    p.n_tiles = nullptr;
+  } else {
+    int4* tiles = static_cast<int4*>(g.tiles);
+    rc = build_tiles(p.offsets, p.n_experts, bm, tiles, g.count, stream);
+    if (rc) return rc;
+    p.tiles = tiles;
+    p.n_tiles = g.count;
+  }
   const int64_t max_tiles = max_row_tiles(p.n_routes, p.n_experts, bm);
   return tensor ? launch_row_gemm_umma(p, max_tiles, stream) : launch_row_gemm_simt(p, max_tiles, stream);
 }

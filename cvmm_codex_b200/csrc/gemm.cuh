@@ -64,6 +64,9 @@ struct SegGemm {
 constexpr int64_t kRouteRowsPad = 128;
 // Rows each expert segment of the expert-padded sorted layout is padded to.
 constexpr int64_t kPadRows = CVMM_PAD_ROWS;
+// Experts up to which the tensor-core row GEMM builds its tile table in the
+// kernel (RowGemm::tiles == nullptr) instead of reading one from build_tiles.
+constexpr int64_t kRowPlanExperts = 1024;
 int pad_starts(const int64_t* offsets, int64_t n_experts, int64_t pad, int* pad_start, cudaStream_t stream);
 int sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64_t* index, int64_t div,
                      const void* scale, int scale_dtype, const int32_t* sorted_sel, const int64_t* offsets,

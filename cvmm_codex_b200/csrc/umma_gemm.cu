@@ -92,6 +92,7 @@ constexpr uint32_t kStoreBox = 32 * 128;                  // one 32-row x 64-col
 constexpr uint32_t kStagingBytes = 8 * 32 * kStageRowBytes;
 static_assert(kStagingBytes >= 8 * kStoreBox, "staging too small");
 constexpr int kRingEntries = 72;
+constexpr int kPlanExperts = (int)kRowPlanExperts;  // experts up to which the row GEMM builds its tile table itself
 struct IdxSlot {
   int x[kRingEntries];
   int g[kRingEntries];
@@ -109,7 +110,10 @@ struct Smem {
   static constexpr uint32_t misc = bars + (5 * S + 5) * 8;  // tmem slot, abort flag
   static constexpr uint32_t staging = (misc + 16 + 1023) / 1024 * 1024;  // swizzled TMA store boxes
   static constexpr uint32_t ring = staging + kStagingBytes;
-  static constexpr uint32_t used = ring + S * (uint32_t)sizeof(IdxSlot);
+  // Row GEMM tile plan built in the kernel: first tile and segment start of
+  // every expert (kPlanExperts + 1 entries each) and the scan's warp totals.
+  static constexpr uint32_t plan = ring + S * (uint32_t)sizeof(IdxSlot);
+  static constexpr uint32_t used = plan + (2 * (kPlanExperts + 1) + 32) * 4;
   static constexpr uint32_t alloc = used + 1024;  // slack to align the base
   static_assert(alloc <= 232448, "shared memory plan exceeds 227 KiB");
   static_assert(staging % 1024 == 0 && kStageRowBytes % 16 == 0 && ring % 16 == 0, "misaligned smem region");
@@ -392,7 +396,33 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
   uint8_t* smem = align_smem(smem_raw);
   const Bars bar = carve_bars<L, S>(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total = *p.n_tiles * n_n;
+  // Tile table: 128-route M tiles of every expert segment, in expert order.
+  // Without a table from the host (p.tiles == nullptr, at most kPlanExperts
+  // experts) every CTA derives it from the offsets: tstart[e] = first tile of
+  // expert e, sbeg[e] = its first sorted route (sbeg[E] = n_routes).
+  int* tstart = reinterpret_cast<int*>(smem + L::plan);
+  int* sbeg = tstart + kPlanExperts + 1;
+  const bool own_tiles = p.tiles == nullptr;
+  const int n_exp = (int)p.n_experts;
+  if (own_tiles) {
+    const int per = (n_exp + (int)blockDim.x - 1) / (int)blockDim.x;
+    const int e0 = min((int)threadIdx.x * per, n_exp), e1 = min(e0 + per, n_exp);
+    int cnt = 0;
+    for (int e = e0; e < e1; ++e) cnt += (int)((p.offsets[e] - seg_begin(p.offsets, e) + BM - 1) / BM);
+    int run = block_exclusive_scan(cnt, sbeg + kPlanExperts + 1);
+    for (int e = e0; e < e1; ++e) {
+      const int64_t b = seg_begin(p.offsets, e);
+      tstart[e] = run;
+      sbeg[e] = (int)b;
+      run += (int)((p.offsets[e] - b + BM - 1) / BM);
+    }
+    if (threadIdx.x == blockDim.x - 1) {
+      tstart[n_exp] = run;
+      sbeg[n_exp] = (int)p.offsets[n_exp - 1];
+    }
+    __syncthreads();
+  }
+  const int total = (own_tiles ? tstart[n_exp] : *p.n_tiles) * n_n;
   const int nkb = (int)((p.K + BK - 1) / BK);
   const int op = p.op_dtype;
   const bool a_fast = flags & 1, b_fast = flags & 2, c_vec = flags & 4;
@@ -400,7 +430,16 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
                                      EPI2 ? 2 * kEpilogue : kEpilogue, (flags & kFlagACopy) ? 2 : 1);
 
   auto entry = [&](int tt) -> int4 {
-    return tt < total ? p.tiles[tt / n_n] : make_int4(0, 0, 0, 0);
+    if (tt >= total) return make_int4(0, 0, 0, 0);
+    const int m = tt / n_n;
+    if (!own_tiles) return p.tiles[m];
+    int lo = 0, hi = n_exp - 1;  // last expert with tstart[e] <= m (its tiles hold m)
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (tstart[mid] <= m) lo = mid; else hi = mid - 1;
+    }
+    const int r0 = sbeg[lo] + BM * (m - tstart[lo]);
+    return make_int4(lo, r0, min(BM, sbeg[lo + 1] - r0), m);
   };
   // A row (before a_div) of tile row rr: gathered index, or the row of the
   // expert-padded sorted layout.

@@ -153,6 +153,12 @@ def expert_offsets(sorted_sel: torch.Tensor, n_experts: int) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------ GEMMs
+ROW_PLAN_EXPERTS = 1024  # kRowPlanExperts: tensor-core row GEMMs build their tile table in-kernel
+
+
+def _row_gemm_launches(op_dtype: torch.dtype, n_experts: int) -> int:
+    return 1 if op_dtype != torch.float32 and n_experts <= ROW_PLAN_EXPERTS else 2
+
 def _gemm_ws(lib, n_routes, n_experts, dev, m_dim=0, n_dim=0, op_dtype=torch.bfloat16):
     return _ws(lib.cvmm_gemm_workspace_size(n_routes, n_experts, m_dim, n_dim, 0, 0,
                                             dtype_code(op_dtype), 0), dev)
@@ -184,7 +190,8 @@ def forward(x: torch.Tensor, sel_index: torch.Tensor, offsets: torch.Tensor, key
                               ptr(keys), dtype_code(keys.dtype), E, K, N,
                               keys.stride(0), keys.stride(1), keys.stride(2),
                               ptr(out), dtype_code(out_dtype), out.stride(0), dtype_code(op_dtype),
-                              ptr(x_pad_start), ptr(out_pad_start), ptr(x_copy), ptr(ws), ws.numel(), stream)
+                              ptr(x_pad_start), ptr(out_pad_start), ptr(x_copy), ptr(ws), ws.numel(), stream,
+                              kernels=_row_gemm_launches(op_dtype, E))
     check(rc, "cvmm_forward")
     return out
 
@@ -260,7 +267,8 @@ def backward_x(g: torch.Tensor, g_index: Optional[torch.Tensor], g_div: int, out
                                  ptr(w2), dtype_code(w2.dtype) if w2 is not None else 0,
                                  ptr(x2), dtype_code(x2.dtype) if x2 is not None else 0,
                                  x2.stride(0) if x2 is not None else 0, ptr(gsel),
-                                 dtype_code(op_dtype), ptr(g_pad_start), ptr(out_pad_start), ptr(ws), ws.numel(), stream)
+                                 dtype_code(op_dtype), ptr(g_pad_start), ptr(out_pad_start), ptr(ws), ws.numel(), stream,
+                                 kernels=_row_gemm_launches(op_dtype, E))
     check(rc, "cvmm_backward_x")
     return out if mode == 0 else (out, gsel)
 
