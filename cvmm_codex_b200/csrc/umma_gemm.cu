@@ -1,6 +1,6 @@
 // tcgen05 (5th-generation tensor core) grouped GEMMs for bf16/fp16 arithmetic.
 //
-// Both kernels are persistent and warp-specialised (320 threads, one CTA per
+// Both kernels are persistent and warp-specialised (352 threads, one CTA per
 // SM, tiles assigned round-robin):
 //   warps 0-3  producers: gather the operand rows of every stage with 16-byte
 //              cp.async straight into the 128-byte-swizzled shared-memory
@@ -12,7 +12,10 @@
 //              one output row per thread), convert and store them;
 //   warp 8     allocates TMEM (two accumulator slots) and its lane 0 issues
 //              tcgen05.mma (M=128, N=BN, K=16) and tcgen05.commit;
-//   warp 9     lane 0 loads the expert-weight tiles with TMA (row GEMM).
+//   warp 9     lane 0 loads the expert-weight tiles with TMA (row GEMM) or
+//              stages route rows for the grad-W index ring;
+//   warp 10    lane 0 stores the gathered A tiles back as the expert-padded
+//              sorted copy when the row GEMM is asked for one (forward).
 // Barriers: full[s] / empty[s] per smem stage (S stages), acc_full[a] /
 // acc_empty[a] per TMEM accumulator slot (2 slots), so the epilogue of tile i
 // overlaps the main loop of tile i+1.
@@ -46,7 +49,9 @@ constexpr int kProducers = 128;     // warps 0-3
 constexpr int kEpilogue = 128;      // warps 4-7
 constexpr int kMmaWarp = 8;
 constexpr int kFlagACopy = 1 << 17;  // row GEMM: write the gathered A tiles to RowGemm::a_copy
-constexpr int kThreads = 320;
+constexpr int kLoaderWarp = 9;
+constexpr int kStoreWarp = 10;  // row GEMM with an A copy: stores the gathered A tiles
+constexpr int kThreads = 352;
 constexpr uint32_t kAtomRowsBytes = 64 * 128;  // one 64-row x 128-byte MN-major atom column
 
 // Development-only knobs (compiled in with -DCVMM_TRACE; absent from the
@@ -322,17 +327,11 @@ __device__ __forceinline__ uint32_t setup(const Bars& b, int full_count, int idx
   return *b.tmem_slot;
 }
 
-// MMA issuer shared by both kernels: tile_nkb(t) gives the K stages of tile t;
-// on_stage(t, kb, s) runs after stage s's MMAs are issued, and on_stage(-1,
-// 0, 0) once after the last.
-struct NoStageHook {
-  __device__ void operator()(int, int, int) const {}
-};
-
-template <int BN, int S, class NkbFn, class StageFn = NoStageHook>
+// MMA issuer shared by both kernels: tile_nkb(t) gives the K stages of tile t.
+template <int BN, int S, class NkbFn>
 __device__ __forceinline__ void mma_loop(const Bars& b, uint64_t* consume, uint8_t* smem, uint32_t tmem,
                                          uint32_t idesc, bool a_mn, bool b_mn, int total, NkbFn tile_nkb,
-                                         bool skip_mma, StageFn on_stage = StageFn()) {
+                                         bool skip_mma) {
   using L = Smem<BN, S>;
   uint32_t it = 0;
   int local = 0;
@@ -364,12 +363,10 @@ __device__ __forceinline__ void mma_loop(const Bars& b, uint64_t* consume, uint8
         if (!skip_mma) ptx::mma_f16(d, ad, bd, idesc, (kb | j) != 0 ? 1u : 0u);
       }
       ptx::mma_commit(&b.empty[s]);
-      on_stage(tt, kb, s);
     }
     if (!ok) break;
     ptx::mma_commit(&b.accf[a]);
   }
-  on_stage(-1, 0, 0);
   // Everything issued must finish before TMEM is released.
   ptx::mma_commit(b.drain);
   ptx::mbar_wait(b.drain, 0, kTagDrain);
@@ -706,23 +703,32 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = ptx::instr_desc_f16(BM, BN, op == BF16, false, !B_KMAJOR);
-      if (flags & kFlagACopy) {
-        // Store-back of the gathered A tiles: the stage's A tile (op dtype,
-        // 128-byte swizzle) goes to its padded rows by TMA; the stage is
-        // released (second arrival on `empty`) once that store has read it,
-        // two stages later, so stores overlap the next stages' MMAs.
-        int q0 = -1, q1 = -1;
-        auto store_a = [&](int tt, int kb, int s) {
-          if (tt < 0) {
-            ptx::bulk_wait_read<0>();
-            if (q0 >= 0) ptx::mbar_arrive(&bar.empty[q0]);
-            if (q1 >= 0) ptx::mbar_arrive(&bar.empty[q1]);
-            ptx::bulk_wait_all();
-            return;
+      mma_loop<BN, S>(bar, bar.full, smem, tmem, idesc, false, !B_KMAJOR, total, [&](int) { return nkb; },
+                      CVMM_DBG(flags, 256));
+    }
+    __syncwarp();
+  } else if (warp == kStoreWarp) {
+    // ------------------------------------------------------------ A tile store-back
+    // Each full stage's A tile (op dtype, already in the 128-byte swizzle TMA
+    // uses) goes to its rows of the expert-padded sorted copy; the stage is
+    // released (second arrival on `empty`, after the MMAs' commit) once the
+    // store has read it, two stages later, so stores stay in flight while
+    // this thread moves on. A separate warp keeps these waits off the MMA issue.
+    if ((flags & kFlagACopy) && lane == 0) {
+      uint32_t it = 0;
+      int q0 = -1, q1 = -1;
+      bool aborted = false;
+      for (int tt = blockIdx.x; tt < total && !aborted; tt += gridDim.x) {
+        const int prow = (int)kPadRows * entry(tt).w;
+        const bool store = tt % n_n == 0;  // the A tile is the same for every column tile
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % S;
+          if (!ptx::mbar_wait_or_abort(&bar.full[s], (it / S) & 1, kTagFull, bar.abort)) {
+            aborted = true;
+            break;
           }
-          if (tt % n_n == 0)
-            ptx::tma_store_2d(&tmap_a, ptx::smem_u32(smem + s * L::stage_bytes), kb * BK,
-                              (int)kPadRows * entry(tt).w);
+          ptx::fence_proxy_async_smem();
+          if (store) ptx::tma_store_2d(&tmap_a, ptx::smem_u32(smem + s * L::stage_bytes), kb * BK, prow);
           ptx::bulk_commit();
           if (q1 >= 0) {
             ptx::bulk_wait_read<2>();
@@ -734,16 +740,14 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
           } else {
             q0 = s;
           }
-        };
-        mma_loop<BN, S>(bar, bar.full, smem, tmem, idesc, false, !B_KMAJOR, total, [&](int) { return nkb; },
-                        CVMM_DBG(flags, 256), store_a);
-      } else {
-        mma_loop<BN, S>(bar, bar.full, smem, tmem, idesc, false, !B_KMAJOR, total, [&](int) { return nkb; },
-                        CVMM_DBG(flags, 256));
+        }
       }
+      ptx::bulk_wait_read<0>();
+      if (q0 >= 0) ptx::mbar_arrive(&bar.empty[q0]);
+      if (q1 >= 0) ptx::mbar_arrive(&bar.empty[q1]);
+      ptx::bulk_wait_all();
     }
-    __syncwarp();
-  } else if (B_TMA && lane == 0) {
+  } else if (warp == kLoaderWarp && B_TMA && lane == 0) {
     // ------------------------------------------------------------ B tiles by TMA
     ptx::tma_prefetch_desc(&tmap_b);
     if (EPI2) ptx::tma_prefetch_desc(&tmap_a);
@@ -1083,7 +1087,7 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
                       CVMM_DBG(flags, 256));
     }
     __syncwarp();
-  } else {
+  } else if (warp == kLoaderWarp) {
     // ------------------------------------------------------------ index warp
     // (idle when both operands are dense: their rows follow from the unit)
     uint32_t it = 0;
