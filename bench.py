@@ -47,6 +47,9 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--eager", action="store_true", help="time eager steps instead of CUDA-graph replays")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--ep", action="store_true",
+                   help="expert-sharded mode: each rank owns E/N experts, routes travel by all-to-all "
+                        "(eager steps; e.g. --workload stress_up_4096_h512)")
     p.add_argument("--also", default="ff_down_1024_weighted",
                    help="comma-separated extra workloads reported under 'also' (N=1 only)")
     return p.parse_args()
@@ -260,6 +263,73 @@ def time_e2e(run, d, steps, flush):
     b_ev.record()
     torch.cuda.synchronize()
     return a.elapsed_time(b_ev) / steps, h2d, 4
+
+
+def run_ep(args, rank, world, local_rank):
+    """Expert-sharded step: rank r owns experts [r E/N, (r+1) E/N) and its own
+    T tokens; the routes go to their experts' owners and back by all-to-all
+    (cvmm_codex_b200.expert_parallel). The route counts pass through the host,
+    so the steps run eagerly (no CUDA graph)."""
+    import torch.distributed as dist
+
+    from cvmm_codex_b200.expert_parallel import ep_cvmm, expert_range
+    from cvmm_codex_b200.workloads import WORKLOADS, make_inputs
+
+    torch.cuda.set_device(local_rank)
+    w = WORKLOADS[args.workload]
+    if w.route_input:
+        raise SystemExit("--ep takes token-shaped workloads (route rows are formed by the dispatch)")
+    d = make_inputs(w, "cuda", seed=rank)
+    keys_full = make_inputs(w, "cuda", seed=0)["keys"]  # the same weights on every rank
+    lo, hi = expert_range(w.E, rank, world)
+    kl = keys_full[lo:hi].clone().requires_grad_(True)
+    x = d["x"].requires_grad_(True)
+    wt = d["weights"]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def step():
+        x.grad = None
+        kl.grad = None
+        with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+            out = ep_cvmm(x, d["sel"], kl, w.E, weights=wt)
+        out.backward(d["grad_out"])
+        return out
+
+    with ClockSampler(local_rank) as clk:
+        clk.wait_first(5.0)
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        clk.mark()
+        total = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            step()
+            b.record()
+            torch.cuda.synchronize()
+            total += a.elapsed_time(b)
+    t = torch.tensor([total], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item() / args.steps
+    flops = w.flops() * world
+    return {
+        "metric": METRIC, "value": round(flops / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; shapes of the BASELINE config, inputs generated on device)",
+        "config": {"workload": w.name, "tokens_per_gpu": w.T, "d_in": w.d_in, "d_out": w.d_out, "experts": w.E,
+                   "experts_per_gpu": hi - lo, "top_k": w.k, "weighted": w.weighted,
+                   "parallelism": f"expert-sharded ep{world} (all-to-all dispatch)", "cuda_graph": False,
+                   "l2": "flushed (256 MiB write) before every timed step"},
+        "clocks": clk.summary(),
+        "gpu_launches": None,
+    }
 
 
 def run_ours(args, rank, world, local_rank):
@@ -532,7 +602,7 @@ def main():
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                     device_id=torch.device("cuda", local_rank))
         with contextlib.redirect_stdout(sys.stderr):
-            line = run_ours(args, rank, world, local_rank)
+            line = (run_ep if args.ep else run_ours)(args, rank, world, local_rank)
     finally:
         sys.stdout.flush()
         os.dup2(saved_fd, 1)
