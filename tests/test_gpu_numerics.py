@@ -172,3 +172,20 @@ def test_sorted_operands_match_gathered_path_bitwise(route_input, weighted, d_in
             assert b is None
             continue
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("n_experts,weighted", [(1024, False), (1100, False), (1024, True)])
+def test_many_experts_tile_table_paths(n_experts, weighted):
+    """Up to 1024 experts the tensor-core row GEMM derives its tile table from
+    the offsets in the kernel; above that it reads the table build_tiles makes.
+    Both, with most experts empty or holding a single route, against the oracle."""
+    g = torch.Generator().manual_seed(17)
+    T, k, d_in, d_out = 1500, 2, 64, 64
+    x = torch.randn(T, d_in, generator=g)
+    keys = torch.randn(n_experts, d_in, d_out, generator=g) / 8
+    sel = torch.randint(0, n_experts, (T, k), generator=g)
+    sel[:300, 0] = 7  # one expert with several 128-route tiles
+    w = torch.rand(T, k, generator=g) if weighted else None
+    grad = torch.randn(*((T, d_out) if weighted else (T, k, d_out)), generator=g)
+    out, gx, gk, gw = run_case(x.bfloat16(), keys, sel, w, grad, False, torch.bfloat16)
+    check_oracle(out, gx, gk, gw, x.bfloat16(), keys, sel, w, grad, "bfloat16")
