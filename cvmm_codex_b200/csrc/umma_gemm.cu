@@ -728,7 +728,8 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
             break;
           }
           ptx::fence_proxy_async_smem();
-          if (store) ptx::tma_store_2d(&tmap_a, ptx::smem_u32(smem + s * L::stage_bytes), kb * BK, prow);
+          if (store && !CVMM_DBG(flags, 1 << 18))
+            ptx::tma_store_2d(&tmap_a, ptx::smem_u32(smem + s * L::stage_bytes), kb * BK, prow);
           ptx::bulk_commit();
           if (q1 >= 0) {
             ptx::bulk_wait_read<2>();
