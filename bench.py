@@ -144,7 +144,7 @@ def build_step(w, d, world):
     keys = d["keys"].requires_grad_(True)
     wt = None if d["weights"] is None else d["weights"].requires_grad_(True)
 
-    def step(sel, grad_out):
+    def compute(sel, grad_out):
         x.grad = None
         keys.grad = None
         if wt is not None:
@@ -156,36 +156,49 @@ def build_step(w, d, world):
         else:
             out = cvmm(x, sel2, keys)
         out.backward(grad_out)
-        if world > 1:
-            allreduce_expert_grads(keys)  # the token-sharding exchange (NCCL)
         return out
 
+    def exchange():
+        if world > 1:
+            allreduce_expert_grads(keys)  # the token-sharding exchange (NCCL)
+
+    def step(sel, grad_out):
+        out = compute(sel, grad_out)
+        exchange()
+        return out
+
+    step.compute = compute
+    step.exchange = exchange
     return step
 
 
 class GraphedStep:
-    """The step captured once as a CUDA graph and replayed: every kernel of the
-    step (selector prep, GEMMs, copies, reductions, the NCCL all-reduce when
-    N > 1) runs on each replay; only the host's per-launch work is gone. Inputs
-    are the captured tensors d["sel"], d["grad_out"], x, keys, weights, which
-    the e2e loop overwrites in place before each replay."""
+    """The step's computation captured once as a CUDA graph and replayed: every
+    kernel of it (selector prep, GEMMs, copies, reductions) runs on each
+    replay; only the host's per-launch work is gone. With N > 1 the NCCL
+    all-reduce of grad-W follows each replay as an ordinary (eager) collective
+    on the same stream; collectives are kept out of the graph. Inputs are the
+    captured tensors d["sel"], d["grad_out"], x, keys, weights, which the e2e
+    loop overwrites in place before each replay."""
 
     def __init__(self, step, d):
         self.d = d
+        self.exchange = step.exchange
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
             for _ in range(3):
-                step(d["sel"], d["grad_out"])
+                step.compute(d["sel"], d["grad_out"])
         torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            self.out = step(d["sel"], d["grad_out"])
+            self.out = step.compute(d["sel"], d["grad_out"])
         torch.cuda.synchronize()
 
     def __call__(self, sel=None, grad_out=None):
         self.graph.replay()
+        self.exchange()
         return self.out
 
 
@@ -599,7 +612,7 @@ def main():
 
             import torch.distributed as dist
             torch.cuda.set_device(local_rank)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                     device_id=torch.device("cuda", local_rank))
         with contextlib.redirect_stdout(sys.stderr):
             line = (run_ep if args.ep else run_ours)(args, rank, world, local_rank)
