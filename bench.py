@@ -74,17 +74,23 @@ class ClockSampler:
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, active: bool = True, interval_ms: int = 20):
+        # With several ranks on one box only one sampler runs (local rank 0):
+        # one nvidia-smi poller per GPU would compete for the driver.
         self.index = index
+        self.active = active
+        self.interval_ms = interval_ms
         self.proc = None
         self.lines = []
         self.thread = None
 
     def __enter__(self):
+        if not self.active:
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", str(self.interval_ms)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except Exception:
@@ -308,7 +314,7 @@ def run_ep(args, rank, world, local_rank):
         out.backward(d["grad_out"])
         return out
 
-    with ClockSampler(local_rank) as clk:
+    with ClockSampler(local_rank, active=local_rank == 0, interval_ms=20 if world == 1 else 50) as clk:
         clk.wait_first(5.0)
         for _ in range(max(args.warmup, 3)):
             step()
@@ -372,7 +378,7 @@ def run_ours(args, rank, world, local_rank):
             except Exception as exc:  # capture unsupported here: time the eager step
                 print(f"CUDA graph capture failed ({exc!r}); timing eager steps", file=sys.stderr)
                 torch.cuda.synchronize()
-        with ClockSampler(local_rank) as clk:
+        with ClockSampler(local_rank, active=local_rank == 0, interval_ms=20 if world == 1 else 50) as clk:
             clk.wait_first(5.0)  # nvidia-smi takes a moment to print its first line
             for _ in range(max(args.warmup, 3)):
                 run(d["sel"], d["grad_out"])
@@ -383,9 +389,19 @@ def run_ours(args, rank, world, local_rank):
             clk.mark()
             total_ms = time_steps(run, d, args.steps, flush)
             # A short timed region may end between two samples: keep the same
-            # replays running (untimed) until the sampler has seen the load.
+            # replays running (untimed) until the sampler (rank 0's) has seen
+            # the load. With N > 1 every replay ends in an all-reduce, so rank 0
+            # decides each round and broadcasts it: all ranks run the same
+            # sequence of collectives.
             t_end = time.perf_counter() + 1.0
-            while clk.since_mark() < 10 and time.perf_counter() < t_end:
+            while True:
+                more = clk.since_mark() < 10 and time.perf_counter() < t_end
+                if world > 1:
+                    flag = torch.tensor([1 if more else 0], device="cuda")
+                    dist.broadcast(flag, src=0)
+                    more = bool(flag.item())
+                if not more:
+                    break
                 for _ in range(20):
                     run(d["sel"], d["grad_out"])
                 torch.cuda.synchronize()
