@@ -10,9 +10,10 @@
 // range actually present (max - min). For every realistic expert count
 // (< 2048 experts) that is ONE pass of histogram -> scan -> scatter. Each warp
 // owns a chunk of consecutive routes (128 or more, at most 2048 chunks, so
-// that even 64k routes spread over ~128 CTAs); the scatter ranks equal digits
-// inside a warp with __match_any_sync, which keeps the sort stable without any
-// cross-warp ordering inside a CTA. Extra passes (keys spread over > 2048
+// that even 64k routes spread over ~128 CTAs). Digit counts are kept per CTA
+// (4 warp chunks), which keeps the single-CTA scan short; the scatter orders
+// the warps of its CTA by their own histograms and ranks equal digits inside
+// a warp with __match_any_sync, so the sort is stable. Extra passes (keys spread over > 2048
 // values) are launched unconditionally but exit on the device when the key
 // range does not need them, so the host never synchronises.
 #include "common.cuh"
