@@ -30,7 +30,7 @@ from typing import Optional, Union
 
 import torch
 
-from . import ops
+from ._torch_ops import calls as ops  # every device call: a registered torch custom op under torch.compile
 
 
 @dataclass
@@ -116,6 +116,14 @@ cvmm_gather_x_grad_w_max_top_k = int(os.environ.get("CVMM_GATHER_X_GRAD_W_MAX_TO
 # Costs one extra [n_routes + 128 * n_experts, d_in] op-dtype copy of x kept
 # for the backward.
 cvmm_sorted_operands = os.environ.get("CVMM_B200_SORTED_OPERANDS", "1").lower() not in ("0", "false", "no", "off")
+# sm_100a engine knob: the weighted grad-W reads a weight-scaled, expert-padded
+# sorted copy of the token grads (True) instead of gathering and scaling the
+# token grad rows inside the GEMM (False). Both give bit-identical results.
+cvmm_weighted_grad_copy = os.environ.get("CVMM_B200_WEIGHTED_GRAD_COPY", "0").lower() in ("1", "true", "yes", "on")
+# Opt-in host check of the device status word after every CVMM forward and
+# backward (synchronises the stream): raises RuntimeError when a kernel gave up
+# on a bounded wait or met an out-of-range expert id.
+cvmm_check_device_status = os.environ.get("CVMM_B200_CHECK_STATUS", "0").lower() in ("1", "true", "yes", "on")
 
 
 def create_kernels():
@@ -171,6 +179,16 @@ def _sortable(t: torch.Tensor, op_dtype: torch.dtype) -> bool:
             and t.shape[-1] % 8 == 0)
 
 
+def _raise_on_device_status(where: str) -> None:
+    """Reads and clears the library's device status word (synchronises) and
+    raises if a kernel recorded a timeout or an out-of-range expert id."""
+    from . import _lib
+    code, site, aux = _lib.device_status(reset=True)
+    if code != 0:
+        what = {1: "a bounded wait ran out", 2: "an expert id outside [0, n_experts)"}.get(code, "error")
+        raise RuntimeError(f"{where}: device status {code} ({what}; site {site}, value {aux})")
+
+
 class CVMM(torch.autograd.Function):
     """Autograd function with the reference's signature (cvmm.py:1521-1755)."""
 
@@ -196,9 +214,7 @@ class CVMM(torch.autograd.Function):
             # copy for the grad-W as it goes, instead of a separate copy pass.
             # Its pad starts depend only on the offsets; the backward takes them
             # from the grad copy it makes anyway.
-            xs = torch.empty((sel_index.numel() + n_experts * ops.PAD_ROWS, x.shape[-1]), dtype=op_dtype,
-                             device=x.device)
-            res = ops.forward(x, sel_index, offsets, keys_op, out_index, op_dtype, op_dtype, x_copy=xs)
+            res, xs = ops.forward(x, sel_index, offsets, keys_op, out_index, op_dtype, op_dtype, x_copy=True)
             res = res.view(*sel.shape, res.shape[-1])
         elif reduction_weight is not None:
             rows = out_pad = None
@@ -218,6 +234,8 @@ class CVMM(torch.autograd.Function):
         ctx.op_type = op_dtype
         ctx.keys_type = keys.dtype
         ctx.dtype = op_dtype
+        if cvmm_check_device_status:
+            _raise_on_device_status("CVMM.forward")
         return res
 
     @staticmethod
@@ -277,12 +295,18 @@ class CVMM(torch.autograd.Function):
             gt = g.reshape(-1, g.shape[-1])  # token grads of the combined output
             if need_keys:
                 # dW_e = sum_p x[sel_index[p]]^T (bf16(w_p) * g[route_p // k])  (cvmm.py:1341-1383)
-                if xs is not None and _sortable(gt, op):
-                    # The weight product is applied (and rounded) in the sorted copy.
+                if xs is not None and _sortable(gt, op) and cvmm_weighted_grad_copy:
+                    # The weight product is applied (and rounded) in a sorted copy.
                     gs, gpad = ops.sort_rows_padded(gt, route, k, sel, offsets, n_experts, dtype=op, scale=w)
                     grad_keys = ops.backward_w(xs, None, 1, gs, None, 1, offsets, n_experts, op,
                                                g_pad_start=gpad, x_pad_start=xpad, n_routes=n_routes)
                     del gs
+                elif xs is not None:
+                    # Token grad rows gathered straight from g (L2-resident) and
+                    # scaled by op(w) in shared memory (cvmm.py:591-599): no
+                    # R x d_out weighted copy is written.
+                    grad_keys = ops.backward_w(xs, None, 1, gt, route, k, offsets, n_experts, op,
+                                               w=w, w_index=route, x_pad_start=xpad, n_routes=n_routes)
                 else:
                     grad_keys = ops.backward_w(x, sel_index, 1, gt, route, k, offsets, n_experts, op,
                                                w=w, w_index=route)
@@ -302,6 +326,8 @@ class CVMM(torch.autograd.Function):
         if grad_keys is not None and ctx.keys_type != torch.float32:
             grad_keys = grad_keys.to(ctx.keys_type)
         del top_k
+        if cvmm_check_device_status:
+            _raise_on_device_status("CVMM.backward")
         return grad_x, None, None, None, grad_keys, None, grad_w
 
 
@@ -310,11 +336,14 @@ known_shapes = set()
 
 def cvmm(x: torch.Tensor, sel: Union[torch.Tensor, CVMMSel], keys: torch.Tensor):
     """x @ keys[sel] per route (reference cvmm.py:1759-1783)."""
-    create_kernels()
+    if not torch.compiler.is_compiling():
+        # Module state and the stdout line of the reference (eager only: a
+        # traced print would break the compiled graph).
+        create_kernels()
+        sh = (x.shape, keys.shape)
+        if sh not in known_shapes:
+            print("New shape:", sh)
+            known_shapes.add(sh)
     if not isinstance(sel, CVMMSel):
         sel = cvmm_prepare_sel(sel, keys.shape[0])
-    sh = (x.shape, keys.shape)
-    if sh not in known_shapes:
-        print("New shape:", sh)
-        known_shapes.add(sh)
     return CVMM.apply(x, sel.raw_sel, sel.sel_index, sel.sel, keys, sel.out_index, sel.reduction_weight)

@@ -92,6 +92,67 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* __restrict__ s
   }
 }
 
+// 16-bit rows, 16-byte accesses: one thread per CPT chunks of 8 columns of
+// one token (chunks sub, sub + tpt, ... so consecutive lanes read consecutive
+// 16 bytes), with the route rows of up to kVecRoutes routes times CPT chunks
+// (16 x 16 bytes) in flight per thread. At ff_*_1024 shapes that is 32 threads
+// per 1024-column token row, 4x fewer threads than one chunk per thread,
+// which bounded the old kernel by latency (about 50 waves of two dependent
+// loads). Same arithmetic and route order as combine_kernel, so the results
+// are bit-identical.
+constexpr int kVecRoutes = 4;
+
+template <int CPT>
+__global__ void __launch_bounds__(256) combine_vec_kernel(const uint4* __restrict__ src, int s_dtype,
+                                                          const void* __restrict__ w, int w_dtype,
+                                                          const int32_t* __restrict__ rows, uint4* __restrict__ out,
+                                                          int o_dtype, int64_t T, int64_t k, int64_t groups) {
+  const int64_t tpt = groups / CPT;  // threads per token
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= T * tpt) return;
+  const int64_t t = i / tpt, sub = i - t * tpt;
+  float acc[CPT][8];
+#pragma unroll
+  for (int c = 0; c < CPT; ++c)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[c][e] = 0.f;
+  for (int64_t j0 = 0; j0 < k; j0 += kVecRoutes) {
+    uint4 q[kVecRoutes][CPT];
+    float wj[kVecRoutes];
+#pragma unroll
+    for (int u = 0; u < kVecRoutes; ++u) {
+      const int64_t j = j0 + u;
+      if (j < k) {
+        const int64_t r = t * k + j;
+        const int64_t row = rows ? rows[r] : r;
+        wj[u] = w ? round_to(load_as_float(w, w_dtype, r), s_dtype) : 1.f;
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) q[u][c] = src[row * groups + sub + c * tpt];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kVecRoutes; ++u) {
+      if (j0 + u >= k) break;
+#pragma unroll
+      for (int c = 0; c < CPT; ++c) {
+        const uint32_t wd[4] = {q[u][c].x, q[u][c].y, q[u][c].z, q[u][c].w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          acc[c][2 * h] = fmaf(wj[u], bits_to_float((uint16_t)(wd[h] & 0xffffu), s_dtype), acc[c][2 * h]);
+          acc[c][2 * h + 1] = fmaf(wj[u], bits_to_float((uint16_t)(wd[h] >> 16), s_dtype), acc[c][2 * h + 1]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < CPT; ++c) {
+    uint32_t wd[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) wd[h] = pack2(acc[c][2 * h], acc[c][2 * h + 1], o_dtype);
+    out[t * groups + sub + c * tpt] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  }
+}
+
 // Self-test of the bounded-wait path every persistent kernel relies on: one
 // thread waits on an mbarrier that nothing ever arrives on, through the same
 // bounded wait as the GEMM roles, so the wait runs out after `limit_ns`, the
@@ -361,10 +422,20 @@ int cvmm_weighted_combine(const void* y, int y_dtype, const void* w, int w_dtype
   if (n_tokens == 0) return CVMM_OK;
   if (!y || !out) return fail(CVMM_ERR_INVALID_ARG, "cvmm_weighted_combine: null pointer");
   const bool vec = n_dim % 8 == 0 && y_dtype != F32 && out_dtype != F32 && al16(y) && al16(out);
-  const int64_t work = n_tokens * ((n_dim + 7) / 8);
+  const int64_t groups = (n_dim + 7) / 8;
+  const int64_t work = n_tokens * groups;
   const unsigned grid = (unsigned)((work + 255) / 256);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (vec)
+  const int cpt = groups % 4 == 0 ? 4 : (groups % 2 == 0 ? 2 : 1);
+  if (vec && cpt > 1) {
+    const unsigned g2 = (unsigned)((n_tokens * (groups / cpt) + 255) / 256);
+    const uint4* ys = static_cast<const uint4*>(y);
+    uint4* os = static_cast<uint4*>(out);
+    if (cpt == 4)
+      combine_vec_kernel<4><<<g2, 256, 0, s>>>(ys, y_dtype, w, w_dtype, y_rows, os, out_dtype, n_tokens, top_k, groups);
+    else
+      combine_vec_kernel<2><<<g2, 256, 0, s>>>(ys, y_dtype, w, w_dtype, y_rows, os, out_dtype, n_tokens, top_k, groups);
+  } else if (vec)
     combine_kernel<true><<<grid, 256, 0, s>>>(y, y_dtype, w, w_dtype, y_rows, out, out_dtype, n_tokens, top_k, n_dim);
   else
     combine_kernel<false><<<grid, 256, 0, s>>>(y, y_dtype, w, w_dtype, y_rows, out, out_dtype, n_tokens, top_k, n_dim);

@@ -263,6 +263,10 @@ __global__ void offsets_kernel(const int32_t* __restrict__ sorted, int64_t n, in
   }
   if (i >= n) return;
   const int64_t a = sorted[i];
+  // An expert id outside [0, n_experts) would index past the weights: record
+  // it (site 1 = sorted position) in the status word; the GEMMs never read
+  // such routes (they only visit the routes inside [0, offsets[E-1])).
+  if (a < 0 || a >= n_experts) report(CVMM_DEV_BAD_INDEX, 1, (long long)a);
   if (i == 0)
     for (int64_t e = 0; e < min(a, n_experts); ++e) offsets[e] = 0;
   const int64_t b = i + 1 < n ? (int64_t)sorted[i + 1] : n_experts;

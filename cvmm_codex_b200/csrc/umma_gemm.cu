@@ -21,8 +21,10 @@
 // overlaps the main loop of tile i+1.
 //
 // Row gathering is the heart of CVMM: the A rows of a forward tile are
-// x[sel_index[p]] for 128 consecutive sorted routes p of one expert, so no
-// gathered copy of x is ever materialised in HBM. Tiles never straddle two
+// x[sel_index[p]] for 128 consecutive sorted routes p of one expert, read
+// straight from x. When the caller asks for it (kFlagACopy), warp 10 also
+// stores those gathered tiles as the expert-padded sorted copy of x that the
+// grad-W kernel reads as dense TMA boxes. Tiles never straddle two
 // experts (the tile scheduler cuts every expert segment into its own tiles),
 // unlike the reference kernel which re-runs the K loop per expert present in
 // a tile (cvmm.py:167,236-238).
@@ -1275,7 +1277,11 @@ static int seg_launch(const SegGemm& p, int64_t max_units, int flags, cudaStream
   // as dense 64-row boxes.
   const bool g_dense = p.g_pad_start != nullptr, x_dense = p.x_pad_start != nullptr;
   const int64_t padded_rows = p.n_routes + kPadRows * p.n_experts;
-  const bool gt = (flags & 3) == 3 && !(dbg_flags() & 4096) &&
+  // TMA needs both operands in the expert-padded layout (dense boxes): a
+  // gathered grad operand goes through the cp.async producers, whose row
+  // gathers measured about twice the throughput of tile::gather4 here
+  // (4.1 vs 2.1 TB/s for 256-byte row pieces out of L2).
+  const bool gt = (flags & 3) == 3 && g_dense && !(dbg_flags() & 4096) &&
                   make_rows_map(&xmap, p.x, p.op_dtype, p.M, x_dense ? padded_rows : p.n_routes, p.x_ld,
                                 x_dense ? 64 : 1) &&
                   make_rows_map(&gmap, p.g, p.op_dtype, p.N, g_dense ? padded_rows : p.n_routes, p.g_ld,

@@ -1,9 +1,9 @@
 """Generates the golden fixtures in this folder from the reference itself.
 
-Run in a checkout that has the reference (RobertCsordas/cvmm_codex) at
-$CVMM_REFERENCE (default /root/reference):
+Run with the path of a checkout of the reference (RobertCsordas/cvmm_codex)
+as the argument (or in $CVMM_REFERENCE):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <path-to-reference-checkout>
 
 It imports the reference module `cvmm.py` and its test oracle `_reference`
 (test_cvmm_correctness.py:7-15) on CPU -- nothing here needs a GPU -- and
@@ -24,7 +24,7 @@ import sys
 import torch
 
 sys.dont_write_bytecode = True
-REF = os.environ.get("CVMM_REFERENCE", "/root/reference")
+REF = os.environ.get("CVMM_REFERENCE")  # checkout of the reference repository (required)
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
@@ -125,6 +125,10 @@ def make_numerics(ref_test):
 
 
 if __name__ == "__main__":
+    if len(sys.argv) > 1:
+        REF = sys.argv[1]
+    if not REF:
+        sys.exit("usage: make_golden.py <path-to-reference-checkout> (or set CVMM_REFERENCE)")
     ref_cvmm, ref_test = _import_reference()
     torch.save(make_selector(ref_cvmm), os.path.join(HERE, "selector.pt"))
     torch.save(make_numerics(ref_test), os.path.join(HERE, "numerics.pt"))

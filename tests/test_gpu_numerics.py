@@ -136,6 +136,14 @@ def test_top1_and_raw_selector():
     assert out.shape == (T, n)
     e = O.forward(_np(x), sel.cpu().numpy()[:, None], _np(keys), op="bfloat16").reshape(T, n)
     assert O.rel_max_err(_np(out), e) < 2e-2
+    # Backward of the route-indexed selector path: grads of x and keys.
+    grad = torch.randn(T, n, generator=g)
+    out.backward(grad.cuda().to(out.dtype))
+    gn = grad.to(out.dtype).float().double().numpy()[:, None, :]
+    ex, ek, _ = O.backward(_np(x), sel.cpu().numpy()[:, None], _np(keys), gn, op="bfloat16")
+    for a, e in ((x.grad, ex.reshape(T, d)), (keys.grad, ek)):
+        assert O.rel_max_err(_np(a), e) < 2e-2
+        assert O.rel_rms_err(_np(a), e) < 1e-2
 
 
 def test_device_status_clean():
@@ -172,6 +180,34 @@ def test_sorted_operands_match_gathered_path_bitwise(route_input, weighted, d_in
             assert b is None
             continue
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("route_input", [True, False])
+def test_weighted_grad_gather_matches_scaled_copy_bitwise(route_input):
+    """The weighted grad-W either reads a weight-scaled sorted copy of the token
+    grads or gathers and scales the token grad rows in shared memory; both
+    apply op(op(g) * op(w)) (cvmm.py:591-599) to the same operands in the same
+    order, so grad_keys is bit-identical."""
+    import cvmm_codex_b200.api as A
+    g = torch.Generator().manual_seed(8)
+    T, k, E, d_in, d_out = 900, 4, 7, 64, 320
+    sel = torch.randint(0, E, (T, k), generator=g)
+    sel[: T // 2, 1] = 3  # one expert split into several chunks
+    x = torch.randn(*((T, k, d_in) if route_input else (T, d_in)), generator=g).bfloat16()
+    keys = torch.randn(E, d_in, d_out, generator=g) / d_in ** 0.5
+    w = torch.rand(T, k, generator=g)
+    grad = torch.randn(T, d_out, generator=g)
+    res = {}
+    old = A.cvmm_weighted_grad_copy
+    try:
+        for mode in (True, False):
+            A.cvmm_weighted_grad_copy = mode
+            res[mode] = run_case(x, keys, sel, w, grad, route_input, torch.bfloat16)
+    finally:
+        A.cvmm_weighted_grad_copy = old
+    for a, b in zip(res[True], res[False]):
+        assert torch.equal(a, b)
+    check_oracle(*res[False], x, keys, sel, w, grad, "bfloat16")
 
 
 @pytest.mark.parametrize("n_experts,weighted", [(1024, False), (1100, False), (1024, True)])

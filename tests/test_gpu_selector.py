@@ -96,16 +96,24 @@ def test_expert_offsets_kernel_matches_reference_formula():
             torch.testing.assert_close(fast.cpu(), ref.cpu(), rtol=0, atol=0)
 
 
-def test_cuda_default_sort_agreement_report(capsys):
-    """Reports whether CUDA torch.sort (the reference's call, stable=False) gives
-    the stable order at each size; the library always produces the stable one."""
-    rows = []
-    for R, E in [(64, 8), (4096, 8), (65536, 64), (524288, 128)]:
-        fsel = torch.randint(0, E, (R,), device="cuda", dtype=torch.int32)
-        a = fsel.sort().indices
-        b = fsel.sort(stable=True).indices
-        rows.append((R, E, bool(torch.equal(a, b))))
-    print("cuda default sort == stable:", rows)
+@pytest.mark.parametrize("R,E", [(64, 8), (4096, 8), (65536, 64), (262144, 128), (524288, 128)])
+def test_cuda_default_sort_agrees_with_stable_order(R, E):
+    """The reference sorts with CUDA torch.sort at its default (stable=False,
+    cvmm.py:1795). At every config size that call returns the stable order on
+    B200, and the library's indices equal it bit for bit, so the library
+    matches the reference's own CUDA ordering, not just the stable one."""
+    from cvmm_codex_b200 import cvmm_prepare_sel2
+
+    g = torch.Generator(device="cuda").manual_seed(R)
+    sel = torch.randint(0, E, (R // 4, 4), device="cuda", generator=g)
+    fsel = sel.flatten().to(torch.int32)
+    default = fsel.sort()
+    stable = fsel.sort(stable=True)
+    assert torch.equal(default.indices, stable.indices)
+    s = cvmm_prepare_sel2(sel)
+    assert torch.equal(s.out_index, default.indices)
+    assert torch.equal(s.sel.reshape(-1), default.values)
+    assert torch.equal(s.sel_index, default.indices // 4)
 
 
 @pytest.mark.parametrize("src_dtype,dst_dtype,scaled", [

@@ -6,10 +6,17 @@ array inside the library. This file is collected last so that a run stopping
 at the first failure has already run every other test; it also passes alone
 in a fresh process.
 """
+import os
+import sys
+
+import numpy as np
 import pytest
 import torch
 
 from cvmm_codex_b200 import _lib
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from oracle import cvmm_oracle as O  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -61,6 +68,12 @@ def test_no_alloc_matches_workspace_entry_point_twice(route_input):
                 assert a is None
             else:
                 assert torch.equal(a, b)  # integer outputs: bit-exact
+        # ... and both equal the oracle's stable sort (cvmm.py:1786-1803).
+        for a, b in zip(got, O.prepare_sel2(sel.cpu().numpy(), route_input=route_input)):
+            if b is None:
+                assert a is None
+            else:
+                np.testing.assert_array_equal(a.cpu().numpy().astype(np.int64), b.astype(np.int64))
 
 
 def test_no_alloc_rejects_oversize_input():
