@@ -119,7 +119,7 @@ cvmm_sorted_operands = os.environ.get("CVMM_B200_SORTED_OPERANDS", "1").lower() 
 # sm_100a engine knob: the weighted grad-W reads a weight-scaled, expert-padded
 # sorted copy of the token grads (True) instead of gathering and scaling the
 # token grad rows inside the GEMM (False). Both give bit-identical results.
-cvmm_weighted_grad_copy = os.environ.get("CVMM_B200_WEIGHTED_GRAD_COPY", "0").lower() in ("1", "true", "yes", "on")
+cvmm_weighted_grad_copy = os.environ.get("CVMM_B200_WEIGHTED_GRAD_COPY", "1").lower() not in ("0", "false", "no", "off")
 # Opt-in host check of the device status word after every CVMM forward and
 # backward (synchronises the stream): raises RuntimeError when a kernel gave up
 # on a bounded wait or met an out-of-range expert id.

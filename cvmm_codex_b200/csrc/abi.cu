@@ -95,15 +95,14 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* __restrict__ s
 // 16-bit rows, 16-byte accesses: one thread per CPT chunks of 8 columns of
 // one token (chunks sub, sub + tpt, ... so consecutive lanes read consecutive
 // 16 bytes), with the route rows of up to kVecRoutes routes times CPT chunks
-// (16 x 16 bytes) in flight per thread. At ff_*_1024 shapes that is 32 threads
-// per 1024-column token row, 4x fewer threads than one chunk per thread,
-// which bounded the old kernel by latency (about 50 waves of two dependent
-// loads). Same arithmetic and route order as combine_kernel, so the results
-// are bit-identical.
+// (8 x 16 bytes) in flight per thread, and at most 85 registers per thread so
+// that 3 CTAs (24 warps) share an SM: a CTA-per-SM occupancy of 1 (CPT = 4,
+// 141 registers) measured 2.1 TB/s, latency-bound. Same arithmetic and route
+// order as combine_kernel, so the results are bit-identical.
 constexpr int kVecRoutes = 4;
 
 template <int CPT>
-__global__ void __launch_bounds__(256) combine_vec_kernel(const uint4* __restrict__ src, int s_dtype,
+__global__ void __launch_bounds__(256, 3) combine_vec_kernel(const uint4* __restrict__ src, int s_dtype,
                                                           const void* __restrict__ w, int w_dtype,
                                                           const int32_t* __restrict__ rows, uint4* __restrict__ out,
                                                           int o_dtype, int64_t T, int64_t k, int64_t groups) {
@@ -269,8 +268,16 @@ static int64_t segw_chunk(int64_t n_routes, int64_t n_experts, int64_t m_dim, in
   const int64_t mt = (m_dim + (tensor ? 127 : 63)) / (tensor ? 128 : 64);
   const int64_t nt = (n_dim + (tensor ? 255 : 63)) / (tensor ? 256 : 64);
   if (n_experts * mt * nt >= 8 * 148) return std::max<int64_t>(64, (n_routes + 63) / 64 * 64);
+  // Experts longer than `chunk` routes are split into partial slots that
+  // seg_reduce adds. Units run longest first over the SMs, so a unit only has
+  // to be short next to one SM's share of the work (n_routes * mt * nt / 148
+  // route-tiles): chunks of at least half that share keep the SMs balanced
+  // while splitting only the heavy experts (at ff_up_1024, 2048 instead of
+  // 1024 routes, which split about half of the 64 experts).
   int64_t chunk = 1024;
-  while (chunk > 128 && (n_routes / chunk) * mt * nt < 2 * 148) chunk /= 2;
+  while (chunk < 8192 && chunk * 2 <= n_routes * mt * nt / 148) chunk *= 2;
+  // ... but at least one unit tile per SM (every expert is at least one unit).
+  while (chunk > 128 && std::max<int64_t>(n_experts, n_routes / chunk) * mt * nt < 148) chunk /= 2;
   while (2 * ((n_routes + chunk - 1) / chunk) * m_dim * n_dim * 4 > ((int64_t)256 << 20)) chunk *= 2;
   return chunk;
 }
@@ -426,15 +433,10 @@ int cvmm_weighted_combine(const void* y, int y_dtype, const void* w, int w_dtype
   const int64_t work = n_tokens * groups;
   const unsigned grid = (unsigned)((work + 255) / 256);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int cpt = groups % 4 == 0 ? 4 : (groups % 2 == 0 ? 2 : 1);
-  if (vec && cpt > 1) {
-    const unsigned g2 = (unsigned)((n_tokens * (groups / cpt) + 255) / 256);
-    const uint4* ys = static_cast<const uint4*>(y);
-    uint4* os = static_cast<uint4*>(out);
-    if (cpt == 4)
-      combine_vec_kernel<4><<<g2, 256, 0, s>>>(ys, y_dtype, w, w_dtype, y_rows, os, out_dtype, n_tokens, top_k, groups);
-    else
-      combine_vec_kernel<2><<<g2, 256, 0, s>>>(ys, y_dtype, w, w_dtype, y_rows, os, out_dtype, n_tokens, top_k, groups);
+  if (vec && groups % 2 == 0) {
+    const unsigned g2 = (unsigned)((n_tokens * (groups / 2) + 255) / 256);
+    combine_vec_kernel<2><<<g2, 256, 0, s>>>(static_cast<const uint4*>(y), y_dtype, w, w_dtype, y_rows,
+                                             static_cast<uint4*>(out), out_dtype, n_tokens, top_k, groups);
   } else if (vec)
     combine_kernel<true><<<grid, 256, 0, s>>>(y, y_dtype, w, w_dtype, y_rows, out, out_dtype, n_tokens, top_k, n_dim);
   else

@@ -33,9 +33,26 @@ inline size_t dtype_size(int d) {
 }
 
 // Entry points implemented across the .cu files.
-// min_chunk: fewest routes per radix-sort warp chunk (128 by default; the
-// allocation-free entry uses 1024 to keep its static scratch small).
-constexpr int64_t kSelMinChunk = 128;
+// Selector sort: one persistent CTA of kSelWarps warps per slice of routes, at
+// most kSelMaxGrid CTAs (and never more than the SMs). min_chunk: fewest
+// routes per CTA (rounded up to kSelWarps * 32; the allocation-free entry uses
+// 1024 so its static scratch holds the counts of at most 64 CTAs).
+constexpr int64_t kSelMinChunk = 512;
+constexpr int kSelWarps = 16;
+constexpr int64_t kSelMaxGrid = 256;
+constexpr int64_t sel_round(int64_t v) { return (v + kSelWarps * 32 - 1) / (kSelWarps * 32) * (kSelWarps * 32); }
+constexpr int64_t sel_cta_len_min(int64_t min_chunk) { return sel_round(min_chunk < 1 ? 1 : min_chunk); }
+constexpr int64_t sel_grid_bound(int64_t n, int64_t min_chunk) {
+  return (n + sel_cta_len_min(min_chunk) - 1) / sel_cta_len_min(min_chunk) < kSelMaxGrid
+             ? (n + sel_cta_len_min(min_chunk) - 1) / sel_cta_len_min(min_chunk)
+             : kSelMaxGrid;
+}
+constexpr size_t sel_align(size_t v) { return (v + 255) / 256 * 256; }
+// Header, per-(bin, CTA) counts, bin totals, and the ping-pong key/value buffers of the extra passes.
+constexpr size_t sel_ws_bytes(int64_t n, int64_t min_chunk) {
+  return 256 + sel_align((size_t)2048 * sel_grid_bound(n, min_chunk) * 4) + sel_align(2048 * 4) +
+         4 * sel_align((size_t)n * 4);
+}
 size_t sel_prepare_workspace_size(int64_t n, int64_t min_chunk = kSelMinChunk);
 int sel_prepare(const void* sel, int sel_dtype, int64_t n, int64_t top_k, int route_input,
                 int32_t* raw_sel, int32_t* sorted_sel, int64_t* sel_index, int64_t* out_index,

@@ -14,13 +14,12 @@
 namespace cvmm {
 
 // Sized for CVMM_NOALLOC_MAX_ROUTES routes: the radix-sort header, the
-// per-chunk histograms and the ping-pong key/value buffers. Every GPU that
-// loads the library keeps this much memory until the process exits.
+// per-(digit, CTA) counts and the ping-pong key/value buffers (about 1.6 MB).
+// Every GPU that loads the library keeps this much memory until the process
+// exits.
 constexpr int64_t kNoAllocMaxRoutes = CVMM_NOALLOC_MAX_ROUTES;
-constexpr int64_t kNoAllocChunk = 1024;  // routes per radix-sort warp chunk
-constexpr size_t kNoAllocScratchBytes =
-    256 + ((kNoAllocMaxRoutes + kNoAllocChunk - 1) / kNoAllocChunk) * 2048 * sizeof(int) +
-    4 * kNoAllocMaxRoutes * sizeof(int32_t);
+constexpr int64_t kNoAllocChunk = 1024;  // fewest routes per sorting CTA
+constexpr size_t kNoAllocScratchBytes = sel_ws_bytes(kNoAllocMaxRoutes, kNoAllocChunk);
 
 static __device__ __align__(256) unsigned char g_sel_scratch[kNoAllocScratchBytes];
 
