@@ -47,10 +47,12 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--eager", action="store_true", help="time eager steps instead of CUDA-graph replays")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--serial-allreduce", action="store_true",
+                   help="N > 1: one grad-W all-reduce after the backward instead of overlapping it with grad-x")
     p.add_argument("--ep", action="store_true",
                    help="expert-sharded mode: each rank owns E/N experts, routes travel by all-to-all "
                         "(eager steps; e.g. --workload stress_up_4096_h512)")
-    p.add_argument("--also", default="ff_down_1024_weighted",
+    p.add_argument("--also", default="ff_down_1024_weighted,ffn_1024",
                    help="comma-separated extra workloads reported under 'also' (N=1 only)")
     return p.parse_args()
 
@@ -142,31 +144,45 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ our arm
-def build_step(w, d, world):
+def build_step(w, d, world, overlap=True):
+    """One step of the public API: cvmm_prepare_sel2 -> cvmm (autocast) ->
+    backward. With N > 1 ranks the fp32 expert-weight gradient is summed over
+    the ranks by NCCL: overlapped with grad-x (dist.OverlappedGradReduce, the
+    default) or as one all-reduce after the backward (overlap=False)."""
+    from contextlib import nullcontext
+
     from cvmm_codex_b200 import cvmm, cvmm_prepare_sel2
-    from cvmm_codex_b200.dist import allreduce_expert_grads
+    from cvmm_codex_b200.dist import OverlappedGradReduce, allreduce_expert_grads
 
     x = d["x"].requires_grad_(True)
     keys = d["keys"].requires_grad_(True)
     wt = None if d["weights"] is None else d["weights"].requires_grad_(True)
+    reducer = OverlappedGradReduce() if (world > 1 and overlap) else None
 
     def compute(sel, grad_out):
         x.grad = None
         keys.grad = None
         if wt is not None:
             wt.grad = None
-        sel2 = cvmm_prepare_sel2(sel, wt, route_input=w.route_input)
-        if w.amp:
-            with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+        with (reducer if reducer is not None else nullcontext()):
+            sel2 = cvmm_prepare_sel2(sel, wt, route_input=w.route_input)
+            if w.amp:
+                with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+                    out = cvmm(x, sel2, keys)
+            else:
                 out = cvmm(x, sel2, keys)
-        else:
-            out = cvmm(x, sel2, keys)
-        out.backward(grad_out)
+            out.backward(grad_out)
         return out
 
-    def exchange():
-        if world > 1:
-            allreduce_expert_grads(keys)  # the token-sharding exchange (NCCL)
+    def exchange(graphed=False):
+        """The weight-gradient exchange still to issue after `compute` (eager)
+        or after a replay of its captured graph."""
+        if world == 1:
+            return
+        if reducer is None:
+            allreduce_expert_grads(keys)  # one NCCL all-reduce after the backward
+        elif graphed:
+            reducer.launch(keys.grad)  # side stream, behind the graph's grad-W event
 
     def step(sel, grad_out):
         out = compute(sel, grad_out)
@@ -182,10 +198,11 @@ class GraphedStep:
     """The step's computation captured once as a CUDA graph and replayed: every
     kernel of it (selector prep, GEMMs, copies, reductions) runs on each
     replay; only the host's per-launch work is gone. With N > 1 the NCCL
-    all-reduce of grad-W follows each replay as an ordinary (eager) collective
-    on the same stream; collectives are kept out of the graph. Inputs are the
-    captured tensors d["sel"], d["grad_out"], x, keys, weights, which the e2e
-    loop overwrites in place before each replay."""
+    all-reduce of grad-W is not captured: it is issued after each replay on a
+    side stream that waits on an event node the graph records right after
+    grad-W, so it overlaps the graph's grad-x kernels. Inputs are the captured
+    tensors d["sel"], d["grad_out"], x, keys, weights, which the e2e loop
+    overwrites in place before each replay."""
 
     def __init__(self, step, d):
         self.d = d
@@ -194,7 +211,7 @@ class GraphedStep:
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
             for _ in range(3):
-                step.compute(d["sel"], d["grad_out"])
+                step(d["sel"], d["grad_out"])
         torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
@@ -204,7 +221,7 @@ class GraphedStep:
 
     def __call__(self, sel=None, grad_out=None):
         self.graph.replay()
-        self.exchange()
+        self.exchange(graphed=True)
         return self.out
 
 
@@ -372,7 +389,7 @@ def run_ours(args, rank, world, local_rank):
     def measure(name, with_e2e, with_roofline):
         w = WORKLOADS[name]
         d = make_inputs(w, "cuda", seed=rank)
-        step = build_step(w, d, world)
+        step = build_step(w, d, world, overlap=not args.serial_allreduce)
         rec = ops.Recorder()
         for _ in range(max(args.warmup, 3)):
             step(d["sel"], d["grad_out"])
@@ -451,6 +468,8 @@ def run_ours(args, rank, world, local_rank):
         "config": {"workload": w.name, "tokens_per_gpu": w.T, "d_in": w.d_in, "d_out": w.d_out,
                    "experts": w.E, "top_k": w.k, "weighted": w.weighted, "route_input": w.route_input,
                    "global_tokens": w.T * world, "parallelism": f"token-sharded dp{world}",
+                   "grad_w_allreduce": None if world == 1 else ("after backward" if args.serial_allreduce
+                                                                 else "overlapped with grad-x"),
                    "l2": "flushed (256 MiB write) before every timed step",
                    "cuda_graph": main["graphed"],
                    "flops_per_step_per_gpu": w.flops(),
@@ -471,6 +490,8 @@ def run_ours(args, rank, world, local_rank):
             also[name] = {"value": round(r["tflops"], 3), "unit": "TFLOP/s", "ms_per_step": round(r["ms"], 4),
                           "pct_bf16_peak_sustained": round(100 * r["tflops"] / pk["bf16_tflops_sustained"], 2),
                           "roofline": r["roofline"], "step_roofline": r["step_roofline"]}
+        for name in [s for s in args.also.split(",") if s in FFN_SHAPES]:
+            also[name] = measure_ffn(FFN_SHAPES[name], args, flush, pk)
         line["also"] = also
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w, budget_s=10.0)
@@ -487,14 +508,106 @@ def gemm_bytes(w):
     R, T, E, di, do = w.R, w.T, w.E, w.d_in, w.d_out
     act = 2 if w.amp else 4
     wts = E * di * do * 4
-    x_rows = R if w.route_input else T        # unique input rows
+    x_rows = w.x_rows                         # unique input rows
     g_rows = T if w.weighted else R           # unique grad rows
     fw = x_rows * di * act + wts + g_rows * do * act + (R * 4 if w.weighted else 0)
     gx = g_rows * do * act + wts + x_rows * di * act
     if w.weighted:
-        gx += R * 4 + R * 4 + (R * di * act if w.route_input else 0)  # w in, sel grad out, x for the dot
+        gx += R * 4 + R * 4 + (w.x_rows * di * act if w.route_input else 0)  # w in, sel grad out, x for the dot
     gw = x_rows * di * act + g_rows * do * act + wts + (R * 4 if w.weighted else 0)
     return {"cvmm_forward": fw, "cvmm_backward_x": gx, "cvmm_backward_w": gw}
+
+
+# ------------------------------------------------------------------ the sigma-MoE layer
+# The reference's FFN benchmark shapes (benchmark_ffn_moe.py:26-38): B x T tokens,
+# model width D, expert width H, top-K of E experts.
+FFN_SHAPES = {
+    "ffn_1024": dict(B=8, T=2048, D=1024, H=128, K=8, E=512),
+    "ffn_2048": dict(B=4, T=2048, D=2048, H=128, K=8, E=512),
+}
+
+
+def measure_ffn(shape, args, flush, pk):
+    """One sigma-MoE FFN layer step (router matmul, fused router top-k, one
+    selector prep, up projection with fused GELU, weighted down projection,
+    full backward) as a CUDA graph, against the same layer composed as the
+    reference writes it (torch softmax/topk/renormalisation, F.gelu, two
+    selector preps) on the same CVMM kernels. Seeded synthetic inputs; fp32
+    parameters under bf16 autocast."""
+    import math
+
+    import torch.nn.functional as F
+
+    from cvmm_codex_b200 import cvmm, cvmm_prepare_sel2, sigma_moe_ffn
+
+    B, T, D, H, K, E = (shape[k] for k in ("B", "T", "D", "H", "K", "E"))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(B * T, D, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    gate = (torch.randn(D, E, device="cuda", generator=g) / math.sqrt(D)).requires_grad_(True)
+    w_up = (torch.randn(E, D, H, device="cuda", generator=g) / math.sqrt(D)).requires_grad_(True)
+    w_down = (torch.randn(E, H, D, device="cuda", generator=g) / math.sqrt(H)).requires_grad_(True)
+    grad = torch.randn(B * T, D, device="cuda", generator=g).bfloat16()
+    params = (x, gate, w_up, w_down)
+
+    def fused():
+        with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+            out = sigma_moe_ffn(x, gate, w_up, w_down, K)
+        out.backward(grad)
+
+    def composed():  # benchmark_ffn_moe.py:87-98
+        with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+            logits = x @ gate
+            probs = torch.softmax(logits.float(), dim=-1)
+            weights, sel = probs.topk(K, dim=-1)
+            weights = weights / weights.sum(dim=-1, keepdim=True).clamp_min(1e-20)
+            sel_up = cvmm_prepare_sel2(sel)
+            hidden = F.gelu(cvmm(x, sel_up, w_up))
+            sel_down = cvmm_prepare_sel2(sel_up, weights, route_input=True)
+            out = cvmm(hidden.view(B * T, K, H), sel_down, w_down)
+        out.backward(grad)
+
+    def run(fn):
+        def step():
+            for p in params:
+                p.grad = None
+            fn()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                step()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+        torch.cuda.synchronize()
+        total = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            graph.replay()
+            b.record()
+            b.synchronize()
+            total += a.elapsed_time(b)
+        del graph
+        return total / args.steps
+
+    ms = run(fused)
+    ms_composed = run(composed)
+    R = B * T * K
+    flops_cvmm = 12.0 * R * D * H        # up + down, 3 GEMMs each
+    flops_router = 6.0 * B * T * D * E   # x @ gate forward and its two backward GEMMs
+    return {"value": round((flops_cvmm + flops_router) / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+            "ms_per_step": round(ms, 4), "ms_per_step_reference_composition": round(ms_composed, 4),
+            "config": {"tokens": B * T, "d_model": D, "expert_width": H, "top_k": K, "experts": E,
+                       "flops_cvmm": flops_cvmm, "flops_router": flops_router,
+                       "what": "sigma-MoE FFN layer fw+bw: fused router top-k, one selector prep, "
+                               "GELU in the up projection's epilogue"}}
 
 
 def call_work(w, name):
@@ -519,7 +632,7 @@ def call_work(w, name):
     if name == "cvmm_cast":
         return 0.0, 0.0, float(wts * (4 + 2))
     if name == "cvmm_sort_rows_padded":
-        x_copy = (R if w.route_input else T) * di * 2 + R * di * 2
+        x_copy = w.x_rows * di * 2 + R * di * 2
         g_copy = (T * do * 2 + R * 4 if w.weighted else R * do * 2) + R * do * 2
         return 0.0, 0.0, float((x_copy + g_copy) / 2 if w.weighted else g_copy)
     if name == "cvmm_pad_starts":

@@ -45,7 +45,7 @@ SIGNATURES = {
                           _P, _I, _L, _I, _P, _P, _P, _P, _S, _P]),
     "cvmm_weighted_combine": (_I, [_P, _I, _P, _I, _P, _I, _L, _L, _L, _P, _P]),
     "cvmm_backward_x": (_I, [_P, _I, _L, _P, _L, _P, _P, _L, _P, _I, _L, _L, _L, _L, _L, _L,
-                             _P, _I, _L, _I, _P, _I, _P, _I, _L, _P, _I, _P, _P, _P, _S, _P]),
+                             _P, _I, _L, _I, _P, _I, _P, _I, _L, _L, _P, _I, _P, _P, _P, _S, _P]),
     "cvmm_backward_w": (_I, [_P, _I, _L, _P, _L, _P, _I, _L, _P, _L, _P, _I, _P, _P, _L, _L,
                              _L, _L, _P, _I, _P, _P, _P, _S, _P]),
     "cvmm_sort_rows_padded": (_I, [_P, _I, _L, _P, _L, _P, _I, _P, _P, _L, _L, _L, _P, _I, _P, _P]),
@@ -55,6 +55,10 @@ SIGNATURES = {
     "cvmm_selftest_wait_timeout": (_I, [_L, _P]),
     "cvmm_weighted_token_backward": (_I, [_P, _I, _P, _I, _P, _I, _P, _I, _P, _L, _L, _L, _P]),
     "cvmm_cast": (_I, [_P, _I, _P, _I, _L, _P]),
+    "cvmm_forward_gelu": (_I, [_P, _I, _L, _L, _P, _P, _P, _L, _P, _I, _L, _L, _L, _L, _L, _L,
+                               _P, _P, _I, _L, _I, _P, _P, _S, _P]),
+    "cvmm_gelu_backward": (_I, [_P, _P, _P, _I, _L, _P]),
+    "cvmm_router_topk": (_I, [_P, _I, _L, _L, _L, _I, _P, _P, _P]),
 }
 
 _lib = None
@@ -82,7 +86,7 @@ def load():
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if lib.cvmm_abi_version() != 5:
+        if lib.cvmm_abi_version() != 6:
             raise CvmmLibraryError("libcvmm_sm100.so ABI version mismatch; rebuild it")
         _lib = lib
     return _lib

@@ -170,9 +170,9 @@ def _(x, sel_index, offsets, keys, out_index, out_dtype, op_dtype, x_pad_start, 
 def backward_x(g: torch.Tensor, g_index: Optional[torch.Tensor], g_div: int, out_index: Optional[torch.Tensor],
                offsets: torch.Tensor, keys: torch.Tensor, out_dtype: torch.dtype, op_dtype: torch.dtype,
                w: Optional[torch.Tensor], x: Optional[torch.Tensor], g_pad_start: Optional[torch.Tensor],
-               out_pad_start: Optional[torch.Tensor], n_routes: int) -> tuple[torch.Tensor, torch.Tensor]:
+               out_pad_start: Optional[torch.Tensor], n_routes: int, x_div: int) -> tuple[torch.Tensor, torch.Tensor]:
     res = ops.backward_x(g, g_index, g_div, out_index, offsets, keys, out_dtype, op_dtype, w=w, x=x,
-                         g_pad_start=g_pad_start, out_pad_start=out_pad_start, n_routes=n_routes)
+                         g_pad_start=g_pad_start, out_pad_start=out_pad_start, n_routes=n_routes, x_div=x_div)
     if w is None:
         return res, torch.empty(0, dtype=torch.float32, device=g.device)
     return res
@@ -180,7 +180,7 @@ def backward_x(g: torch.Tensor, g_index: Optional[torch.Tensor], g_div: int, out
 
 @backward_x.register_fake
 def _(g, g_index, g_div, out_index, offsets, keys, out_dtype, op_dtype, w, x, g_pad_start, out_pad_start,
-      n_routes):
+      n_routes, x_div):
     E, K, N = keys.shape
     rows = n_routes + E * PAD if out_pad_start is not None else n_routes
     return (g.new_empty((rows, K), dtype=out_dtype),
@@ -201,6 +201,47 @@ def backward_w(x: torch.Tensor, x_index: Optional[torch.Tensor], x_div: int, g: 
 def _(x, x_index, x_div, g, g_index, g_div, offsets, n_experts, op_dtype, w, w_index, g_pad_start, x_pad_start,
       n_routes):
     return x.new_empty((n_experts, x.shape[-1], g.shape[-1]), dtype=torch.float32)
+
+
+# ------------------------------------------------------------------ sigma-MoE layer pieces
+@torch.library.custom_op("cvmm_b200::forward_gelu", mutates_args=())
+def forward_gelu(x: torch.Tensor, sel_index: torch.Tensor, offsets: torch.Tensor, keys: torch.Tensor,
+                 out_index: Optional[torch.Tensor], op_dtype: torch.dtype,
+                 x_copy: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    xs = None
+    if x_copy:
+        xs = torch.empty((sel_index.numel() + keys.shape[0] * PAD, x.shape[-1]), dtype=op_dtype, device=x.device)
+    h, z = ops.forward_gelu(x, sel_index, offsets, keys, out_index, op_dtype, x_copy=xs)
+    return h, z, (xs if xs is not None else torch.empty(0, dtype=op_dtype, device=x.device))
+
+
+@forward_gelu.register_fake
+def _(x, sel_index, offsets, keys, out_index, op_dtype, x_copy):
+    E, K, N = keys.shape
+    R = sel_index.numel()
+    return (x.new_empty((R, N), dtype=op_dtype), x.new_empty((R, N), dtype=op_dtype),
+            x.new_empty((R + E * PAD, K) if x_copy else (0,), dtype=op_dtype))
+
+
+@torch.library.custom_op("cvmm_b200::gelu_backward", mutates_args=())
+def gelu_backward(grad: torch.Tensor, pre_act: torch.Tensor) -> torch.Tensor:
+    return ops.gelu_backward(grad, pre_act)
+
+
+@gelu_backward.register_fake
+def _(grad, pre_act):
+    return torch.empty_like(pre_act)
+
+
+@torch.library.custom_op("cvmm_b200::router_topk", mutates_args=())
+def router_topk(logits: torch.Tensor, top_k: int, renormalize: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    return ops.router_topk(logits, top_k, renormalize)
+
+
+@router_topk.register_fake
+def _(logits, top_k, renormalize):
+    shape = (*logits.shape[:-1], top_k)
+    return logits.new_empty(shape, dtype=torch.float32), logits.new_empty(shape, dtype=torch.int64)
 
 
 # ------------------------------------------------------------------ the reference's op schema
@@ -298,15 +339,16 @@ class _Calls:
         return (out, xs) if x_copy else out
 
     def backward_x(self, g, g_index, g_div, out_index, offsets, keys, out_dtype, op_dtype, w=None, x=None,
-                   g_pad_start=None, out_pad_start=None, n_routes=None):
+                   g_pad_start=None, out_pad_start=None, n_routes=None, x_div=1):
         if n_routes is None:
             n_routes = out_index.numel()
         if self._tracing():
             out, gsel = torch.ops.cvmm_b200.backward_x(g, g_index, g_div, out_index, offsets, keys, out_dtype,
-                                                       op_dtype, w, x, g_pad_start, out_pad_start, int(n_routes))
+                                                       op_dtype, w, x, g_pad_start, out_pad_start, int(n_routes),
+                                                       int(x_div))
             return out if w is None else (out, gsel)
         return ops.backward_x(g, g_index, g_div, out_index, offsets, keys, out_dtype, op_dtype, w=w, x=x,
-                              g_pad_start=g_pad_start, out_pad_start=out_pad_start, n_routes=n_routes)
+                              g_pad_start=g_pad_start, out_pad_start=out_pad_start, n_routes=n_routes, x_div=x_div)
 
     def backward_w(self, x, x_index, x_div, g, g_index, g_div, offsets, n_experts, op_dtype, w=None, w_index=None,
                    g_pad_start=None, x_pad_start=None, n_routes=None):
@@ -317,6 +359,28 @@ class _Calls:
                                                   op_dtype, w, w_index, g_pad_start, x_pad_start, int(n_routes))
         return ops.backward_w(x, x_index, x_div, g, g_index, g_div, offsets, n_experts, op_dtype, w=w,
                               w_index=w_index, g_pad_start=g_pad_start, x_pad_start=x_pad_start, n_routes=n_routes)
+
+    def forward_gelu(self, x, sel_index, offsets, keys, out_index, op_dtype, x_copy=False):
+        """Returns (h, z, x_copy or None)."""
+        if self._tracing():
+            h, z, xs = torch.ops.cvmm_b200.forward_gelu(x, sel_index, offsets, keys, out_index, op_dtype,
+                                                        bool(x_copy))
+            return h, z, (xs if x_copy else None)
+        xs = None
+        if x_copy:
+            xs = torch.empty((sel_index.numel() + keys.shape[0] * PAD, x.shape[-1]), dtype=op_dtype, device=x.device)
+        h, z = ops.forward_gelu(x, sel_index, offsets, keys, out_index, op_dtype, x_copy=xs)
+        return h, z, xs
+
+    def gelu_backward(self, grad, pre_act):
+        if self._tracing():
+            return torch.ops.cvmm_b200.gelu_backward(grad, pre_act)
+        return ops.gelu_backward(grad, pre_act)
+
+    def router_topk(self, logits, top_k, renormalize=True):
+        if self._tracing():
+            return torch.ops.cvmm_b200.router_topk(logits, top_k, renormalize)
+        return ops.router_topk(logits, top_k, renormalize)
 
 
 calls = _Calls()

@@ -120,6 +120,12 @@ cvmm_sorted_operands = os.environ.get("CVMM_B200_SORTED_OPERANDS", "1").lower() 
 # sorted copy of the token grads (True) instead of gathering and scaling the
 # token grad rows inside the GEMM (False). Both give bit-identical results.
 cvmm_weighted_grad_copy = os.environ.get("CVMM_B200_WEIGHTED_GRAD_COPY", "1").lower() not in ("0", "false", "no", "off")
+# Data-parallel hook (None, or an object with grad_keys_ready(grad_keys) and
+# backward_done()): CVMM.backward calls grad_keys_ready on the compute stream
+# as soon as the fp32 expert-weight gradient is written, before the grad-x
+# work, and backward_done just before it returns, so a caller can reduce the
+# weight gradient across ranks while grad-x runs (dist.OverlappedGradReduce).
+cvmm_backward_hook = None
 # Opt-in host check of the device status word after every CVMM forward and
 # backward (synchronises the stream): raises RuntimeError when a kernel gave up
 # on a bounded wait or met an out-of-range expert id.
@@ -179,6 +185,23 @@ def _sortable(t: torch.Tensor, op_dtype: torch.dtype) -> bool:
             and t.shape[-1] % 8 == 0)
 
 
+def _routes_per_row(x: torch.Tensor, sel: torch.Tensor, out_index: Optional[torch.Tensor]) -> int:
+    """Routes that share one row of x. 1 for the reference's two layouts
+    (token-shaped x with out_index, route-shaped x without). A route-indexed
+    selector sel [..., K] over x [..., H, d] with K = r * H (r > 1) means that
+    the r consecutive routes of every row read that row: SwitchHead's output
+    projection, whose 2 routes per head read the head's value row. The
+    reference needs x repeated r times for this (x.repeat_interleave); here
+    the kernels index row p // r instead (no reference counterpart)."""
+    if out_index is not None or x.dim() < 2 or sel.dim() < 1:
+        return 1
+    rows = x.numel() // x.shape[-1]
+    n = sel.numel()
+    if rows == 0 or rows >= n or n % rows != 0 or tuple(x.shape[:-2]) != tuple(sel.shape[:-1]):
+        return 1
+    return n // rows
+
+
 def _raise_on_device_status(where: str) -> None:
     """Reads and clears the library's device status word (synchronises) and
     raises if a kernel recorded a timeout or an out-of-range expert id."""
@@ -202,19 +225,27 @@ class CVMM(torch.autograd.Function):
         n_experts = keys.shape[0]
         offsets = ops.expert_offsets(sel, n_experts)
         keys_op = _operand(keys, op_dtype)
+        # Routes per x row: 1, except for a route-indexed selector over an x
+        # whose rows are shared by consecutive routes (SwitchHead: the 2 routes
+        # of a head read that head's value row; see _routes_per_row).
+        rph = _routes_per_row(x, sel, out_index)
+        x_index, oi = sel_index, out_index
+        if rph > 1:
+            x_index = torch.div(sel_index, rph, rounding_mode="floor")
+            oi = sel_index  # outputs stay route-indexed
         xs = xpad = None
         if _sortable(x, op_dtype) and reduction_weight is not None:
             # Expert-sorted, 128-row padded op-dtype copy of the route rows of x:
             # the forward and the grad-W read it as dense tiles (the reference's
             # grouped-x copy, cvmm.py:1123-1138).
-            xs, xpad = ops.sort_rows_padded(x, sel_index, 1, sel, offsets, n_experts, dtype=op_dtype)
+            xs, xpad = ops.sort_rows_padded(x, sel_index, rph, sel, offsets, n_experts, dtype=op_dtype)
         a = x if xs is None else xs
         if reduction_weight is None and _sortable(x, op_dtype):
             # The forward gathers x's rows anyway: it writes that sorted padded
             # copy for the grad-W as it goes, instead of a separate copy pass.
             # Its pad starts depend only on the offsets; the backward takes them
             # from the grad copy it makes anyway.
-            res, xs = ops.forward(x, sel_index, offsets, keys_op, out_index, op_dtype, op_dtype, x_copy=True)
+            res, xs = ops.forward(x, x_index, offsets, keys_op, oi, op_dtype, op_dtype, x_copy=True)
             res = res.view(*sel.shape, res.shape[-1])
         elif reduction_weight is not None:
             rows = out_pad = None
@@ -223,112 +254,219 @@ class CVMM(torch.autograd.Function):
                 # stores); the weighted combine gathers them per token.
                 out_pad = xpad
                 rows = ops.padded_route_rows(out_index if out_index is not None else sel_index, sel, offsets, xpad)
-            y = ops.forward(a, sel_index, offsets, keys_op, out_index, op_dtype, op_dtype, x_pad_start=xpad,
+            y = ops.forward(a, x_index, offsets, keys_op, oi, op_dtype, op_dtype, x_pad_start=xpad,
                             out_pad_start=out_pad)
             res = ops.weighted_combine(y, reduction_weight, op_dtype, y_rows=rows)
             res = res.view(*reduction_weight.shape[:-1], res.shape[-1])
         else:
-            res = ops.forward(a, sel_index, offsets, keys_op, out_index, op_dtype, op_dtype, x_pad_start=xpad)
+            res = ops.forward(a, x_index, offsets, keys_op, oi, op_dtype, op_dtype, x_pad_start=xpad)
             res = res.view(*sel.shape, res.shape[-1])
         ctx.save_for_backward(x, keys_op, raw_sel, sel, sel_index, out_index, reduction_weight, offsets, xs, xpad)
         ctx.op_type = op_dtype
         ctx.keys_type = keys.dtype
         ctx.dtype = op_dtype
+        ctx.rph = rph
         if cvmm_check_device_status:
             _raise_on_device_status("CVMM.forward")
         return res
 
     @staticmethod
     def backward(ctx, grad_output):
-        x, keys_op, raw_sel, sel, sel_index, out_index, w, offsets, xs, xpad = ctx.saved_tensors
-        need_x = ctx.needs_input_grad[0]
-        need_keys = ctx.needs_input_grad[4]
-        need_w = len(ctx.needs_input_grad) > 6 and ctx.needs_input_grad[6] and w is not None
-        op = ctx.op_type
-        n_experts = keys_op.shape[0]
-        n_routes = sel.numel()
-        top_k = raw_sel.shape[-1] if raw_sel.dim() > 0 else 1
-        # Route id of every sorted position: where its output row lives.
-        route = out_index if out_index is not None else sel_index
-        g = grad_output
-        if g.dtype not in (torch.float32, torch.float16, torch.bfloat16):
-            g = g.float()
-        x_rows = x.reshape(-1, x.shape[-1]).shape[0]
+        return _cvmm_backward(ctx, ctx.saved_tensors, grad_output)
 
-        grad_x = grad_keys = grad_w = None
-        if w is None:
-            g2 = g.reshape(n_routes, g.shape[-1])
-            g_rows, g_idx, g_pad = g2, route, None
-            if _sortable(g2, op):
-                # One expert-padded sorted copy of the route grads (the
-                # reference's grouping copy, cvmm.py:1161) lets both GEMMs read
-                # them as dense tensor-core tiles.
-                g_rows, g_pad = ops.sort_rows_padded(g2, route, 1, sel, offsets, n_experts, dtype=op)
-                g_idx = None
-            if xs is not None and xpad is None:
-                xpad = g_pad if g_pad is not None else ops.pad_starts(offsets, n_experts)
-            if need_keys:
-                # dW_e = sum_p x[sel_index[p]]^T g[route[p]]  (cvmm.py:1163-1198)
-                if xs is not None:
-                    grad_keys = ops.backward_w(xs, None, 1, g_rows, g_idx, 1, offsets, n_experts, op,
-                                               g_pad_start=g_pad, x_pad_start=xpad, n_routes=n_routes)
-                else:
-                    grad_keys = ops.backward_w(x, sel_index, 1, g_rows, g_idx, 1, offsets, n_experts, op,
-                                               g_pad_start=g_pad)
-            if need_x:
-                # gx_route[route] = g[route] W_e^T, then summed over k (cvmm.py:1199-1223)
-                if x_rows == n_routes:
-                    gxr = ops.backward_x(g_rows, g_idx, 1, route, offsets, keys_op, x.dtype, op, g_pad_start=g_pad)
-                    grad_x = gxr.view_as(x)
-                elif g_pad is not None and x.dtype == op and x.shape[-1] % 8 == 0:
-                    # Route grads stay in the padded sorted layout (dense TMA
-                    # tile stores); the k-sum gathers them per token.
-                    gxs = ops.backward_x(g_rows, None, 1, None, offsets, keys_op, x.dtype, op, g_pad_start=g_pad,
-                                         out_pad_start=g_pad, n_routes=n_routes)
-                    rows = ops.padded_route_rows(route, sel, offsets, g_pad)
-                    grad_x = ops.sum_routes(gxs, n_routes // x_rows, x.dtype, src_rows=rows).view_as(x)
-                else:
-                    gxr = ops.backward_x(g_rows, g_idx, 1, route, offsets, keys_op, x.dtype, op, g_pad_start=g_pad)
-                    grad_x = ops.sum_routes(gxr, n_routes // x_rows, x.dtype).view_as(x)
-        else:
-            k = w.shape[-1]
-            gt = g.reshape(-1, g.shape[-1])  # token grads of the combined output
-            if need_keys:
-                # dW_e = sum_p x[sel_index[p]]^T (bf16(w_p) * g[route_p // k])  (cvmm.py:1341-1383)
-                if xs is not None and _sortable(gt, op) and cvmm_weighted_grad_copy:
-                    # The weight product is applied (and rounded) in a sorted copy.
-                    gs, gpad = ops.sort_rows_padded(gt, route, k, sel, offsets, n_experts, dtype=op, scale=w)
-                    grad_keys = ops.backward_w(xs, None, 1, gs, None, 1, offsets, n_experts, op,
-                                               g_pad_start=gpad, x_pad_start=xpad, n_routes=n_routes)
-                    del gs
-                elif xs is not None:
-                    # Token grad rows gathered straight from g (L2-resident) and
-                    # scaled by op(w) in shared memory (cvmm.py:591-599): no
-                    # R x d_out weighted copy is written.
-                    grad_keys = ops.backward_w(xs, None, 1, gt, route, k, offsets, n_experts, op,
-                                               w=w, w_index=route, x_pad_start=xpad, n_routes=n_routes)
-                else:
-                    grad_keys = ops.backward_w(x, sel_index, 1, gt, route, k, offsets, n_experts, op,
-                                               w=w, w_index=route)
-            if need_x or need_w:
-                if out_index is None and tuple(x.shape[:-1]) == tuple(w.shape):
-                    # Route-shaped input: fused grad-x + sel-weight grad (cvmm.py:1386-1433)
-                    gx, gsel = ops.backward_x(gt, route, k, route, offsets, keys_op, x.dtype, op,
-                                              w=w, x=x)
-                    grad_x = gx.view_as(x) if need_x else None
-                    grad_w = gsel.view_as(w).to(w.dtype) if need_w else None
-                else:
-                    # Token-shaped input: route grads, then weighted token sums (cvmm.py:1726-1750)
-                    rg = ops.backward_x(gt, route, k, route, offsets, keys_op, op, op)
-                    gx, gsel = ops.weighted_token_backward(rg, w, x, need_x, need_w, x.dtype)
-                    grad_x = gx.view_as(x) if need_x else None
-                    grad_w = gsel.view_as(w).to(w.dtype) if need_w else None
-        if grad_keys is not None and ctx.keys_type != torch.float32:
-            grad_keys = grad_keys.to(ctx.keys_type)
-        del top_k
+
+def _cvmm_backward(ctx, saved, grad_output):
+    """CVMM.backward on the tensors saved by the forward (shared with CVMMGelu)."""
+    x, keys_op, raw_sel, sel, sel_index, out_index, w, offsets, xs, xpad = saved
+    need_x = ctx.needs_input_grad[0]
+    need_keys = ctx.needs_input_grad[4]
+    need_w = len(ctx.needs_input_grad) > 6 and ctx.needs_input_grad[6] and w is not None
+    op = ctx.op_type
+    rph = getattr(ctx, "rph", 1)
+    n_experts = keys_op.shape[0]
+    n_routes = sel.numel()
+    top_k = raw_sel.shape[-1] if raw_sel.dim() > 0 else 1
+    # Route id of every sorted position: where its output row lives.
+    route = out_index if out_index is not None else sel_index
+    g = grad_output
+    if g.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        g = g.float()
+    x_rows = x.reshape(-1, x.shape[-1]).shape[0]
+
+    grad_x = grad_keys = grad_w = None
+    if w is None:
+        g2 = g.reshape(n_routes, g.shape[-1])
+        g_rows, g_idx, g_pad = g2, route, None
+        if _sortable(g2, op):
+            # One expert-padded sorted copy of the route grads (the
+            # reference's grouping copy, cvmm.py:1161) lets both GEMMs read
+            # them as dense tensor-core tiles.
+            g_rows, g_pad = ops.sort_rows_padded(g2, route, 1, sel, offsets, n_experts, dtype=op)
+            g_idx = None
+        if xs is not None and xpad is None:
+            xpad = g_pad if g_pad is not None else ops.pad_starts(offsets, n_experts)
+        if need_keys:
+            # dW_e = sum_p x[sel_index[p]]^T g[route[p]]  (cvmm.py:1163-1198)
+            if xs is not None:
+                grad_keys = ops.backward_w(xs, None, 1, g_rows, g_idx, 1, offsets, n_experts, op,
+                                           g_pad_start=g_pad, x_pad_start=xpad, n_routes=n_routes)
+            else:
+                grad_keys = ops.backward_w(x, sel_index, rph, g_rows, g_idx, 1, offsets, n_experts, op,
+                                           g_pad_start=g_pad)
+        if grad_keys is not None and cvmm_backward_hook is not None and ctx.keys_type == torch.float32:
+            cvmm_backward_hook.grad_keys_ready(grad_keys)
+        if need_x:
+            # gx_route[route] = g[route] W_e^T, then summed over k (cvmm.py:1199-1223)
+            if x_rows == n_routes:
+                gxr = ops.backward_x(g_rows, g_idx, 1, route, offsets, keys_op, x.dtype, op, g_pad_start=g_pad)
+                grad_x = gxr.view_as(x)
+            elif g_pad is not None and x.dtype == op and x.shape[-1] % 8 == 0:
+                # Route grads stay in the padded sorted layout (dense TMA
+                # tile stores); the k-sum gathers them per token.
+                gxs = ops.backward_x(g_rows, None, 1, None, offsets, keys_op, x.dtype, op, g_pad_start=g_pad,
+                                     out_pad_start=g_pad, n_routes=n_routes)
+                rows = ops.padded_route_rows(route, sel, offsets, g_pad)
+                grad_x = ops.sum_routes(gxs, n_routes // x_rows, x.dtype, src_rows=rows).view_as(x)
+            else:
+                gxr = ops.backward_x(g_rows, g_idx, 1, route, offsets, keys_op, x.dtype, op, g_pad_start=g_pad)
+                grad_x = ops.sum_routes(gxr, n_routes // x_rows, x.dtype).view_as(x)
+    else:
+        k = w.shape[-1]
+        gt = g.reshape(-1, g.shape[-1])  # token grads of the combined output
+        if need_keys:
+            # dW_e = sum_p x[sel_index[p]]^T (bf16(w_p) * g[route_p // k])  (cvmm.py:1341-1383)
+            if xs is not None and _sortable(gt, op) and cvmm_weighted_grad_copy:
+                # The weight product is applied (and rounded) in a sorted copy.
+                gs, gpad = ops.sort_rows_padded(gt, route, k, sel, offsets, n_experts, dtype=op, scale=w)
+                grad_keys = ops.backward_w(xs, None, 1, gs, None, 1, offsets, n_experts, op,
+                                           g_pad_start=gpad, x_pad_start=xpad, n_routes=n_routes)
+                del gs
+            elif xs is not None:
+                # Token grad rows gathered straight from g (L2-resident) and
+                # scaled by op(w) in shared memory (cvmm.py:591-599): no
+                # R x d_out weighted copy is written.
+                grad_keys = ops.backward_w(xs, None, 1, gt, route, k, offsets, n_experts, op,
+                                           w=w, w_index=route, x_pad_start=xpad, n_routes=n_routes)
+            else:
+                grad_keys = ops.backward_w(x, sel_index, rph, gt, route, k, offsets, n_experts, op,
+                                           w=w, w_index=route)
+        if grad_keys is not None and cvmm_backward_hook is not None and ctx.keys_type == torch.float32:
+            cvmm_backward_hook.grad_keys_ready(grad_keys)
+        if need_x or need_w:
+            if out_index is None and rph > 1:
+                # Route-indexed selector over shared x rows (SwitchHead heads):
+                # the fused route grad-x + sel-weight grad reads x row p / rph,
+                # then each row sums its rph route grads.
+                gx, gsel = ops.backward_x(gt, route, k, route, offsets, keys_op, x.dtype, op, w=w, x=x,
+                                          x_div=rph)
+                grad_x = ops.sum_routes(gx, rph, x.dtype).view_as(x) if need_x else None
+                grad_w = gsel.view_as(w).to(w.dtype) if need_w else None
+            elif out_index is None and tuple(x.shape[:-1]) == tuple(w.shape):
+                # Route-shaped input: fused grad-x + sel-weight grad (cvmm.py:1386-1433)
+                gx, gsel = ops.backward_x(gt, route, k, route, offsets, keys_op, x.dtype, op,
+                                          w=w, x=x)
+                grad_x = gx.view_as(x) if need_x else None
+                grad_w = gsel.view_as(w).to(w.dtype) if need_w else None
+            else:
+                # Token-shaped input: route grads, then weighted token sums (cvmm.py:1726-1750)
+                rg = ops.backward_x(gt, route, k, route, offsets, keys_op, op, op)
+                gx, gsel = ops.weighted_token_backward(rg, w, x, need_x, need_w, x.dtype)
+                grad_x = gx.view_as(x) if need_x else None
+                grad_w = gsel.view_as(w).to(w.dtype) if need_w else None
+    if grad_keys is not None and ctx.keys_type != torch.float32:
+        grad_keys = grad_keys.to(ctx.keys_type)
+    del top_k
+    if cvmm_backward_hook is not None:
+        if ctx.keys_type != torch.float32 and grad_keys is not None:
+            cvmm_backward_hook.grad_keys_ready(grad_keys)  # after the cast: no overlap
+        cvmm_backward_hook.backward_done()
+    if cvmm_check_device_status:
+        _raise_on_device_status("CVMM.backward")
+    return grad_x, None, None, None, grad_keys, None, grad_w
+
+
+class CVMMGelu(torch.autograd.Function):
+    """gelu(cvmm(x, sel, keys)) with the activation fused into the forward
+    GEMM's epilogue (unweighted selector; bf16/fp16 autocast): the forward
+    writes h = gelu(z) and keeps z = the rounded GEMM output for the backward,
+    which applies gelu'(z) to the incoming gradient and then runs CVMM's
+    backward on it. The reference computes F.gelu(cvmm(...)) as two passes
+    (benchmark_ffn_moe.py:93-94); the numerics are the same: z is rounded to
+    the op dtype, the GELU is evaluated in fp32 on it and rounded."""
+
+    @staticmethod
+    def forward(ctx, x, raw_sel, sel_index, sel, keys, out_index):
+        op_dtype = get_dtype()
+        n_experts = keys.shape[0]
+        offsets = ops.expert_offsets(sel, n_experts)
+        keys_op = _operand(keys, op_dtype)
+        want_copy = _sortable(x, op_dtype)
+        h, z, xs = ops.forward_gelu(x, sel_index, offsets, keys_op, out_index, op_dtype, x_copy=want_copy)
+        ctx.save_for_backward(x, keys_op, raw_sel, sel, sel_index, out_index, None, offsets, xs, None, z)
+        ctx.op_type = op_dtype
+        ctx.keys_type = keys.dtype
+        ctx.dtype = op_dtype
         if cvmm_check_device_status:
-            _raise_on_device_status("CVMM.backward")
-        return grad_x, None, None, None, grad_keys, None, grad_w
+            _raise_on_device_status("CVMMGelu.forward")
+        return h.view(*sel.shape, h.shape[-1])
+
+    @staticmethod
+    def backward(ctx, grad_h):
+        saved = ctx.saved_tensors
+        z = saved[10]
+        g = grad_h.reshape(z.shape)
+        if g.dtype != z.dtype:
+            g = g.to(z.dtype)
+        dz = ops.gelu_backward(g, z).view(grad_h.shape)
+        return _cvmm_backward(ctx, saved[:10], dz)[:6]
+
+
+def cvmm_gelu(x: torch.Tensor, sel: Union[torch.Tensor, CVMMSel], keys: torch.Tensor) -> torch.Tensor:
+    """F.gelu(cvmm(x, sel, keys)) with GELU fused into the GEMM epilogue (no
+    reference counterpart as one call; the reference composes the two,
+    benchmark_ffn_moe.py:93-94). Falls back to that composition, on the same
+    device kernels plus torch's GELU, for fp32 arithmetic (no autocast) and
+    for a weighted selector."""
+    if not isinstance(sel, CVMMSel):
+        sel = cvmm_prepare_sel(sel, keys.shape[0])
+    op_dtype = get_dtype()
+    if op_dtype == torch.float32 or sel.reduction_weight is not None:
+        return torch.nn.functional.gelu(cvmm(x, sel, keys))
+    if not torch.compiler.is_compiling():
+        create_kernels()
+    return CVMMGelu.apply(x, sel.raw_sel, sel.sel_index, sel.sel, keys, sel.out_index)
+
+
+def router_topk(logits: torch.Tensor, top_k: int, renormalize: bool = True):
+    """(weights, sel) of the sigma-MoE router (benchmark_ffn_moe.py:89-92):
+    softmax(float(logits)), top-k in descending order, weights renormalised
+    to sum to one; one fused kernel. Differentiable w.r.t. the logits."""
+    return _RouterTopK.apply(logits, int(top_k), bool(renormalize))
+
+
+class _RouterTopK(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, logits, top_k, renormalize):
+        w, sel = ops.router_topk(logits, top_k, renormalize)
+        ctx.save_for_backward(logits, sel, w)
+        ctx.renormalize = renormalize
+        ctx.mark_non_differentiable(sel)
+        return w, sel
+
+    @staticmethod
+    def backward(ctx, grad_w, grad_sel):
+        logits, sel, w = ctx.saved_tensors
+        p = torch.softmax(logits.float(), dim=-1)
+        gw = grad_w.float()
+        if ctx.renormalize:
+            # w = p_sel / s, s = sum(p_sel): d p_sel = (dw - sum(dw * w)) / s
+            s = p.gather(-1, sel).sum(-1, keepdim=True).clamp_min(1e-20)
+            gp_sel = (gw - (gw * w).sum(-1, keepdim=True)) / s
+        else:
+            gp_sel = gw
+        gp = torch.zeros_like(p).scatter_(-1, sel, gp_sel)
+        gl = p * (gp - (p * gp).sum(-1, keepdim=True))
+        return gl.to(logits.dtype), None, None
 
 
 known_shapes = set()

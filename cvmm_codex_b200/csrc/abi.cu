@@ -152,6 +152,102 @@ __global__ void __launch_bounds__(256, 3) combine_vec_kernel(const uint4* __rest
   }
 }
 
+// dz = dh * gelu'(z), fp32 math on the 16-bit values, rounded once (the
+// elementwise backward of F.gelu that follows the down projection's grad-x).
+__global__ void __launch_bounds__(256) gelu_backward_kernel(const void* __restrict__ grad, const void* __restrict__ z,
+                                                            void* __restrict__ out, int dtype, int64_t n, bool vec) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (vec) {
+    const uint4* g4 = static_cast<const uint4*>(grad);
+    const uint4* z4 = static_cast<const uint4*>(z);
+    uint4* o4 = static_cast<uint4*>(out);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n / 8; i += stride) {
+      const uint4 gv = g4[i], zv = z4[i];
+      const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, zw[4] = {zv.x, zv.y, zv.z, zv.w};
+      uint32_t ow[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float lo = bits_to_float((uint16_t)(gw[h] & 0xffffu), dtype) *
+                         gelu_erf_grad(bits_to_float((uint16_t)(zw[h] & 0xffffu), dtype));
+        const float hi = bits_to_float((uint16_t)(gw[h] >> 16), dtype) *
+                         gelu_erf_grad(bits_to_float((uint16_t)(zw[h] >> 16), dtype));
+        ow[h] = pack2(lo, hi, dtype);
+      }
+      o4[i] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    }
+    return;
+  }
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride)
+    store_from_float(out, dtype, i, load_as_float(grad, dtype, i) * gelu_erf_grad(load_as_float(z, dtype, i)));
+}
+
+// Router of the sigma-MoE layer (the caller of CVMM, benchmark_ffn_moe.py:89-92):
+// probs = softmax(float(logits)); (w, sel) = top-k(probs) in descending order;
+// w /= max(sum(w), 1e-20) when renormalize. One warp per token, the token's
+// logits held in registers (n_experts <= 1024: 32 per lane); the top-k are k
+// rounds of a warp arg-max (ties to the lower expert id).
+constexpr int kRouterMaxExperts = 1024;
+
+__global__ void __launch_bounds__(256) router_topk_kernel(const void* __restrict__ logits, int dtype, int64_t T,
+                                                          int64_t E, int64_t k, int renorm,
+                                                          int64_t* __restrict__ sel, float* __restrict__ weights) {
+  constexpr int kPer = kRouterMaxExperts / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  if (t >= T) return;
+  float v[kPer];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) {
+    const int64_t e = lane + 32 * q;
+    v[q] = e < E ? load_as_float(logits, dtype, t * E + e) : -INFINITY;
+    mx = fmaxf(mx, v[q]);
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) {
+    v[q] = (lane + 32 * q) < E ? expf(v[q] - mx) : 0.f;
+    sum += v[q];
+  }
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) v[q] = (lane + 32 * q) < E ? v[q] / sum : -1.f;
+  float mine = 0.f;  // lane j < k keeps the j-th selected probability
+  int64_t my_e = 0;
+  float tot = 0.f;
+  for (int j = 0; j < (int)k; ++j) {
+    float bv = -2.f;
+    int be = 0x7fffffff;
+#pragma unroll
+    for (int q = 0; q < kPer; ++q)
+      if (v[q] > bv) {
+        bv = v[q];
+        be = lane + 32 * q;
+      }
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+      if (ov > bv || (ov == bv && oe < be)) {
+        bv = ov;
+        be = oe;
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kPer; ++q)
+      if (lane + 32 * q == be) v[q] = -1.f;  // remove the winner (only its lane holds it)
+    if (lane == j) {
+      mine = bv;
+      my_e = be;
+    }
+    tot += bv;
+  }
+  if (lane < k) {
+    sel[t * k + lane] = my_e;
+    weights[t * k + lane] = renorm ? mine / fmaxf(tot, 1e-20f) : mine;
+  }
+}
+
 // Self-test of the bounded-wait path every persistent kernel relies on: one
 // thread waits on an mbarrier that nothing ever arrives on, through the same
 // bounded wait as the GEMM roles, so the wait runs out after `limit_ns`, the
@@ -335,7 +431,7 @@ using namespace cvmm;
 // ================================================================== C ABI
 extern "C" {
 
-int cvmm_abi_version(void) { return 5; }
+int cvmm_abi_version(void) { return 6; }
 
 const char* cvmm_last_error(void) { return t_err; }
 
@@ -419,6 +515,63 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld, const
   return run_row_gemm(p, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), "cvmm_forward");
 }
 
+int cvmm_forward_gelu(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld, const int64_t* sel_index,
+                      const int64_t* out_index, const int64_t* offsets, int64_t n_routes, const void* keys,
+                      int keys_dtype, int64_t n_experts, int64_t k_dim, int64_t n_dim, int64_t ks_e, int64_t ks_k,
+                      int64_t ks_n, void* out, void* pre_act, int out_dtype, int64_t out_ld, int op_dtype,
+                      void* x_copy, void* workspace, size_t workspace_bytes, cvmm_stream_t stream) {
+  if (op_dtype == F32 || (out_dtype != BF16 && out_dtype != F16) || out_dtype != op_dtype)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward_gelu: needs a bf16/fp16 op_dtype and out_dtype == op_dtype");
+  if (!pre_act) return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward_gelu: null pre_act");
+  if (!is_float_dtype(x_dtype) || !is_float_dtype(keys_dtype))
+    return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_forward_gelu: unsupported dtype");
+  if (n_routes < 0 || n_experts <= 0 || k_dim < 0 || n_dim <= 0 || x_rows < 0 || x_ld < k_dim || out_ld < n_dim)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward_gelu: bad sizes");
+  if (n_routes == 0) return CVMM_OK;
+  if (n_routes > (int64_t)INT32_MAX || x_rows > (int64_t)INT32_MAX)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward_gelu: more than 2^31 routes or rows");
+  if (!x || !sel_index || !offsets || !keys || !out)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_forward_gelu: null pointer");
+  RowGemm p = {};
+  p.a = x; p.a_dtype = x_dtype; p.a_ld = x_ld; p.a_rows = x_rows;
+  p.a_index = sel_index; p.a_div = 1;
+  p.b = keys; p.b_dtype = keys_dtype; p.bs_e = ks_e; p.bs_k = ks_k; p.bs_n = ks_n;
+  p.c = out; p.c_dtype = out_dtype; p.c_ld = out_ld; p.c_index = out_index ? out_index : sel_index;
+  p.a_copy = x_copy;
+  p.offsets = offsets; p.n_routes = n_routes; p.n_experts = n_experts; p.K = k_dim; p.N = n_dim;
+  p.mode = 0; p.op_dtype = op_dtype; p.act = 1; p.c2 = pre_act;
+  return run_row_gemm(p, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), "cvmm_forward_gelu");
+}
+
+int cvmm_gelu_backward(const void* grad, const void* pre_act, void* grad_pre_act, int dtype, int64_t n,
+                       cvmm_stream_t stream) {
+  if (dtype != BF16 && dtype != F16) return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_gelu_backward: bf16/fp16 only");
+  if (n < 0) return fail(CVMM_ERR_INVALID_ARG, "cvmm_gelu_backward: bad size");
+  if (n == 0) return CVMM_OK;
+  if (!grad || !pre_act || !grad_pre_act) return fail(CVMM_ERR_INVALID_ARG, "cvmm_gelu_backward: null pointer");
+  const bool vec = n % 8 == 0 && al16(grad) && al16(pre_act) && al16(grad_pre_act);
+  const int64_t items = vec ? n / 8 : n;
+  const unsigned grid = (unsigned)std::min<int64_t>((items + 255) / 256, 148 * 16);
+  gelu_backward_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(grad, pre_act, grad_pre_act,
+                                                                                dtype, n, vec);
+  return check_launch("cvmm_gelu_backward");
+}
+
+int cvmm_router_topk(const void* logits, int logits_dtype, int64_t n_tokens, int64_t n_experts, int64_t top_k,
+                     int renormalize, int64_t* sel, float* weights, cvmm_stream_t stream) {
+  if (logits_dtype != F32 && logits_dtype != BF16 && logits_dtype != F16)
+    return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_router_topk: unsupported logits dtype");
+  if (n_tokens < 0 || n_experts <= 0 || n_experts > kRouterMaxExperts || top_k <= 0 || top_k > n_experts ||
+      top_k > 32)
+    return fail(CVMM_ERR_INVALID_ARG, "cvmm_router_topk: needs 1 <= top_k <= min(32, n_experts), n_experts <= 1024");
+  if (n_tokens == 0) return CVMM_OK;
+  if (!logits || !sel || !weights) return fail(CVMM_ERR_INVALID_ARG, "cvmm_router_topk: null pointer");
+  const unsigned grid = (unsigned)((n_tokens + 7) / 8);
+  router_topk_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      logits, logits_dtype, n_tokens, n_experts, top_k, renormalize, sel, weights);
+  return check_launch("cvmm_router_topk");
+}
+
 int cvmm_weighted_combine(const void* y, int y_dtype, const void* w, int w_dtype, void* out,
                           int out_dtype, int64_t n_tokens, int64_t top_k, int64_t n_dim,
                           const int32_t* y_rows, cvmm_stream_t stream) {
@@ -475,8 +628,8 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
                     const void* keys, int keys_dtype, int64_t n_experts, int64_t k_dim, int64_t n_dim,
                     int64_t ks_e, int64_t ks_k, int64_t ks_n, void* out, int out_dtype, int64_t out_ld,
                     int mode, const void* w, int w_dtype, const void* x, int x_dtype, int64_t x_ld,
-                    float* gsel, int op_dtype, const int32_t* g_pad_start, const int32_t* out_pad_start,
-                    void* workspace, size_t workspace_bytes, cvmm_stream_t stream) {
+                    int64_t x_div, float* gsel, int op_dtype, const int32_t* g_pad_start,
+                    const int32_t* out_pad_start, void* workspace, size_t workspace_bytes, cvmm_stream_t stream) {
   if (!is_float_dtype(g_dtype) || !is_float_dtype(keys_dtype) || !is_float_dtype(out_dtype) ||
       !is_float_dtype(op_dtype))
     return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_backward_x: unsupported dtype");
@@ -492,7 +645,8 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: a padded sorted output needs mode 0 and a bf16/fp16 op_dtype");
   if (g_pad_start && op_dtype == F32)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: the padded sorted gradient layout needs bf16/fp16 op_dtype");
-  if (mode == 1 && (!w || !x || !gsel || !is_float_dtype(w_dtype) || !is_float_dtype(x_dtype) || x_ld < k_dim))
+  if (mode == 1 && (!w || !x || !gsel || !is_float_dtype(w_dtype) || !is_float_dtype(x_dtype) || x_ld < k_dim ||
+                    x_div <= 0))
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_x: mode 1 needs w, x and gsel");
   RowGemm p = {};
   // B_e[kk][nn] = keys[e][nn][kk]: contract over n_dim, produce k_dim columns.
@@ -502,6 +656,7 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
   p.c = out; p.c_dtype = out_dtype; p.c_ld = out_ld; p.c_index = out_index;
   p.offsets = offsets; p.n_routes = n_routes; p.n_experts = n_experts; p.K = n_dim; p.N = k_dim;
   p.mode = mode; p.w = w; p.w_dtype = w_dtype; p.x = x; p.x_dtype = x_dtype; p.x_ld = x_ld;
+  p.x_div = x_div > 0 ? x_div : 1;
   p.gsel = gsel; p.op_dtype = op_dtype; p.a_pad_start = g_pad_start; p.c_pad_start = out_pad_start;
   return run_row_gemm(p, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), "cvmm_backward_x");
 }

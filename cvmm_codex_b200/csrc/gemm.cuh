@@ -24,6 +24,7 @@ struct RowGemm {
   int mode;
   const void* w; int w_dtype;
   const void* x; int x_dtype; int64_t x_ld;
+  int64_t x_div;       // mode 1: route p's x row is c_index[p] / x_div (1, or the routes sharing one row)
   float* gsel;
   int op_dtype;
   const int4* tiles;   // (expert, first sorted position, rows, tile index) per M tile; with
@@ -33,7 +34,21 @@ struct RowGemm {
   const int* a_pad_start;  // non-null: A is the expert-padded sorted layout (row = pad_start[e] + p - seg_begin(e))
   const int* c_pad_start;  // non-null: C is the expert-padded sorted layout (16-bit, mode 0; c_index unused)
   const int* n_tiles;  // number of valid entries in `tiles`
+  int act;             // mode 0 only, 0 = none; 1 = GELU: c2[row] = op(acc) (the pre-activation, kept for
+  void* c2;            // the backward) and c[row] = cast(gelu(op(acc))), the up-projection + F.gelu of
+                       // the sigma-MoE layer in one epilogue (erf form, fp32 math on the rounded value)
 };
+
+// GELU of the reference's F.gelu (approximate = 'none'): 0.5 x (1 + erf(x / sqrt 2)),
+// evaluated in fp32 on an op-dtype value, in that operation order.
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+
+// d gelu / dx = Phi(x) + x phi(x), Phi the normal CDF, phi its density.
+__device__ __forceinline__ float gelu_erf_grad(float x) {
+  const float cdf = 0.5f * (1.0f + erff(x * 0.70710678118654752f));
+  const float pdf = expf(-0.5f * x * x) * 0.39894228040143268f;
+  return cdf + x * pdf;
+}
 
 // Per-expert segment reduction: grad-weight.
 //   out[e][m][n] = sum_{p in seg(e)} op(X[x_row(p)][m]) * G'_p[n]

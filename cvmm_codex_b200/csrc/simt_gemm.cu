@@ -232,10 +232,12 @@ __device__ __forceinline__ void store8(char* to, int dtype, const float (&v)[8])
 // op(scale[index[p]]), rounded again); rows [n_routes, n_routes + n_experts *
 // kPadRows) enumerate every expert's candidate padding rows, and those inside
 // the expert's padded segment are zeroed.
-// Each CTA owns 32 consecutive virtual rows: lane l of warp 0 resolves row
-// l's source, destination and scale (one round of index loads for all 32
-// rows, in parallel), then the CTA's 256 threads stream the rows' chunks
+// Each CTA owns ROWS consecutive virtual rows: thread r < ROWS resolves row
+// r's source, destination and scale (one round of dependent index loads for
+// all rows, in parallel), then the CTA's 256 threads stream the rows' chunks
 // with kSortBatch loads in flight per thread before converting and storing.
+// Short rows (<= 512 bytes) take 128 rows per CTA, so that the index round
+// is paid once per 32 KiB or more instead of once per 8 KiB.
 // MODE 0: 16-byte copy (same dtype, no scale), 1: 8-element vectors with
 // conversion (and scale), 2: scalar elements.
 constexpr int kSortBatch = 8;
@@ -247,18 +249,18 @@ struct SortRowMeta {
   int pad;
 };
 
-template <int MODE>
+template <int MODE, int ROWS>
 __global__ void __launch_bounds__(256) sort_rows_padded_kernel(
     const char* __restrict__ src, int src_dtype, int64_t src_ld, const int64_t* __restrict__ index, int64_t div,
     const void* __restrict__ scale, int scale_dtype, const int32_t* __restrict__ sorted_sel,
     const int64_t* __restrict__ offsets, const int* __restrict__ pad_start, int64_t n_routes, int64_t n_experts,
     int64_t cols, char* __restrict__ dst, int dst_dtype) {
-  __shared__ SortRowMeta meta[32];
+  __shared__ SortRowMeta meta[ROWS];
   const int tid = threadIdx.x, lane = tid & 31;
-  const int64_t v0 = blockIdx.x * (int64_t)32;
+  const int64_t v0 = blockIdx.x * (int64_t)ROWS;
   const int64_t total = n_routes + n_experts * kPadRows;
-  if (tid < 32) {
-    const int64_t v = v0 + lane;
+  if (tid < ROWS) {
+    const int64_t v = v0 + tid;
     SortRowMeta m = {-1, -1, 1.f, 0};
     if (v < n_routes) {
       const int64_t r = index[v];
@@ -271,12 +273,12 @@ __global__ void __launch_bounds__(256) sort_rows_padded_kernel(
       const int64_t cnt = offsets[e] - seg_begin(offsets, e);
       if (cnt + i < (cnt + kPadRows - 1) / kPadRows * kPadRows) m.dst = (pad_start[e] + cnt + i) * cols;
     }
-    meta[lane] = m;
+    meta[tid] = m;
   }
   __syncthreads();
   const int ssz = dtype_bytes(src_dtype), dsz = dtype_bytes(dst_dtype);
   if (MODE == 2) {
-    for (int rr = tid >> 5; rr < 32; rr += blockDim.x >> 5) {
+    for (int rr = tid >> 5; rr < ROWS; rr += blockDim.x >> 5) {
       const SortRowMeta m = meta[rr];
       if (m.dst < 0) continue;
       for (int64_t c = lane; c < cols; c += 32) {
@@ -289,7 +291,7 @@ __global__ void __launch_bounds__(256) sort_rows_padded_kernel(
   }
   // Work items: (row, 8-element chunk) pairs; MODE 0 moves 16-byte chunks.
   const int64_t per_row = MODE == 0 ? cols * dsz / 16 : cols / 8;
-  const int64_t items = 32 * per_row;
+  const int64_t items = ROWS * per_row;
   const uint32_t pr = (uint32_t)per_row;  // items < 2^32: 32-bit row / chunk split
   constexpr int kBatch = MODE == 0 ? kSortBatch : kSortBatch / 2;
   for (int64_t base = 0; base < items; base += (int64_t)blockDim.x * kBatch) {
@@ -352,21 +354,22 @@ int sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64
   const bool aligned = ((cols * ssz) % 16 == 0) && ((src_ld * ssz) % 16 == 0) && ((cols * dsz) % 16 == 0) &&
                        (((uintptr_t)src & 15u) == 0) && (((uintptr_t)dst & 15u) == 0) && cols % 8 == 0;
   const int64_t rows = n_routes + n_experts * kPadRows;
-  const unsigned grid = (unsigned)std::max<int64_t>((rows + 31) / 32, 1);
+  const int mode = (aligned && src_dtype == dst_dtype && scale == nullptr) ? 0 : (aligned ? 1 : 2);
+  const bool short_rows = mode != 2 && cols * std::max(ssz, dsz) <= 512;
+  const int64_t rpc = short_rows ? 128 : 32;  // rows per CTA
+  const unsigned grid = (unsigned)std::max<int64_t>((rows + rpc - 1) / rpc, 1);
   const char* s = static_cast<const char*>(src);
   char* d = static_cast<char*>(dst);
-  if (aligned && src_dtype == dst_dtype && scale == nullptr)
-    sort_rows_padded_kernel<0><<<grid, 256, 0, stream>>>(s, src_dtype, src_ld, index, div, scale, scale_dtype,
-                                                         sorted_sel, offsets, pad_start, n_routes, n_experts, cols, d,
-                                                         dst_dtype);
-  else if (aligned)
-    sort_rows_padded_kernel<1><<<grid, 256, 0, stream>>>(s, src_dtype, src_ld, index, div, scale, scale_dtype,
-                                                         sorted_sel, offsets, pad_start, n_routes, n_experts, cols, d,
-                                                         dst_dtype);
-  else
-    sort_rows_padded_kernel<2><<<grid, 256, 0, stream>>>(s, src_dtype, src_ld, index, div, scale, scale_dtype,
-                                                         sorted_sel, offsets, pad_start, n_routes, n_experts, cols, d,
-                                                         dst_dtype);
+#define CVMM_SORT_LAUNCH(MODE, ROWS)                                                                              \
+  sort_rows_padded_kernel<MODE, ROWS><<<grid, 256, 0, stream>>>(s, src_dtype, src_ld, index, div, scale,        \
+                                                                scale_dtype, sorted_sel, offsets, pad_start,      \
+                                                                n_routes, n_experts, cols, d, dst_dtype)
+  if (mode == 0 && short_rows) CVMM_SORT_LAUNCH(0, 128);
+  else if (mode == 0) CVMM_SORT_LAUNCH(0, 32);
+  else if (mode == 1 && short_rows) CVMM_SORT_LAUNCH(1, 128);
+  else if (mode == 1) CVMM_SORT_LAUNCH(1, 32);
+  else CVMM_SORT_LAUNCH(2, 32);
+#undef CVMM_SORT_LAUNCH
   return check_launch("sort_rows_padded");
 }
 
@@ -494,7 +497,7 @@ __global__ void __launch_bounds__(THREADS) row_gemm_kernel(RowGemm p) {
       } else {
         const float a = round_to(acc[i][j], p.op_dtype);
         store_from_float(p.c, p.c_dtype, c_row * p.c_ld + n, round_to(a * wv, p.op_dtype));
-        dot = fmaf(a, load_as_float(p.x, p.x_dtype, c_row * p.x_ld + n), dot);
+        dot = fmaf(a, load_as_float(p.x, p.x_dtype, idx_div(c_row, p.x_div) * p.x_ld + n), dot);
       }
     }
     if (p.mode == 1) {

@@ -98,6 +98,9 @@ constexpr uint32_t kStoreBox = 32 * 128;                  // one 32-row x 64-col
 // 32 rows of kStageRowBytes.
 constexpr uint32_t kStagingBytes = 8 * 32 * kStageRowBytes;
 static_assert(kStagingBytes >= 8 * kStoreBox, "staging too small");
+// BN = 256 tiles drained by two epilogue warp groups: two store boxes per warp (64 KiB).
+constexpr uint32_t staging_bytes(int bn) { return bn >= 256 ? 16 * kStoreBox : kStagingBytes; }
+static_assert(16 * kStoreBox >= kStagingBytes, "wide staging must also hold the row-transpose blocks");
 constexpr int kRingEntries = 72;
 constexpr int kPlanExperts = (int)kRowPlanExperts;  // experts up to which the row GEMM builds its tile table itself
 struct IdxSlot {
@@ -116,7 +119,7 @@ struct Smem {
   static constexpr uint32_t bars = S * stage_bytes;
   static constexpr uint32_t misc = bars + (5 * S + 5) * 8;  // tmem slot, abort flag
   static constexpr uint32_t staging = (misc + 16 + 1023) / 1024 * 1024;  // swizzled TMA store boxes
-  static constexpr uint32_t ring = staging + kStagingBytes;
+  static constexpr uint32_t ring = staging + staging_bytes(BN);
   // Row GEMM tile plan built in the kernel: first tile and segment start of
   // every expert (kPlanExperts + 1 entries each) and the scan's warp totals.
   static constexpr uint32_t plan = ring + S * (uint32_t)sizeof(IdxSlot);
@@ -389,7 +392,9 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_c, int flags,
                 int n_n) {
   static_assert(!A_TMA || B_TMA, "TMA row gathers are used together with TMA weight tiles");
-  static_assert(!EPI2 || (A_TMA && BN == 128), "two epilogue groups need dense TMA A tiles and BN = 128");
+  static_assert(!EPI2 || (A_TMA && (BN == 128 || BN == 256)), "two epilogue groups need dense TMA A tiles and BN >= 128");
+  // Store boxes per epilogue warp: two (alternating) unless the two groups share a 128-column tile.
+  constexpr int kBoxes = (EPI2 && BN == 128) ? 1 : 2;
   using L = Smem<BN, S>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_smem(smem_raw);
@@ -587,7 +592,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
     // Dense C (expert-padded sorted output): each 32-row x 64-column block is
     // written to a swizzled box of the warp and stored by TMA.
     const bool c_dense = flags & 128;
-    const uint32_t cbox = ptx::smem_u32(smem + L::staging) + (EPI2 ? warp * kStoreBox : ew * 2 * kStoreBox);
+    const uint32_t cbox = ptx::smem_u32(smem + L::staging) + (EPI2 ? warp : ew) * kBoxes * kStoreBox;
     int cbuf = 0;
     auto crow_of = [&](const int4& en) -> int64_t {
       return (c_dense || rr >= en.z) ? -1 : p.c_index[en.y + rr];
@@ -603,7 +608,8 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
     uint4 xr[8];
     auto load_x = [&](int64_t row, int64_t col0) {
       if (!x_vec || row < 0 || col0 + 64 > p.N) return;
-      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const char*>(p.x) + (row * p.x_ld + col0) * 2);
+      const uint4* src =
+          reinterpret_cast<const uint4*>(static_cast<const char*>(p.x) + (idx_div(row, p.x_div) * p.x_ld + col0) * 2);
 #pragma unroll
       for (int q = 0; q < 8; ++q) xr[q] = src[q];
     };
@@ -635,11 +641,11 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
           // The store issued earlier from this box must have read it (two
           // boxes per warp: the one before last; one box: the last).
           if (lane == 0) {
-            if (EPI2) ptx::bulk_wait_read<0>();
+            if (kBoxes == 1) ptx::bulk_wait_read<0>();
             else ptx::bulk_wait_read<1>();
           }
           __syncwarp();
-          const uint32_t box = cbox + (EPI2 ? 0u : cbuf * kStoreBox);
+          const uint32_t box = cbox + (kBoxes == 1 ? 0u : cbuf * kStoreBox);
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             uint32_t w4[4];
@@ -684,9 +690,18 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const float av = round_to(v[j], op);
-              if (j < ncols) dot = fmaf(av, load_as_float(p.x, p.x_dtype, crow * p.x_ld + nc + j), dot);
+              if (j < ncols) dot = fmaf(av, load_as_float(p.x, p.x_dtype, idx_div(crow, p.x_div) * p.x_ld + nc + j), dot);
               v[j] = round_to(av * wv, op);
             }
+          }
+          if (p.act == 1) {
+            // Pre-activation (rounded to the output dtype) to c2, GELU of it to c.
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = round_to(v[j], p.c_dtype);
+            if (!CVMM_DBG(flags, 16384))
+              warp_store_block(p.c2, p.c_dtype, row_ok ? crow * p.c_ld + nc : -1, v, ncols, stage, c_vec);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
           }
           if (!CVMM_DBG(flags, 16384))
             warp_store_block(p.c, p.c_dtype, row_ok ? crow * p.c_ld + nc : -1, v, ncols, stage, c_vec);
@@ -1239,8 +1254,8 @@ static int row_launch(const RowGemm& p, int64_t max_tiles, int flags, cudaStream
   }
   const int64_t work = max_tiles * n_n;
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(work, sm_count()));
-  if (a_dense && BN == 128 && !(dbg_flags() & 32768)) {
-    auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true, true, BN == 128>;
+  if (a_dense && BN >= 128 && !(dbg_flags() & 32768)) {
+    auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true, true, (BN >= 128)>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
     kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, cmap, flags, n_n);
@@ -1326,6 +1341,14 @@ int launch_row_gemm_umma(const RowGemm& p, int64_t max_tiles, cudaStream_t strea
   if (p.N <= 64) {
     return b_kmajor ? row_launch<64, 7, true>(p, max_tiles, flags, stream)
                     : row_launch<64, 7, false>(p, max_tiles, flags, stream);
+  }
+  // Dense A (expert-padded sorted rows) with a wide output: 128 x 256 tiles
+  // read each A tile half as often as 128 x 128 ones (grad-x of ff_up, the
+  // forward of ff_down: N = 1024), with both epilogue warp groups draining
+  // 128 columns each.
+  if (p.N >= 256 && p.a_pad_start && p.mode == 0 && (flags & 3) == 3) {
+    return b_kmajor ? row_launch<256, 3, true>(p, max_tiles, flags, stream)
+                    : row_launch<256, 3, false>(p, max_tiles, flags, stream);
   }
   return b_kmajor ? row_launch<128, 5, true>(p, max_tiles, flags, stream)
                   : row_launch<128, 5, false>(p, max_tiles, flags, stream);

@@ -17,9 +17,10 @@ from ._lib import check, dtype_code, ptr
 
 # Kernels each native entry point launches (for launch accounting).
 KERNELS_PER_CALL = {
-    "cvmm_sel_prepare": 10, "cvmm_expert_offsets": 1, "cvmm_forward": 2, "cvmm_backward_x": 2,
+    "cvmm_sel_prepare": 1, "cvmm_expert_offsets": 1, "cvmm_forward": 2, "cvmm_backward_x": 2,
     "cvmm_backward_w": 4, "cvmm_weighted_combine": 1, "cvmm_sum_routes": 1,
     "cvmm_weighted_token_backward": 1, "cvmm_cast": 1, "cvmm_sort_rows_padded": 2, "cvmm_pad_starts": 1,
+    "cvmm_forward_gelu": 1, "cvmm_gelu_backward": 1, "cvmm_router_topk": 1, "cvmm_padded_route_rows": 1,
 }
 
 
@@ -234,7 +235,7 @@ def backward_x(g: torch.Tensor, g_index: Optional[torch.Tensor], g_div: int, out
                offsets: torch.Tensor, keys: torch.Tensor, out_dtype: torch.dtype,
                op_dtype: torch.dtype, w: Optional[torch.Tensor] = None,
                x: Optional[torch.Tensor] = None, g_pad_start: Optional[torch.Tensor] = None,
-               out_pad_start: Optional[torch.Tensor] = None, n_routes: Optional[int] = None):
+               out_pad_start: Optional[torch.Tensor] = None, n_routes: Optional[int] = None, x_div: int = 1):
     """Route gradients a_p = g[g_index[p] // g_div] @ keys[e_p]^T stored at out_index[p].
 
     Plain (w is None): returns out [R, d_in]. Weighted route-shaped input (w and x
@@ -266,7 +267,7 @@ def backward_x(g: torch.Tensor, g_index: Optional[torch.Tensor], g_div: int, out
                                  keys.stride(2), ptr(out), dtype_code(out_dtype), out.stride(0), mode,
                                  ptr(w2), dtype_code(w2.dtype) if w2 is not None else 0,
                                  ptr(x2), dtype_code(x2.dtype) if x2 is not None else 0,
-                                 x2.stride(0) if x2 is not None else 0, ptr(gsel),
+                                 x2.stride(0) if x2 is not None else 0, int(x_div), ptr(gsel),
                                  dtype_code(op_dtype), ptr(g_pad_start), ptr(out_pad_start), ptr(ws), ws.numel(), stream,
                                  kernels=_row_gemm_launches(op_dtype, E))
     check(rc, "cvmm_backward_x")
@@ -395,3 +396,63 @@ def cast(src: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
         rc = _invoke("cvmm_cast", lib.cvmm_cast, ptr(s), dtype_code(s.dtype), ptr(out), dtype_code(dtype), s.numel(), stream)
     check(rc, "cvmm_cast")
     return out
+
+
+# ------------------------------------------------------------------ sigma-MoE layer pieces
+def forward_gelu(x: torch.Tensor, sel_index: torch.Tensor, offsets: torch.Tensor, keys: torch.Tensor,
+                 out_index: Optional[torch.Tensor], op_dtype: torch.dtype, x_copy: Optional[torch.Tensor] = None):
+    """Up projection with GELU fused into the epilogue: returns (h, z) [R, N]
+    with z = op(x[sel_index[p]] @ keys[e_p]) and h = gelu(z) (F.gelu, erf form)
+    at row out_index[p] (or sel_index[p]); x_copy as in forward()."""
+    _require_cuda(x, sel_index, offsets, keys, out_index)
+    lib = _lib.load()
+    x2 = _rows(x)
+    n_routes = sel_index.numel()
+    E, K, N = keys.shape
+    if x2.shape[1] != K:
+        raise ValueError(f"cvmm: x feature size {x2.shape[1]} != keys.shape[1] {K}")
+    h = torch.empty((n_routes, N), dtype=op_dtype, device=x.device)
+    z = torch.empty((n_routes, N), dtype=op_dtype, device=x.device)
+    ws = _gemm_ws(lib, n_routes, E, x.device)
+    with _Device(x.device) as stream:
+        rc = _invoke("cvmm_forward_gelu", lib.cvmm_forward_gelu, ptr(x2), dtype_code(x2.dtype), x2.shape[0],
+                     x2.stride(0), ptr(sel_index), ptr(out_index), ptr(offsets), n_routes,
+                     ptr(keys), dtype_code(keys.dtype), E, K, N, keys.stride(0), keys.stride(1), keys.stride(2),
+                     ptr(h), ptr(z), dtype_code(op_dtype), h.stride(0), dtype_code(op_dtype), ptr(x_copy),
+                     ptr(ws), ws.numel(), stream, kernels=_row_gemm_launches(op_dtype, E))
+    check(rc, "cvmm_forward_gelu")
+    return h, z
+
+
+def gelu_backward(grad: torch.Tensor, pre_act: torch.Tensor) -> torch.Tensor:
+    """grad * gelu'(pre_act), elementwise (16-bit tensors of one dtype)."""
+    _require_cuda(grad, pre_act)
+    lib = _lib.load()
+    g = grad.contiguous()
+    z = pre_act.contiguous()
+    if g.dtype != z.dtype:
+        g = g.to(z.dtype)
+    out = torch.empty_like(z)
+    with _Device(z.device) as stream:
+        rc = _invoke("cvmm_gelu_backward", lib.cvmm_gelu_backward, ptr(g), ptr(z), ptr(out), dtype_code(z.dtype),
+                     z.numel(), stream)
+    check(rc, "cvmm_gelu_backward")
+    return out
+
+
+def router_topk(logits: torch.Tensor, top_k: int, renormalize: bool = True):
+    """(weights fp32 [..., k], sel int64 [..., k]): top-k of softmax(float(logits))
+    in descending order, optionally renormalised to sum to one (the sigma-MoE
+    router, benchmark_ffn_moe.py:89-92)."""
+    _require_cuda(logits)
+    lib = _lib.load()
+    lg = logits.contiguous()
+    E = lg.shape[-1]
+    T = lg.numel() // E
+    sel = torch.empty((*lg.shape[:-1], int(top_k)), dtype=torch.int64, device=lg.device)
+    w = torch.empty((*lg.shape[:-1], int(top_k)), dtype=torch.float32, device=lg.device)
+    with _Device(lg.device) as stream:
+        rc = _invoke("cvmm_router_topk", lib.cvmm_router_topk, ptr(lg), dtype_code(lg.dtype), T, E, int(top_k),
+                     int(bool(renormalize)), ptr(sel), ptr(w), stream)
+    check(rc, "cvmm_router_topk")
+    return w, sel

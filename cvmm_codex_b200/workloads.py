@@ -34,6 +34,20 @@ class Workload:
     def R(self) -> int:
         return self.T * self.k
 
+    @property
+    def x_rows(self) -> int:
+        """Rows of x: tokens (token input), routes (route input), or token
+        heads when the routes of one head share its value row (SwitchHead)."""
+        if self.heads:
+            return self.T * self.heads
+        return self.R if self.route_input else self.T
+
+    def route_rows(self, x):
+        """x as one row per route (the layout the reference's API takes)."""
+        if self.heads:
+            return x.repeat_interleave(self.k // self.heads, dim=-2).reshape(self.R, -1)
+        return x.reshape(self.R, -1) if self.route_input else x.repeat_interleave(self.k, dim=0)
+
     def flops(self) -> int:
         """fw + grad-x + grad-W multiply-adds x2 (the headline FLOP count)."""
         return 3 * 2 * self.R * self.d_in * self.d_out
@@ -68,9 +82,9 @@ def make_inputs(w: Workload, device="cuda", seed: int = 0, token_slice: Optional
     T = w.T
     x_shape = (T, w.k, w.d_in) if w.route_input else (T, w.d_in)
     if w.skew == "heads":
-        # Per-head value rows, repeated for the head's 2 selected experts.
-        v = torch.randn(T, w.heads, w.d_in, generator=g, device=dev)
-        x = v.repeat_interleave(w.k // w.heads, dim=1)
+        # Per-head value rows [T, heads, d_head]; the 2 routes of a head read its
+        # row (no repeat_interleave copy: the kernels index row route // 2).
+        x = torch.randn(T, w.heads, w.d_in, generator=g, device=dev)
     else:
         x = torch.randn(*x_shape, generator=g, device=dev)
     keys = torch.randn(w.E, w.d_in, w.d_out, generator=g, device=dev) / math.sqrt(w.d_in)

@@ -52,7 +52,7 @@ typedef struct CUstream_st* cvmm_stream_t; /* == cudaStream_t */
 #define CVMM_DEV_BAD_INDEX 2
 
 /* ABI version of this header; bumped on any signature change. */
-int cvmm_abi_version(void);  /* 5 */
+int cvmm_abi_version(void);  /* 6 */
 
 /* Message for the last failed call on the calling host thread. */
 const char* cvmm_last_error(void);
@@ -138,6 +138,35 @@ int cvmm_forward(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld,
                  void* out, int out_dtype, int64_t out_ld, int op_dtype,
                  const int32_t* x_pad_start, const int32_t* out_pad_start, void* x_copy,
                  void* workspace, size_t workspace_bytes, cvmm_stream_t stream);
+
+/* Forward gathered GEMM with the sigma-MoE layer's activation fused into the
+ * epilogue: for every route, pre_act[row_p] = op(acc) and
+ * out[row_p] = gelu(op(acc)) = 0.5 z (1 + erf(z / sqrt 2)) in fp32 on the
+ * rounded z, rounded once more (both [n_routes, n_dim] with out_ld).
+ * Replaces cvmm(x, sel, w_up) followed by F.gelu in the reference's FFN layer
+ * (benchmark_ffn_moe.py:93-94): the activation pass over the route outputs
+ * disappears and pre_act is what the GELU backward reads. bf16/fp16 op_dtype
+ * and out_dtype == op_dtype; x_copy as in cvmm_forward. */
+int cvmm_forward_gelu(const void* x, int x_dtype, int64_t x_rows, int64_t x_ld,
+                      const int64_t* sel_index, const int64_t* out_index, const int64_t* offsets,
+                      int64_t n_routes, const void* keys, int keys_dtype, int64_t n_experts,
+                      int64_t k_dim, int64_t n_dim, int64_t ks_e, int64_t ks_k, int64_t ks_n,
+                      void* out, void* pre_act, int out_dtype, int64_t out_ld, int op_dtype,
+                      void* x_copy, void* workspace, size_t workspace_bytes, cvmm_stream_t stream);
+
+/* grad_pre_act[i] = grad[i] * gelu'(pre_act[i]) in fp32, rounded to dtype
+ * (bf16/fp16); the backward of F.gelu (torch's GeluBackward, erf form). */
+int cvmm_gelu_backward(const void* grad, const void* pre_act, void* grad_pre_act, int dtype, int64_t n,
+                       cvmm_stream_t stream);
+
+/* Router of the sigma-MoE layer (benchmark_ffn_moe.py:89-92) in one launch:
+ * probs = softmax(float(logits)) over n_experts (<= 1024);
+ * (weights, sel) = top_k(probs) in descending order (ties: lower expert id);
+ * weights /= max(sum(weights), 1e-20) when renormalize != 0.
+ * logits: [n_tokens, n_experts] fp32/bf16/fp16; sel: int64 [n_tokens, top_k];
+ * weights: fp32 [n_tokens, top_k]; 1 <= top_k <= 32. */
+int cvmm_router_topk(const void* logits, int logits_dtype, int64_t n_tokens, int64_t n_experts, int64_t top_k,
+                     int renormalize, int64_t* sel, float* weights, cvmm_stream_t stream);
 /* With x_pad_start != NULL, x is the expert-padded sorted layout made by
  * cvmm_sort_rows_padded: the x row of sorted position p is then
  * x_pad_start[e] + p - seg_begin(e), x_rows is ignored, and sel_index only
@@ -177,7 +206,9 @@ int cvmm_weighted_combine(const void* y, int y_dtype, const void* w, int w_dtype
  *   mode 0: out[out_index[p]] = cast_out(a_p)
  *   mode 1 (weighted, route-shaped x):
  *           out[out_index[p]]  = cast_out( op(op(a_p) * op(w[out_index[p]])) )
- *           gsel[out_index[p]] += sum_j op(a_p)_j * x[out_index[p]]_j   (fp32)
+ *           gsel[out_index[p]] += sum_j op(a_p)_j * x[out_index[p] / x_div]_j   (fp32)
+ *           (x_div = 1 for route-shaped x; x_div = r when r consecutive routes
+ *           share one x row, e.g. the 2 routes of one SwitchHead head)
  * keys strides are those of keys[e][k_dim][n_dim] as in cvmm_forward; the
  * product contracts over n_dim and produces k_dim columns.
  * gsel must be zeroed by the caller (mode 1 accumulates into it).
@@ -187,9 +218,10 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
                     int64_t n_routes, const void* keys, int keys_dtype, int64_t n_experts,
                     int64_t k_dim, int64_t n_dim, int64_t ks_e, int64_t ks_k, int64_t ks_n,
                     void* out, int out_dtype, int64_t out_ld, int mode, const void* w,
-                    int w_dtype, const void* x, int x_dtype, int64_t x_ld, float* gsel,
-                    int op_dtype, const int32_t* g_pad_start, const int32_t* out_pad_start,
-                    void* workspace, size_t workspace_bytes, cvmm_stream_t stream);
+                    int w_dtype, const void* x, int x_dtype, int64_t x_ld, int64_t x_div,
+                    float* gsel, int op_dtype, const int32_t* g_pad_start,
+                    const int32_t* out_pad_start, void* workspace, size_t workspace_bytes,
+                    cvmm_stream_t stream);
 /* out_pad_start != NULL (mode 0 only): out is written in the expert-padded
  * sorted layout as in cvmm_forward, out_index is ignored. */
 

@@ -30,7 +30,7 @@ def step(w, d):
     order = torch.sort(flat.to(torch.int32), stable=True)
     idx = order.indices
     counts = torch.bincount(flat, minlength=w.E)
-    rows = x.reshape(R, -1) if w.route_input else x.repeat_interleave(w.k, dim=0)
+    rows = w.route_rows(x)
     y = torch.empty(R, w.d_out)
     gk = torch.zeros_like(keys)
     gr = torch.empty(R, w.d_in)
@@ -56,5 +56,8 @@ def step(w, d):
         gw = (g.repeat_interleave(w.k, dim=0) * y).sum(-1).view(T, w.k)
     else:
         out, gw = y.view(T, w.k, -1), None
-    gx = gr.view(x.shape) if w.route_input else gr.view(T, w.k, -1).sum(1)
+    if w.heads:
+        gx = gr.view(T, w.heads, w.k // w.heads, -1).sum(2)
+    else:
+        gx = gr.view(x.shape) if w.route_input else gr.view(T, w.k, -1).sum(1)
     return out, gx, gk, gw

@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(lib, name), name
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
     assert set(_lib.SIGNATURES) == set(declared_functions())
-    assert lib.cvmm_abi_version() == 5
+    assert lib.cvmm_abi_version() == 6
 
 
 def test_workspace_queries_need_no_device():
@@ -45,7 +45,7 @@ def test_workspace_queries_need_no_device():
     (lambda l: l.cvmm_forward(None, 2, 10, 4, None, None, None, 5, None, 0, 0, 4, 4, 0, 0, 0, None, 2, 4, 2, None, None, None, None, 0, None), -1),
     (lambda l: l.cvmm_sel_prepare(None, 0, 4, 1, 0, None, None, None, None, None, 0, None), -2),
     (lambda l: l.cvmm_sel_prepare(None, 4, 4, 0, 0, None, None, None, None, None, 0, None), -1),
-    (lambda l: l.cvmm_backward_x(None, 2, 4, None, 1, None, None, 4, None, 2, 1, 4, 4, 0, 0, 0, None, 2, 4, 3, None, 0, None, 0, 0, None, 2, None, None, None, 0, None), -1),
+    (lambda l: l.cvmm_backward_x(None, 2, 4, None, 1, None, None, 4, None, 2, 1, 4, 4, 0, 0, 0, None, 2, 4, 3, None, 0, None, 0, 0, 1, None, 2, None, None, None, 0, None), -1),
     (lambda l: l.cvmm_backward_w(None, 2, 4, None, 0, None, 2, 4, None, 1, None, 0, None, None, 4, 1, 4, 4, None, 2, None, None, None, 0, None), -1),
     (lambda l: l.cvmm_sort_rows_padded(None, 2, 4, None, 1, None, 0, None, None, 4, 2, 8, None, 2, None, None), -1),
     # padded sorted x needs a 16-bit op dtype; a padded g already carries the route weights
@@ -53,7 +53,14 @@ def test_workspace_queries_need_no_device():
     (lambda l: l.cvmm_backward_w(16, 2, 8, None, 1, 16, 2, 8, None, 1, 16, 0, 16, 16, 4, 1, 8, 8, 16, 2, 16, 16, None, 0, None), -1),
     # padded sorted outputs: only for 16-bit arithmetic, mode 0
     (lambda l: l.cvmm_forward(16, 0, 4, 8, 16, None, 16, 4, 16, 0, 1, 8, 8, 64, 8, 1, 16, 0, 8, 0, None, 16, None, None, 0, None), -1),
-    (lambda l: l.cvmm_backward_x(16, 2, 8, None, 1, None, 16, 4, 16, 2, 1, 8, 8, 64, 8, 1, 16, 2, 8, 1, 16, 0, 16, 2, 8, 16, 2, 16, 16, None, 0, None), -1),
+    (lambda l: l.cvmm_backward_x(16, 2, 8, None, 1, None, 16, 4, 16, 2, 1, 8, 8, 64, 8, 1, 16, 2, 8, 1, 16, 0, 16, 2, 8, 1, 16, 2, 16, 16, None, 0, None), -1),
+    # mode 1 needs a positive x_div (routes per x row)
+    (lambda l: l.cvmm_backward_x(16, 2, 8, 16, 1, 16, 16, 4, 16, 2, 1, 8, 8, 64, 8, 1, 16, 2, 8, 1, 16, 0, 16, 2, 8, 0, 16, 2, None, None, None, 0, None), -1),
+    # the fused GELU forward needs 16-bit arithmetic; router top_k in [1, 32], gelu backward 16-bit
+    (lambda l: l.cvmm_forward_gelu(16, 0, 4, 8, 16, None, 16, 4, 16, 0, 1, 8, 8, 64, 8, 1, 16, 16, 0, 8, 0, None, None, 0, None), -1),
+    (lambda l: l.cvmm_router_topk(16, 0, 4, 8, 33, 1, 16, 16, None), -1),
+    (lambda l: l.cvmm_router_topk(16, 3, 4, 8, 2, 1, 16, 16, None), -2),
+    (lambda l: l.cvmm_gelu_backward(16, 16, 16, 0, 4, None), -2),
     (lambda l: l.cvmm_padded_route_rows(None, None, None, None, 4, 2, None, None), -1),
     (lambda l: l.cvmm_selftest_wait_timeout(0, None), -1),
     # x_copy needs 16-bit arithmetic and a row-indexed x

@@ -37,7 +37,7 @@ def run(w, d, scale=1.0):
 
 
 def route_rows(w, t):
-    return t.reshape(w.R, -1) if w.route_input else t.repeat_interleave(w.k, dim=0)
+    return w.route_rows(t)
 
 
 def fp64_reference(w, d):
@@ -71,7 +71,10 @@ def fp64_reference(w, d):
     else:
         out = y.view(w.T, w.k, -1)
         gw = None
-    gx = grows.view(d["x"].shape) if w.route_input else grows.view(w.T, w.k, -1).sum(1)
+    if w.heads:
+        gx = grows.view(w.T, w.heads, w.k // w.heads, -1).sum(2)
+    else:
+        gx = grows.view(d["x"].shape) if w.route_input else grows.view(w.T, w.k, -1).sum(1)
     return out, gx, gk, gw
 
 

@@ -225,3 +225,38 @@ def test_many_experts_tile_table_paths(n_experts, weighted):
     grad = torch.randn(*((T, d_out) if weighted else (T, k, d_out)), generator=g)
     out, gx, gk, gw = run_case(x.bfloat16(), keys, sel, w, grad, False, torch.bfloat16)
     check_oracle(out, gx, gk, gw, x.bfloat16(), keys, sel, w, grad, "bfloat16")
+
+
+@pytest.mark.parametrize("weighted", [True, False])
+def test_shared_head_rows_match_repeated_route_rows(weighted):
+    """SwitchHead output projection: the 2 routes of each head read the head's
+    value row. Passing the per-head rows [T, H, d] (the kernels index row
+    route // 2) gives the same results as the reference's layout, the rows
+    repeated per route with repeat_interleave [T, 2H, d]."""
+    g = torch.Generator().manual_seed(21)
+    T, H, rph, per, d, n = 400, 6, 2, 4, 64, 96
+    E = H * per
+    v = torch.randn(T, H, d, generator=g).bfloat16()
+    keys = torch.randn(E, d, n, generator=g) / 8
+    logits = torch.randn(T, H, per, generator=g)
+    sel = (logits.topk(rph, dim=-1).indices + (torch.arange(H) * per).view(1, -1, 1)).reshape(T, H * rph)
+    w = torch.rand(T, H * rph, generator=g) if weighted else None
+    grad = torch.randn(*((T, n) if weighted else (T, H * rph, n)), generator=g)
+    shared = run_case(v, keys, sel, w, grad, True, torch.bfloat16)
+    vr = v.cuda().requires_grad_(True)
+    rep = vr.repeat_interleave(rph, dim=1)
+    kc = keys.cuda().requires_grad_(True)
+    wc = None if w is None else w.cuda().requires_grad_(True)
+    s2 = cvmm_prepare_sel2(sel.cuda(), wc, route_input=True)
+    with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+        out = cvmm(rep, s2, kc)
+    out.backward(grad.cuda().to(out.dtype))
+    repeated = (out, vr.grad, kc.grad, None if wc is None else wc.grad)
+    for name, a, b in zip(("out", "x_grad", "keys_grad", "w_grad"), shared, repeated):
+        if a is None:
+            assert b is None
+            continue
+        assert a.shape == b.shape, name
+        torch.testing.assert_close(a.float(), b.float(), rtol=1e-2, atol=1e-2 * b.float().abs().max().item())
+        if name != "x_grad":
+            assert torch.equal(a, b), name
