@@ -376,6 +376,13 @@ def run_ep(args, rank, world, local_rank):
     }
 
 
+def workload_config(w, world):
+    """The workload keys of the JSON line, identical in both arms."""
+    return {"workload": w.name, "tokens_per_gpu": w.T, "d_in": w.d_in, "d_out": w.d_out, "experts": w.E,
+            "top_k": w.k, "weighted": w.weighted, "route_input": w.route_input, "global_tokens": w.T * world,
+            "parallelism": f"token-sharded dp{world}", "flops_per_step_per_gpu": w.flops()}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
 
@@ -465,15 +472,12 @@ def run_ours(args, rank, world, local_rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(main["ms"], 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if w.amp else "f32",
         "data": "synthetic (seeded; shapes of the BASELINE config, inputs generated on device)",
-        "config": {"workload": w.name, "tokens_per_gpu": w.T, "d_in": w.d_in, "d_out": w.d_out,
-                   "experts": w.E, "top_k": w.k, "weighted": w.weighted, "route_input": w.route_input,
-                   "global_tokens": w.T * world, "parallelism": f"token-sharded dp{world}",
-                   "grad_w_allreduce": None if world == 1 else ("after backward" if args.serial_allreduce
+        "config": dict(workload_config(w, world),
+                       grad_w_allreduce=None if world == 1 else ("after backward" if args.serial_allreduce
                                                                  else "overlapped with grad-x"),
-                   "l2": "flushed (256 MiB write) before every timed step",
-                   "cuda_graph": main["graphed"],
-                   "flops_per_step_per_gpu": w.flops(),
-                   "pct_bf16_peak_sustained": round(100 * main["tflops"] / world / pk["bf16_tflops_sustained"], 2)},
+                       l2="flushed (256 MiB write) before every timed step",
+                       cuda_graph=main["graphed"],
+                       pct_bf16_peak_sustained=round(100 * main["tflops"] / world / pk["bf16_tflops_sustained"], 2)),
         "clocks": main["clocks"],
         "gpu_launches": main["launches"] * args.steps,
         "roofline": main["roofline"],
@@ -769,8 +773,7 @@ def run_reference(args, rank):
         "metric": METRIC, "value": round(tf, 5), "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": reps,
         "warmup": args.warmup, "ms_per_step": round(best * 1e3, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, same recipe as our arm)",
-        "config": {"workload": w.name, "tokens_per_gpu": w.T, "tokens_timed": n_tok, "d_in": w.d_in,
-                   "d_out": w.d_out, "experts": w.E, "top_k": w.k, "parallelism": "host CPU"},
+        "config": dict(workload_config(w, args.gpus), tokens_timed=n_tok, host="CPU, all host cores"),
         "impl": "reference",
         "cpu_baseline": {"value": round(tf, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
                          "sample": sample},
