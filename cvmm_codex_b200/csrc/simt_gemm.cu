@@ -239,7 +239,8 @@ __device__ __forceinline__ void store8(char* to, int dtype, const float (&v)[8])
 // Short rows (<= 512 bytes) take 128 rows per CTA, so that the index round
 // is paid once per 32 KiB or more instead of once per 8 KiB.
 // MODE 0: 16-byte copy (same dtype, no scale), 1: 8-element vectors with
-// conversion (and scale), 2: scalar elements.
+// conversion (and scale), 2: scalar elements, 3: 16-byte chunks of one 16-bit
+// dtype with the scale applied in registers (the weighted grad copy).
 constexpr int kSortBatch = 8;
 
 struct SortRowMeta {
@@ -289,13 +290,40 @@ __global__ void __launch_bounds__(256) sort_rows_padded_kernel(
     }
     return;
   }
-  // Work items: (row, 8-element chunk) pairs; MODE 0 moves 16-byte chunks.
-  const int64_t per_row = MODE == 0 ? cols * dsz / 16 : cols / 8;
+  // Work items: (row, 8-element chunk) pairs; MODE 0 / 3 move 16-byte chunks.
+  const int64_t per_row = (MODE == 0 || MODE == 3) ? cols * dsz / 16 : cols / 8;
   const int64_t items = ROWS * per_row;
   const uint32_t pr = (uint32_t)per_row;  // items < 2^32: 32-bit row / chunk split
-  constexpr int kBatch = MODE == 0 ? kSortBatch : kSortBatch / 2;
+  constexpr int kBatch = (MODE == 0 || MODE == 3) ? kSortBatch : kSortBatch / 2;
   for (int64_t base = 0; base < items; base += (int64_t)blockDim.x * kBatch) {
-    if (MODE == 0) {
+    if (MODE == 3) {
+      // Same 16-bit dtype in and out, scaled: 16-byte loads, the 8 values
+      // times the op-rounded route weight in fp32, rounded once (as MODE 1).
+      uint4 buf[kSortBatch];
+#pragma unroll
+      for (int u = 0; u < kSortBatch; ++u) {
+        const int64_t it = base + tid + (int64_t)blockDim.x * u;
+        buf[u] = make_uint4(0, 0, 0, 0);
+        if (it < items) {
+          const SortRowMeta& m = meta[(uint32_t)it / pr];
+          if (m.dst >= 0 && m.src >= 0)
+            buf[u] = reinterpret_cast<const uint4*>(src + m.src * ssz)[(uint32_t)it % pr];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kSortBatch; ++u) {
+        const int64_t it = base + tid + (int64_t)blockDim.x * u;
+        if (it >= items) continue;
+        const SortRowMeta& m = meta[(uint32_t)it / pr];
+        if (m.dst < 0) continue;
+        uint32_t w[4] = {buf[u].x, buf[u].y, buf[u].z, buf[u].w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h)
+          w[h] = pack2(bits_to_float((uint16_t)(w[h] & 0xffffu), dst_dtype) * m.scale,
+                       bits_to_float((uint16_t)(w[h] >> 16), dst_dtype) * m.scale, dst_dtype);
+        reinterpret_cast<uint4*>(dst + m.dst * dsz)[(uint32_t)it % pr] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else if (MODE == 0) {
       uint4 buf[kSortBatch];
 #pragma unroll
       for (int u = 0; u < kSortBatch; ++u) {
@@ -354,7 +382,8 @@ int sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64
   const bool aligned = ((cols * ssz) % 16 == 0) && ((src_ld * ssz) % 16 == 0) && ((cols * dsz) % 16 == 0) &&
                        (((uintptr_t)src & 15u) == 0) && (((uintptr_t)dst & 15u) == 0) && cols % 8 == 0;
   const int64_t rows = n_routes + n_experts * kPadRows;
-  const int mode = (aligned && src_dtype == dst_dtype && scale == nullptr) ? 0 : (aligned ? 1 : 2);
+  const bool same16 = src_dtype == dst_dtype && dst_dtype != F32;
+  const int mode = !aligned ? 2 : (src_dtype == dst_dtype && scale == nullptr ? 0 : (same16 ? 3 : 1));
   const bool short_rows = mode != 2 && cols * std::max(ssz, dsz) <= 512;
   const int64_t rpc = short_rows ? 128 : 32;  // rows per CTA
   const unsigned grid = (unsigned)std::max<int64_t>((rows + rpc - 1) / rpc, 1);
@@ -366,6 +395,8 @@ int sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64
                                                                 n_routes, n_experts, cols, d, dst_dtype)
   if (mode == 0 && short_rows) CVMM_SORT_LAUNCH(0, 128);
   else if (mode == 0) CVMM_SORT_LAUNCH(0, 32);
+  else if (mode == 3 && short_rows) CVMM_SORT_LAUNCH(3, 128);
+  else if (mode == 3) CVMM_SORT_LAUNCH(3, 32);
   else if (mode == 1 && short_rows) CVMM_SORT_LAUNCH(1, 128);
   else if (mode == 1) CVMM_SORT_LAUNCH(1, 32);
   else CVMM_SORT_LAUNCH(2, 32);
