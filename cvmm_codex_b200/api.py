@@ -126,6 +126,11 @@ cvmm_weighted_grad_copy = os.environ.get("CVMM_B200_WEIGHTED_GRAD_COPY", "1").lo
 # work, and backward_done just before it returns, so a caller can reduce the
 # weight gradient across ranks while grad-x runs (dist.OverlappedGradReduce).
 cvmm_backward_hook = None
+# sm_100a engine knob: the weighted backward makes ONE unscaled expert-padded
+# sorted copy of the token grads that both grad-W (weights applied in shared
+# memory) and grad-x read as dense tiles (True), instead of the per-GEMM
+# variants selected by cvmm_weighted_grad_copy. Bit-identical results.
+cvmm_weighted_shared_grad_copy = os.environ.get("CVMM_B200_WEIGHTED_SHARED_GRAD", "1").lower() not in ("0", "false", "no", "off")
 # Opt-in host check of the device status word after every CVMM forward and
 # backward (synchronises the stream): raises RuntimeError when a kernel gave up
 # on a bounded wait or met an out-of-range expert id.
@@ -333,14 +338,22 @@ def _cvmm_backward(ctx, saved, grad_output):
     else:
         k = w.shape[-1]
         gt = g.reshape(-1, g.shape[-1])  # token grads of the combined output
+        gs = gpad = None
         if need_keys:
             # dW_e = sum_p x[sel_index[p]]^T (bf16(w_p) * g[route_p // k])  (cvmm.py:1341-1383)
-            if xs is not None and _sortable(gt, op) and cvmm_weighted_grad_copy:
+            if xs is not None and _sortable(gt, op) and cvmm_weighted_shared_grad_copy:
+                # One unscaled expert-padded sorted copy of the token grads feeds
+                # both GEMMs as dense TMA boxes: grad-W applies op(op(g) op(w))
+                # in shared memory (cvmm.py:591-599), grad-x reads it as A.
+                gs, gpad = ops.sort_rows_padded(gt, route, k, sel, offsets, n_experts, dtype=op)
+                grad_keys = ops.backward_w(xs, None, 1, gs, None, 1, offsets, n_experts, op, w=w,
+                                           w_index=route, g_pad_start=gpad, x_pad_start=xpad, n_routes=n_routes)
+            elif xs is not None and _sortable(gt, op) and cvmm_weighted_grad_copy:
                 # The weight product is applied (and rounded) in a sorted copy.
                 gs, gpad = ops.sort_rows_padded(gt, route, k, sel, offsets, n_experts, dtype=op, scale=w)
                 grad_keys = ops.backward_w(xs, None, 1, gs, None, 1, offsets, n_experts, op,
                                            g_pad_start=gpad, x_pad_start=xpad, n_routes=n_routes)
-                del gs
+                gs = None  # weight-scaled: not the operand grad-x needs
             elif xs is not None:
                 # Token grad rows gathered straight from g (L2-resident) and
                 # scaled by op(w) in shared memory (cvmm.py:591-599): no
@@ -353,23 +366,30 @@ def _cvmm_backward(ctx, saved, grad_output):
         if grad_keys is not None and cvmm_backward_hook is not None and ctx.keys_type == torch.float32:
             cvmm_backward_hook.grad_keys_ready(grad_keys)
         if need_x or need_w:
+            if gs is not None:
+                # grad-x / sel-weight grad from the same unscaled sorted copy
+                # (dense A tiles instead of gathered token rows).
+                ga, gia, gk, gpd = gs, None, 1, gpad
+            else:
+                ga, gia, gk, gpd = gt, route, k, None
             if out_index is None and rph > 1:
                 # Route-indexed selector over shared x rows (SwitchHead heads):
                 # the fused route grad-x + sel-weight grad reads x row p / rph,
                 # then each row sums its rph route grads.
-                gx, gsel = ops.backward_x(gt, route, k, route, offsets, keys_op, x.dtype, op, w=w, x=x,
-                                          x_div=rph)
+                gx, gsel = ops.backward_x(ga, gia, gk, route, offsets, keys_op, x.dtype, op, w=w, x=x,
+                                          x_div=rph, g_pad_start=gpd, n_routes=n_routes)
                 grad_x = ops.sum_routes(gx, rph, x.dtype).view_as(x) if need_x else None
                 grad_w = gsel.view_as(w).to(w.dtype) if need_w else None
             elif out_index is None and tuple(x.shape[:-1]) == tuple(w.shape):
                 # Route-shaped input: fused grad-x + sel-weight grad (cvmm.py:1386-1433)
-                gx, gsel = ops.backward_x(gt, route, k, route, offsets, keys_op, x.dtype, op,
-                                          w=w, x=x)
+                gx, gsel = ops.backward_x(ga, gia, gk, route, offsets, keys_op, x.dtype, op,
+                                          w=w, x=x, g_pad_start=gpd, n_routes=n_routes)
                 grad_x = gx.view_as(x) if need_x else None
                 grad_w = gsel.view_as(w).to(w.dtype) if need_w else None
             else:
                 # Token-shaped input: route grads, then weighted token sums (cvmm.py:1726-1750)
-                rg = ops.backward_x(gt, route, k, route, offsets, keys_op, op, op)
+                rg = ops.backward_x(ga, gia, gk, route, offsets, keys_op, op, op, g_pad_start=gpd,
+                                    n_routes=n_routes)
                 gx, gsel = ops.weighted_token_backward(rg, w, x, need_x, need_w, x.dtype)
                 grad_x = gx.view_as(x) if need_x else None
                 grad_w = gsel.view_as(w).to(w.dtype) if need_w else None

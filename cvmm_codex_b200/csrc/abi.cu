@@ -36,7 +36,7 @@ int check_launch(const char* where) {
 // consecutive columns of one token; VEC: 16-bit rows read and written with
 // 16-byte accesses, up to kCombineBatch route rows in flight per thread.
 // Routes are added in ascending j (the reference's sum / bmm order).
-constexpr int kCombineBatch = 8;
+constexpr int kCombineBatch = 4;
 
 template <bool VEC>
 __global__ void __launch_bounds__(256) combine_kernel(const void* __restrict__ src, int s_dtype,
@@ -678,8 +678,6 @@ int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_i
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: null pointer");
   if ((g_pad_start && (op_dtype == F32 || g_dtype != op_dtype)) || (x_pad_start && (op_dtype == F32 || x_dtype != op_dtype)))
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: padded sorted operands need operand dtype == op_dtype (bf16/fp16)");
-  if (g_pad_start && w)
-    return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: a padded g carries the route weights; pass w = NULL");
   if (n_experts > 65535) return fail(CVMM_ERR_INVALID_ARG, "cvmm_backward_w: too many experts");
   const bool tensor = op_dtype != F32;
   GemmWs ws;
@@ -701,7 +699,7 @@ int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_i
   if (rc) return rc;
   // Both operands padded: the GEMM derives every row from its unit and needs
   // no resolved route rows.
-  if (tensor && n_routes > 0 && !(x_pad_start && g_pad_start)) {
+  if (tensor && n_routes > 0 && (!(x_pad_start && g_pad_start) || w)) {
     char* rr = reinterpret_cast<char*>(ws.partials) +
                align_up((size_t)segw_max_slots(n_routes, p.chunk) * m_dim * n_dim * sizeof(float), 256);
     const size_t arr = align_up((size_t)(n_routes + kRouteRowsPad) * 4, 256);

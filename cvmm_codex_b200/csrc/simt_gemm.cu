@@ -178,23 +178,28 @@ int resolve_route_rows(const SegGemm& p, int* xrow, int* grow, float* wsc, cudaS
 }
 
 // pad_start[e] = sum over e' < e of round_up(count(e'), pad): one CTA scan.
-__global__ void __launch_bounds__(1024)
+// Counts and pad starts are below 2^31 (checked by the callers): 32-bit math.
+__global__ void __launch_bounds__(512)
 pad_starts_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int64_t pad, int* __restrict__ pad_start) {
   __shared__ int warp_tot[32];
-  const int t = threadIdx.x;
-  const int64_t per = (n_experts + blockDim.x - 1) / blockDim.x;
-  const int64_t e0 = min((int64_t)t * per, n_experts), e1 = min(e0 + per, n_experts);
+  const int t = threadIdx.x, n = (int)n_experts, pd = (int)pad;
+  const int per = (n + (int)blockDim.x - 1) / (int)blockDim.x;
+  const int e0 = min(t * per, n), e1 = min(e0 + per, n);
+  auto padded = [&](int e) {
+    const int c = (int)(offsets[e] - (e > 0 ? offsets[e - 1] : 0));
+    return (c + pd - 1) / pd * pd;
+  };
   int tot = 0;
-  for (int64_t e = e0; e < e1; ++e) tot += (int)((offsets[e] - seg_begin(offsets, e) + pad - 1) / pad * pad);
+  for (int e = e0; e < e1; ++e) tot += padded(e);
   int run = block_exclusive_scan(tot, warp_tot);
-  for (int64_t e = e0; e < e1; ++e) {
+  for (int e = e0; e < e1; ++e) {
     pad_start[e] = run;
-    run += (int)((offsets[e] - seg_begin(offsets, e) + pad - 1) / pad * pad);
+    run += padded(e);
   }
 }
 
 int pad_starts(const int64_t* offsets, int64_t n_experts, int64_t pad, int* pad_start, cudaStream_t stream) {
-  pad_starts_kernel<<<1, 1024, 0, stream>>>(offsets, n_experts, pad, pad_start);
+  pad_starts_kernel<<<1, 512, 0, stream>>>(offsets, n_experts, pad, pad_start);
   return check_launch("pad_starts");
 }
 

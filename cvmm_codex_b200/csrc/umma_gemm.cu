@@ -386,7 +386,9 @@ __device__ __forceinline__ void mma_loop(const Bars& b, uint64_t* consume, uint8
 // columns 0-63, warps 0-3 columns 64-127 (warp w reaches TMEM lanes
 // 32*(w%4)..+31), which halves the per-tile epilogue time that otherwise
 // bounds the short-K shapes.
-template <int BN, int S, bool B_KMAJOR, bool B_TMA, bool A_TMA, bool EPI2 = false>
+// ACT: the GELU epilogue (RowGemm::act), compiled only into the variants that
+// use it, so the other variants keep their register allocation.
+template <int BN, int S, bool B_KMAJOR, bool B_TMA, bool A_TMA, bool EPI2 = false, bool ACT = false>
 __global__ void __launch_bounds__(kThreads, 1)
 row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
                 const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_c, int flags,
@@ -626,12 +628,22 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
       float wv = 0.f, dot = 0.f;
       if (p.mode == 1 && row_ok) wv = round_to(load_as_float(p.w, p.w_dtype, crow), op);
       const int prow0 = (int)kPadRows * ent.w + ew * 32;  // dense C: this warp's first padded row
+      // The accumulator is handed back to the MMA warp as soon as this warp
+      // has read its last columns out of TMEM, before converting and storing
+      // them, so the next-but-one tile's MMAs start one chunk earlier.
+      const int ch_end = min(c_hi / 64, (int)((p.N - n0 + 63) / 64));
+      bool released = false;
       for (int ch = c_lo / 64; ch < c_hi / 64; ++ch) {
         if (n0 + ch * 64 >= p.N) break;
         if (ch > c_lo / 64) load_x(crow, n0 + ch * 64);
         const bool xv_ok = x_vec && n0 + ch * 64 + 64 <= p.N;
         float v2[64];
         load_acc64(tmem + ((uint32_t)(ew * 32) << 16) + a * BN + ch * 64, v2);
+        if (ch == ch_end - 1) {
+          ptx::tc_fence_before();
+          ptx::mbar_arrive(&bar.acce[a]);
+          released = true;
+        }
         if (stamper && ch == 0) CVMM_STAMP(4, local);
         if (c_dense) {
           if (nkb == 0) {
@@ -694,7 +706,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
               v[j] = round_to(av * wv, op);
             }
           }
-          if (p.act == 1) {
+          if (ACT) {
             // Pre-activation (rounded to the output dtype) to c2, GELU of it to c.
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = round_to(v[j], p.c_dtype);
@@ -708,8 +720,10 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
         }
       }
       if (p.mode == 1 && row_ok) atomicAdd(p.gsel + crow, dot);
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(&bar.acce[a]);
+      if (!released) {
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(&bar.acce[a]);
+      }
       if (stamper) CVMM_STAMP(3, local);
       ent = ent_next;
       ent_next = ent_after;
@@ -883,7 +897,9 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
     // 4 rows per gather4, into the MN-major swizzled stages (route = k row).
     uint32_t it = 0;
     bool aborted = false;
-    const bool g_dense = flags & 32, x_dense = flags & 64, ring_on = !(g_dense && x_dense);
+    // The index ring carries the route weights of a weighted grad-W even when
+    // both operands are dense boxes.
+    const bool g_dense = flags & 32, x_dense = flags & 64, ring_on = WEIGHTED || !(g_dense && x_dense);
     for (int tt = blockIdx.x; tt < total && !aborted; tt += gridDim.x) {
       const int4 u = entry(tt);
       const int rem = tt % per_unit;
@@ -1109,7 +1125,7 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
     // ------------------------------------------------------------ index warp
     // (idle when both operands are dense: their rows follow from the unit)
     uint32_t it = 0;
-    bool aborted = (flags & 96) == 96;
+    bool aborted = !WEIGHTED && (flags & 96) == 96;
     for (int tt = blockIdx.x; tt < total && !aborted; tt += gridDim.x) {
       const int4 u = entry(tt);
       const int nkb = nkb_of(u);
@@ -1252,6 +1268,8 @@ static int row_launch(const RowGemm& p, int64_t max_tiles, int flags, cudaStream
                   "padded sorted output needs mode 0, a bf16/fp16 out_dtype and 16-byte aligned rows");
     flags |= 128;
   }
+  if (p.act == 1 && (a_tma || p.c_pad_start || p.mode != 0))
+    return fail(CVMM_ERR_INVALID_ARG, "the GELU epilogue needs a row-gathered A, row-indexed outputs and mode 0");
   const int64_t work = max_tiles * n_n;
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(work, sm_count()));
   if (a_dense && BN >= 128 && !(dbg_flags() & 32768)) {
@@ -1264,8 +1282,18 @@ static int row_launch(const RowGemm& p, int64_t max_tiles, int flags, cudaStream
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
     kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, cmap, flags, n_n);
+  } else if (tma && p.act == 1) {
+    auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true, false, false, true>;
+    int rc = set_smem(kern, L::alloc);
+    if (rc) return rc;
+    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, cmap, flags, n_n);
   } else if (tma) {
     auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true, false>;
+    int rc = set_smem(kern, L::alloc);
+    if (rc) return rc;
+    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, cmap, flags, n_n);
+  } else if (p.act == 1) {
+    auto kern = row_gemm_kernel<BN, S, BK_MAJOR, false, false, false, true>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
     kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, cmap, flags, n_n);

@@ -234,9 +234,11 @@ int cvmm_backward_x(const void* g, int g_dtype, int64_t g_ld, const int64_t* g_i
  * grad_w: [n_experts, m_dim, n_dim] fp32, fully written (empty experts get 0).
  * x_pad_start / g_pad_start != NULL: x / g is the expert-padded sorted
  * layout of cvmm_sort_rows_padded and x_index, x_div / g_index, g_div are
- * ignored (bf16/fp16 op_dtype, operand dtype == op_dtype). A padded g must
- * already carry the route weights (cvmm_sort_rows_padded's `scale`): w must
- * then be NULL.
+ * ignored (bf16/fp16 op_dtype, operand dtype == op_dtype). A padded g is
+ * used as it is (a copy made with cvmm_sort_rows_padded's `scale` already
+ * carries the route weights: pass w = NULL), or, with w != NULL, it is the
+ * unscaled copy and the weights are applied in shared memory with the same
+ * rounding, which lets one unscaled copy also feed cvmm_backward_x.
  * Long expert segments are split over several CTAs (split-K); their partial
  * sums live in the workspace (cvmm_gemm_workspace_size with k_dim = m_dim)
  * and are added in a fixed order, so results are deterministic. */

@@ -184,10 +184,11 @@ def test_sorted_operands_match_gathered_path_bitwise(route_input, weighted, d_in
 
 @pytest.mark.parametrize("route_input", [True, False])
 def test_weighted_grad_gather_matches_scaled_copy_bitwise(route_input):
-    """The weighted grad-W either reads a weight-scaled sorted copy of the token
-    grads or gathers and scales the token grad rows in shared memory; both
-    apply op(op(g) * op(w)) (cvmm.py:591-599) to the same operands in the same
-    order, so grad_keys is bit-identical."""
+    """The weighted backward reads one unscaled sorted copy of the token grads
+    in both GEMMs (weights applied in grad-W's shared memory), or a
+    weight-scaled sorted copy in grad-W, or gathers and scales the token grad
+    rows inside grad-W; all apply op(op(g) * op(w)) (cvmm.py:591-599) to the
+    same operands in the same order, so every output is bit-identical."""
     import cvmm_codex_b200.api as A
     g = torch.Generator().manual_seed(8)
     T, k, E, d_in, d_out = 900, 4, 7, 64, 320
@@ -198,16 +199,19 @@ def test_weighted_grad_gather_matches_scaled_copy_bitwise(route_input):
     w = torch.rand(T, k, generator=g)
     grad = torch.randn(T, d_out, generator=g)
     res = {}
-    old = A.cvmm_weighted_grad_copy
+    old = (A.cvmm_weighted_shared_grad_copy, A.cvmm_weighted_grad_copy)
     try:
-        for mode in (True, False):
-            A.cvmm_weighted_grad_copy = mode
+        # one unscaled copy shared by grad-W and grad-x; a weight-scaled copy
+        # for grad-W; token grad rows gathered and scaled inside grad-W
+        for mode in ((True, True), (False, True), (False, False)):
+            A.cvmm_weighted_shared_grad_copy, A.cvmm_weighted_grad_copy = mode
             res[mode] = run_case(x, keys, sel, w, grad, route_input, torch.bfloat16)
     finally:
-        A.cvmm_weighted_grad_copy = old
-    for a, b in zip(res[True], res[False]):
-        assert torch.equal(a, b)
-    check_oracle(*res[False], x, keys, sel, w, grad, "bfloat16")
+        A.cvmm_weighted_shared_grad_copy, A.cvmm_weighted_grad_copy = old
+    for mode in ((False, True), (False, False)):
+        for a, b in zip(res[(True, True)], res[mode]):
+            assert torch.equal(a, b), mode
+    check_oracle(*res[(True, True)], x, keys, sel, w, grad, "bfloat16")
 
 
 @pytest.mark.parametrize("n_experts,weighted", [(1024, False), (1100, False), (1024, True)])
