@@ -129,8 +129,11 @@ cvmm_backward_hook = None
 # sm_100a engine knob: the weighted backward makes ONE unscaled expert-padded
 # sorted copy of the token grads that both grad-W (weights applied in shared
 # memory) and grad-x read as dense tiles (True), instead of the per-GEMM
-# variants selected by cvmm_weighted_grad_copy. Bit-identical results.
-cvmm_weighted_shared_grad_copy = os.environ.get("CVMM_B200_WEIGHTED_SHARED_GRAD", "1").lower() not in ("0", "false", "no", "off")
+# variants selected by cvmm_weighted_grad_copy. Same results (the sel-weight
+# grad up to its fp32 summation order). Off by default: at ff_down_1024 it made
+# grad-x faster (74 -> 59 us) but the in-shared-memory scaling slowed grad-W
+# (62 -> 108 us).
+cvmm_weighted_shared_grad_copy = os.environ.get("CVMM_B200_WEIGHTED_SHARED_GRAD", "0").lower() in ("1", "true", "yes", "on")
 # Opt-in host check of the device status word after every CVMM forward and
 # backward (synchronises the stream): raises RuntimeError when a kernel gave up
 # on a bounded wait or met an out-of-range expert id.

@@ -175,11 +175,18 @@ def test_sorted_operands_match_gathered_path_bitwise(route_input, weighted, d_in
             res[mode] = run_case(x, keys, sel, w, grad, route_input, torch.bfloat16)
     finally:
         A.cvmm_sorted_operands = old
-    for a, b in zip(res[True], res[False]):
+    for i, (a, b) in enumerate(zip(res[True], res[False])):
         if a is None:
             assert b is None
             continue
-        assert torch.equal(a, b)
+        if i == 3:
+            # The sel-weight grad is an fp32 sum of per-column-group partial dots
+            # added with atomics; the dense path drains a tile with two epilogue
+            # warp groups (two partials per row), the gathered path with one, so
+            # only the fp32 summation order differs.
+            torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6 * b.abs().max().item())
+        else:
+            assert torch.equal(a, b)
 
 
 @pytest.mark.parametrize("route_input", [True, False])
@@ -209,8 +216,11 @@ def test_weighted_grad_gather_matches_scaled_copy_bitwise(route_input):
     finally:
         A.cvmm_weighted_shared_grad_copy, A.cvmm_weighted_grad_copy = old
     for mode in ((False, True), (False, False)):
-        for a, b in zip(res[(True, True)], res[mode]):
-            assert torch.equal(a, b), mode
+        for i, (a, b) in enumerate(zip(res[(True, True)], res[mode])):
+            if i == 3:  # sel-weight grad: fp32 atomics of partial dots, order differs (see above)
+                torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6 * b.abs().max().item())
+            else:
+                assert torch.equal(a, b), (mode, i)
     check_oracle(*res[(True, True)], x, keys, sel, w, grad, "bfloat16")
 
 
