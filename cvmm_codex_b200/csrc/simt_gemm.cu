@@ -379,6 +379,72 @@ __global__ void __launch_bounds__(256) sort_rows_padded_kernel(
   }
 }
 
+// Wide rows (>= 1 KiB, one 16-bit dtype, MODE 0 copy or MODE 3 scaled): one
+// warp per row, rows strided over a grid of resident warps. Every lane
+// resolves the row's source, destination and scale (the same addresses, one
+// transaction), the next row's metadata is loaded before the current row is
+// copied, and each lane keeps 4 x 16 bytes of the row in flight. The CTA-per-32
+// -rows kernel spent most of its time on its per-CTA index round at these row
+// lengths (the weight-scaled grad copy of ff_down moved 284 MB in 60 us).
+template <int MODE>
+__global__ void __launch_bounds__(256) sort_rows_wide_kernel(
+    const char* __restrict__ src, int64_t src_ld, const int64_t* __restrict__ index, int64_t div,
+    const void* __restrict__ scale, int scale_dtype, const int32_t* __restrict__ sorted_sel,
+    const int64_t* __restrict__ offsets, const int* __restrict__ pad_start, int64_t n_routes, int64_t n_experts,
+    int64_t cols, char* __restrict__ dst, int dtype) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t total = n_routes + n_experts * kPadRows;
+  const int cpr = (int)(cols / 8);  // 16-byte chunks per row
+  auto meta = [&](int64_t v) {
+    SortRowMeta m = {-1, -1, 1.f, 0};
+    if (v < n_routes) {
+      const int64_t r = index[v];
+      const int64_t e = sorted_sel[v];
+      m.src = idx_div(r, div) * src_ld;
+      m.dst = (pad_start[e] + v - seg_begin(offsets, e)) * cols;
+      if (MODE == 3) m.scale = round_to(load_as_float(scale, scale_dtype, r), dtype);
+    } else if (v < total) {
+      const int64_t e = (v - n_routes) / kPadRows, i = (v - n_routes) % kPadRows;
+      const int64_t cnt = offsets[e] - seg_begin(offsets, e);
+      if (cnt + i < (cnt + kPadRows - 1) / kPadRows * kPadRows) m.dst = (pad_start[e] + cnt + i) * cols;
+    }
+    return m;
+  };
+  int64_t v = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  SortRowMeta m = meta(v);
+  for (; v < total; v += nw) {
+    const SortRowMeta nxt = meta(v + nw);
+    if (m.dst >= 0) {
+      const uint4* s4 = reinterpret_cast<const uint4*>(src + m.src * 2);
+      uint4* d4 = reinterpret_cast<uint4*>(dst + m.dst * 2);
+      for (int c0 = 0; c0 < cpr; c0 += 128) {
+        uint4 buf[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = c0 + lane + 32 * j;
+          buf[j] = (c < cpr && m.src >= 0) ? s4[c] : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = c0 + lane + 32 * j;
+          if (c >= cpr) continue;
+          if (MODE == 3) {
+            uint32_t w[4] = {buf[j].x, buf[j].y, buf[j].z, buf[j].w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h)
+              w[h] = pack2(bits_to_float((uint16_t)(w[h] & 0xffffu), dtype) * m.scale,
+                           bits_to_float((uint16_t)(w[h] >> 16), dtype) * m.scale, dtype);
+            buf[j] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+          d4[c] = buf[j];
+        }
+      }
+    }
+    m = nxt;
+  }
+}
+
 int sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64_t* index, int64_t div,
                      const void* scale, int scale_dtype, const int32_t* sorted_sel, const int64_t* offsets,
                      const int* pad_start, int64_t n_routes, int64_t n_experts, int64_t cols, void* dst,
@@ -398,7 +464,15 @@ int sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64
   sort_rows_padded_kernel<MODE, ROWS><<<grid, 256, 0, stream>>>(s, src_dtype, src_ld, index, div, scale,        \
                                                                 scale_dtype, sorted_sel, offsets, pad_start,      \
                                                                 n_routes, n_experts, cols, d, dst_dtype)
-  if (mode == 0 && short_rows) CVMM_SORT_LAUNCH(0, 128);
+  const bool wide = (mode == 0 || mode == 3) && src_dtype != F32 && cols * dsz >= 1024;
+  const unsigned wgrid = (unsigned)std::min<int64_t>((rows + 7) / 8, 148 * 8);
+  if (wide && mode == 0)
+    sort_rows_wide_kernel<0><<<wgrid, 256, 0, stream>>>(s, src_ld, index, div, scale, scale_dtype, sorted_sel,
+                                                        offsets, pad_start, n_routes, n_experts, cols, d, dst_dtype);
+  else if (wide)
+    sort_rows_wide_kernel<3><<<wgrid, 256, 0, stream>>>(s, src_ld, index, div, scale, scale_dtype, sorted_sel,
+                                                        offsets, pad_start, n_routes, n_experts, cols, d, dst_dtype);
+  else if (mode == 0 && short_rows) CVMM_SORT_LAUNCH(0, 128);
   else if (mode == 0) CVMM_SORT_LAUNCH(0, 32);
   else if (mode == 3 && short_rows) CVMM_SORT_LAUNCH(3, 128);
   else if (mode == 3) CVMM_SORT_LAUNCH(3, 32);

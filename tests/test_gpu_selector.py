@@ -116,17 +116,21 @@ def test_cuda_default_sort_agrees_with_stable_order(R, E):
     assert torch.equal(s.sel_index, default.indices // 4)
 
 
-@pytest.mark.parametrize("src_dtype,dst_dtype,scaled", [
-    (torch.bfloat16, torch.bfloat16, False),
-    (torch.float32, torch.bfloat16, False),
-    (torch.bfloat16, torch.bfloat16, True),
-    (torch.float32, torch.float16, True),
+@pytest.mark.parametrize("src_dtype,dst_dtype,scaled,cols", [
+    (torch.bfloat16, torch.bfloat16, False, 136),
+    (torch.float32, torch.bfloat16, False, 136),
+    (torch.bfloat16, torch.bfloat16, True, 136),
+    (torch.float32, torch.float16, True, 136),
+    # rows of 1 KiB and more take the warp-per-row kernel (copy and scaled)
+    (torch.bfloat16, torch.bfloat16, False, 1032),
+    (torch.bfloat16, torch.bfloat16, True, 1024),
+    (torch.float16, torch.float16, True, 4104),
 ])
-def test_sort_rows_padded_matches_oracle(src_dtype, dst_dtype, scaled):
+def test_sort_rows_padded_matches_oracle(src_dtype, dst_dtype, scaled, cols):
     """Expert-padded sorted copy of route rows (the grouping copy of cvmm.py:338-360),
     with the op-dtype rounding and the weighted-grad product rounding of cvmm.py:591-599."""
     g = torch.Generator().manual_seed(21)
-    R, E, cols, pad, k = 3000, 11, 136, 128, 3
+    R, E, pad, k = 3000, 11, 128, 3
     sel = torch.randint(0, E, (R // k, k), generator=g)
     sel[:, 0] = 4  # a long segment
     sel[:, 1] = torch.where(sel[:, 1] == 7, 8, sel[:, 1])  # expert 7 empty unless drawn in column 2
