@@ -35,6 +35,7 @@ _S = ctypes.c_size_t
 SIGNATURES = {
     "cvmm_abi_version": (_I, []),
     "cvmm_last_error": (ctypes.c_char_p, []),
+    "cvmm_set_sm_limit": (_I, [_I]),
     "cvmm_device_status": (_I, [_I, ctypes.POINTER(_I), ctypes.POINTER(ctypes.c_longlong), _P]),
     "cvmm_sel_prepare_workspace_size": (_S, [_L]),
     "cvmm_sel_prepare": (_I, [_P, _I, _L, _L, _I, _P, _P, _P, _P, _P, _S, _P]),

@@ -433,6 +433,11 @@ extern "C" {
 
 int cvmm_abi_version(void) { return 6; }
 
+int cvmm_set_sm_limit(int n_sms) {
+  if (n_sms < 0) return fail(CVMM_ERR_INVALID_ARG, "cvmm_set_sm_limit: n_sms must be >= 0");
+  return g_sm_limit.exchange(n_sms);
+}
+
 const char* cvmm_last_error(void) { return t_err; }
 
 int cvmm_device_status(int reset, int* where, long long* aux, cvmm_stream_t stream) {

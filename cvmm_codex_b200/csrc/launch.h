@@ -6,10 +6,15 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "../../include/cvmm_sm100.h"
 
 namespace cvmm {
+
+// SMs the persistent tensor-core GEMMs may occupy (0: all). Set through
+// cvmm_set_sm_limit while a collective must run next to them.
+inline std::atomic<int> g_sm_limit{0};
 
 // Records `msg` as the calling thread's last error and returns `code`.
 int fail(int code, const char* msg);

@@ -1168,12 +1168,14 @@ static int set_smem(K kernel, uint32_t bytes) {
 
 static inline bool aligned16(const void* ptr) { return ((uintptr_t)ptr & 15u) == 0; }
 
+// SMs a persistent GEMM grid may use: the device's, capped by cvmm_set_sm_limit.
 static int sm_count() {
   int dev = 0, v = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
-      v > 0)
-    return v;
-  return 148;
+  if (!(cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+        v > 0))
+    v = 148;
+  const int lim = g_sm_limit.load(std::memory_order_relaxed);
+  return lim > 0 ? std::min(v, lim) : v;
 }
 
 static int dbg_flags() {

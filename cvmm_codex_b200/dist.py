@@ -50,10 +50,20 @@ class OverlappedGradReduce:
       and makes the compute stream wait for it.
     The gradient is summed in place and in the same order as a plain
     all-reduce after the backward, so results are identical.
+
+    From grad-W to the end of the backward the persistent GEMMs are capped at
+    the device's SMs minus `reserve_sms` (default 16, env CVMM_B200_NCCL_SMS)
+    through cvmm_set_sm_limit: they hold nearly all of an SM's shared memory,
+    so without free SMs the all-reduce's kernels would only start after them.
     """
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, reserve_sms=None):
+        import os
         self.group = group
+        # SMs left free for the collective while grad-x runs: the persistent
+        # GEMMs otherwise hold every SM and NCCL's kernels only start after them.
+        self.reserve = int(os.environ.get("CVMM_B200_NCCL_SMS", "16")) if reserve_sms is None else int(reserve_sms)
+        self._prev_limit = None
         self.side = torch.cuda.Stream()
         self.ready = torch.cuda.Event(external=True)
         self._grad = None
@@ -74,8 +84,16 @@ class OverlappedGradReduce:
     def grad_keys_ready(self, grad_keys: torch.Tensor) -> None:
         self.ready.record()
         self._grad = None if torch.cuda.is_current_stream_capturing() else grad_keys
+        if self.reserve > 0 and dist.is_initialized() and dist.get_world_size(self.group) > 1:
+            from . import _lib
+            n = torch.cuda.get_device_properties(grad_keys.device).multi_processor_count
+            self._prev_limit = _lib.load().cvmm_set_sm_limit(max(1, n - self.reserve))
 
     def backward_done(self) -> None:
+        if self._prev_limit is not None:
+            from . import _lib
+            _lib.load().cvmm_set_sm_limit(self._prev_limit)
+            self._prev_limit = None
         if self._grad is not None:
             grad, self._grad = self._grad, None
             self.launch(grad)

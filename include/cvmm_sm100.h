@@ -54,6 +54,14 @@ typedef struct CUstream_st* cvmm_stream_t; /* == cudaStream_t */
 /* ABI version of this header; bumped on any signature change. */
 int cvmm_abi_version(void);  /* 6 */
 
+/* Caps the number of SMs the persistent tensor-core GEMMs launched from now on
+ * may occupy (one CTA per SM, nearly all of its shared memory); 0 removes the
+ * cap. Returns the previous cap. Process-wide. A data-parallel caller sets it
+ * while an NCCL collective (the grad-W all-reduce) runs next to the grad-x
+ * kernels, so the collective's CTAs find free SMs instead of waiting for the
+ * GEMM to end. No reference counterpart (the reference is single-GPU). */
+int cvmm_set_sm_limit(int n_sms);
+
 /* Message for the last failed call on the calling host thread. */
 const char* cvmm_last_error(void);
 
