@@ -2,6 +2,7 @@
 // argument validation, engine selection and the small memory-bound kernels
 // (weighted combine, top-k sums, token-input weighted backward tail, casts).
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "gemm.cuh"
@@ -372,6 +373,11 @@ static int64_t segw_chunk(int64_t n_routes, int64_t n_experts, int64_t m_dim, in
   // 1024 routes, which split about half of the 64 experts).
   int64_t chunk = 1024;
   while (chunk < 8192 && chunk * 2 <= n_routes * mt * nt / 148) chunk *= 2;
+  // Tuning override (routes per split-K chunk, a multiple of 64) for measurements.
+  if (const char* ev = getenv("CVMM_B200_GRADW_CHUNK")) {
+    const long long v = atoll(ev);
+    if (v >= 64 && v % 64 == 0) return v;
+  }
   // ... but at least one unit tile per SM (every expert is at least one unit).
   while (chunk > 128 && std::max<int64_t>(n_experts, n_routes / chunk) * mt * nt < 148) chunk /= 2;
   while (2 * ((n_routes + chunk - 1) / chunk) * m_dim * n_dim * 4 > ((int64_t)256 << 20)) chunk *= 2;
