@@ -24,6 +24,20 @@ int fail_cuda(const char* where) {
   return CVMM_ERR_LAUNCH;
 }
 
+static std::atomic<int> g_pdl{-1};  // -1: not read from the environment yet
+
+bool pdl_enabled() {
+  int v = g_pdl.load(std::memory_order_relaxed);
+  if (v < 0) {
+    const char* ev = getenv("CVMM_B200_PDL");
+    int want = (ev && ev[0] == '0') ? 0 : 1;
+    int expected = -1;
+    g_pdl.compare_exchange_strong(expected, want);
+    v = g_pdl.load(std::memory_order_relaxed);
+  }
+  return v != 0;
+}
+
 int check_launch(const char* where) {
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) return CVMM_OK;
@@ -44,6 +58,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const void* __restrict__ s
                                                       const void* __restrict__ w, int w_dtype,
                                                       const int32_t* __restrict__ rows, void* __restrict__ out,
                                                       int o_dtype, int64_t T, int64_t k, int64_t N) {
+  pdl_enter();
   const int64_t groups = (N + 7) / 8;
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= T * groups) return;
@@ -107,6 +122,7 @@ __global__ void __launch_bounds__(256, 3) combine_vec_kernel(const uint4* __rest
                                                           const void* __restrict__ w, int w_dtype,
                                                           const int32_t* __restrict__ rows, uint4* __restrict__ out,
                                                           int o_dtype, int64_t T, int64_t k, int64_t groups) {
+  pdl_enter();
   const int64_t tpt = groups / CPT;  // threads per token
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (i >= T * tpt) return;
@@ -157,6 +173,7 @@ __global__ void __launch_bounds__(256, 3) combine_vec_kernel(const uint4* __rest
 // elementwise backward of F.gelu that follows the down projection's grad-x).
 __global__ void __launch_bounds__(256) gelu_backward_kernel(const void* __restrict__ grad, const void* __restrict__ z,
                                                             void* __restrict__ out, int dtype, int64_t n, bool vec) {
+  pdl_enter();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   if (vec) {
     const uint4* g4 = static_cast<const uint4*>(grad);
@@ -192,6 +209,7 @@ constexpr int kRouterMaxExperts = 1024;
 __global__ void __launch_bounds__(256) router_topk_kernel(const void* __restrict__ logits, int dtype, int64_t T,
                                                           int64_t E, int64_t k, int renorm,
                                                           int64_t* __restrict__ sel, float* __restrict__ weights) {
+  pdl_enter();
   constexpr int kPer = kRouterMaxExperts / 32;
   const int lane = threadIdx.x & 31;
   const int64_t t = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
@@ -271,6 +289,7 @@ __global__ void wait_timeout_selftest_kernel(uint64_t limit_ns) {
 __global__ void padded_route_rows_kernel(const int64_t* __restrict__ route, const int32_t* __restrict__ sorted_sel,
                                          const int64_t* __restrict__ offsets, const int32_t* __restrict__ pad_start,
                                          int64_t n_routes, int32_t* __restrict__ rows) {
+  pdl_enter();
   const int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (v >= n_routes) return;
   const int64_t e = sorted_sel[v];
@@ -283,6 +302,7 @@ __global__ void weighted_token_bwd_kernel(const void* __restrict__ rg, int rg_dt
                                           const void* __restrict__ x, int x_dtype,
                                           void* __restrict__ gx, int gx_dtype,
                                           float* __restrict__ gsel, int64_t k, int64_t d) {
+  pdl_enter();
   const int64_t t = blockIdx.x;
   extern __shared__ float red[];  // [blockDim.x / 32]
   for (int64_t j = 0; j < k; ++j) {
@@ -313,6 +333,7 @@ __global__ void weighted_token_bwd_kernel(const void* __restrict__ rg, int rg_dt
 
 __global__ void cast_kernel(const void* __restrict__ src, int s_dtype, void* __restrict__ dst,
                             int d_dtype, int64_t n) {
+  pdl_enter();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     store_from_float(dst, d_dtype, i, load_as_float(src, s_dtype, i));
@@ -321,6 +342,7 @@ __global__ void cast_kernel(const void* __restrict__ src, int s_dtype, void* __r
 // fp32 -> bf16/fp16, 8 elements per thread with 32-byte loads / 16-byte stores.
 __global__ void cast_f32_to_16_vec(const float4* __restrict__ src, uint4* __restrict__ dst,
                                    int d_dtype, int64_t n8) {
+  pdl_enter();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8;
        i += (int64_t)gridDim.x * blockDim.x) {
     const float4 a = src[2 * i], b = src[2 * i + 1];
@@ -437,7 +459,13 @@ using namespace cvmm;
 // ================================================================== C ABI
 extern "C" {
 
-int cvmm_abi_version(void) { return 6; }
+int cvmm_abi_version(void) { return 7; }
+
+int cvmm_set_pdl(int enable) {
+  const int prev = pdl_enabled() ? 1 : 0;
+  g_pdl.store(enable ? 1 : 0);
+  return prev;
+}
 
 int cvmm_set_sm_limit(int n_sms) {
   if (n_sms < 0) return fail(CVMM_ERR_INVALID_ARG, "cvmm_set_sm_limit: n_sms must be >= 0");
@@ -563,7 +591,7 @@ int cvmm_gelu_backward(const void* grad, const void* pre_act, void* grad_pre_act
   const bool vec = n % 8 == 0 && al16(grad) && al16(pre_act) && al16(grad_pre_act);
   const int64_t items = vec ? n / 8 : n;
   const unsigned grid = (unsigned)std::min<int64_t>((items + 255) / 256, 148 * 16);
-  gelu_backward_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(grad, pre_act, grad_pre_act,
+  launch(gelu_backward_kernel, grid, 256, 0, reinterpret_cast<cudaStream_t>(stream), grad, pre_act, grad_pre_act,
                                                                                 dtype, n, vec);
   return check_launch("cvmm_gelu_backward");
 }
@@ -578,7 +606,7 @@ int cvmm_router_topk(const void* logits, int logits_dtype, int64_t n_tokens, int
   if (n_tokens == 0) return CVMM_OK;
   if (!logits || !sel || !weights) return fail(CVMM_ERR_INVALID_ARG, "cvmm_router_topk: null pointer");
   const unsigned grid = (unsigned)((n_tokens + 7) / 8);
-  router_topk_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch(router_topk_kernel, grid, 256, 0, reinterpret_cast<cudaStream_t>(stream),
       logits, logits_dtype, n_tokens, n_experts, top_k, renormalize, sel, weights);
   return check_launch("cvmm_router_topk");
 }
@@ -599,12 +627,12 @@ int cvmm_weighted_combine(const void* y, int y_dtype, const void* w, int w_dtype
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (vec && groups % 2 == 0) {
     const unsigned g2 = (unsigned)((n_tokens * (groups / 2) + 255) / 256);
-    combine_vec_kernel<2><<<g2, 256, 0, s>>>(static_cast<const uint4*>(y), y_dtype, w, w_dtype, y_rows,
+    launch(combine_vec_kernel<2>, g2, 256, 0, s, static_cast<const uint4*>(y), y_dtype, w, w_dtype, y_rows,
                                              static_cast<uint4*>(out), out_dtype, n_tokens, top_k, groups);
   } else if (vec)
-    combine_kernel<true><<<grid, 256, 0, s>>>(y, y_dtype, w, w_dtype, y_rows, out, out_dtype, n_tokens, top_k, n_dim);
+    launch(combine_kernel<true>, grid, 256, 0, s, y, y_dtype, w, w_dtype, y_rows, out, out_dtype, n_tokens, top_k, n_dim);
   else
-    combine_kernel<false><<<grid, 256, 0, s>>>(y, y_dtype, w, w_dtype, y_rows, out, out_dtype, n_tokens, top_k, n_dim);
+    launch(combine_kernel<false>, grid, 256, 0, s, y, y_dtype, w, w_dtype, y_rows, out, out_dtype, n_tokens, top_k, n_dim);
   return check_launch("cvmm_weighted_combine");
 }
 
@@ -629,7 +657,7 @@ int cvmm_padded_route_rows(const int64_t* route, const int32_t* sorted_sel, cons
   if (n_routes == 0) return CVMM_OK;
   if (!route || !sorted_sel || !offsets || !pad_start || !rows)
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_padded_route_rows: null pointer");
-  padded_route_rows_kernel<<<(unsigned)((n_routes + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch(padded_route_rows_kernel, (unsigned)((n_routes + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream),
       route, sorted_sel, offsets, pad_start, n_routes, rows);
   return check_launch("cvmm_padded_route_rows");
 }
@@ -770,8 +798,7 @@ int cvmm_weighted_token_backward(const void* route_grad, int rg_dtype, const voi
   if (!route_grad || !w || (grad_sel && !x))
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_weighted_token_backward: null pointer");
   const int threads = 256;
-  weighted_token_bwd_kernel<<<(unsigned)n_tokens, threads, (threads / 32) * sizeof(float),
-                              reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch(weighted_token_bwd_kernel, (unsigned)n_tokens, threads, (threads / 32) * sizeof(float), reinterpret_cast<cudaStream_t>(stream),
       route_grad, rg_dtype, w, w_dtype, x, x_dtype, grad_x, gx_dtype, grad_sel, top_k, d);
   return check_launch("cvmm_weighted_token_backward");
 }
@@ -784,10 +811,10 @@ int cvmm_cast(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t 
   if (!src || !dst) return fail(CVMM_ERR_INVALID_ARG, "cvmm_cast: null pointer");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (src_dtype == F32 && dst_dtype != F32 && n % 8 == 0 && al16(src) && al16(dst)) {
-    cast_f32_to_16_vec<<<grid_for(n / 8, 256), 256, 0, s>>>(static_cast<const float4*>(src),
+    launch(cast_f32_to_16_vec, grid_for(n / 8, 256), 256, 0, s, static_cast<const float4*>(src),
                                                             static_cast<uint4*>(dst), dst_dtype, n / 8);
   } else {
-    cast_kernel<<<grid_for(n, 256), 256, 0, s>>>(src, src_dtype, dst, dst_dtype, n);
+    launch(cast_kernel, grid_for(n, 256), 256, 0, s, src, src_dtype, dst, dst_dtype, n);
   }
   return check_launch("cvmm_cast");
 }

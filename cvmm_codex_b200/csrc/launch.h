@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <utility>
 
 #include "../../include/cvmm_sm100.h"
 
@@ -15,6 +16,30 @@ namespace cvmm {
 // SMs the persistent tensor-core GEMMs may occupy (0: all). Set through
 // cvmm_set_sm_limit while a collective must run next to them.
 inline std::atomic<int> g_sm_limit{0};
+
+// Programmatic dependent launches (on unless CVMM_B200_PDL=0): every kernel
+// is launched with cudaLaunchAttributeProgrammaticStreamSerialization, so its
+// CTAs are scheduled as the previous kernel on the stream drains and wait in
+// pdl_wait() (device side) for that kernel's completion. In stream capture the
+// attribute becomes a programmatic edge of the graph.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline void launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                   Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // Errors are picked up by check_launch (cudaGetLastError) like <<<>>> launches.
+  (void)cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // Records `msg` as the calling thread's last error and returns `code`.
 int fail(int code, const char* msg);

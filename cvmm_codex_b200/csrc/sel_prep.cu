@@ -123,6 +123,7 @@ sort_kernel(const void* __restrict__ sel, int sel_dtype, int64_t n, int64_t cta_
             int32_t* __restrict__ vbuf0, int32_t* __restrict__ kbuf1, int32_t* __restrict__ vbuf1,
             int32_t* __restrict__ sorted_sel, int64_t* __restrict__ sel_index, int64_t* __restrict__ out_index,
             int64_t top_k, int route_input) {
+  pdl_enter();
   extern __shared__ int hist[];  // [kWarps][kBins] per-warp digit counts, then per-warp write positions
   __shared__ int bin_base[kBins];
   __shared__ int warp_tot[kWarps];
@@ -282,6 +283,7 @@ sort_kernel(const void* __restrict__ sel, int sel_dtype, int64_t n, int64_t cta_
 // written exactly once, with no search.
 __global__ void offsets_kernel(const int32_t* __restrict__ sorted, int64_t n, int64_t n_experts,
                                int64_t* __restrict__ offsets) {
+  pdl_enter();
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (n == 0) {
     if (i < n_experts) offsets[i] = 0;
@@ -354,7 +356,7 @@ int sel_prepare(const void* sel_ptr, int sel_dtype, int64_t n, int64_t top_k, in
     return fail_cuda("cvmm_sel_prepare: cudaFuncSetAttribute");
   if (cudaMemsetAsync(h, 0, sizeof(sel::Header), stream) != cudaSuccess)
     return fail_cuda("cvmm_sel_prepare: memset");
-  sel::sort_kernel<<<grid, sel::kThreads, sel::kSmemBytes, stream>>>(
+  launch(sel::sort_kernel, grid, sel::kThreads, sel::kSmemBytes, stream,
       sel_ptr, sel_dtype, n, cta_len, raw_sel, h, counts, bin_total, buf[0], buf[1], buf[2], buf[3], sorted_sel,
       sel_index, out_index, top_k, route_input);
   return check_launch("cvmm_sel_prepare");
@@ -365,7 +367,7 @@ int expert_offsets(const int32_t* sorted, int64_t n, int64_t n_experts, int64_t*
   if (n < 0 || n_experts <= 0 || !offsets || (n > 0 && !sorted))
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_expert_offsets: bad arguments");
   const int64_t work = n > 0 ? n : n_experts;
-  sel::offsets_kernel<<<(unsigned)((work + 255) / 256), 256, 0, stream>>>(sorted, n, n_experts, offsets);
+  launch(sel::offsets_kernel, (unsigned)((work + 255) / 256), 256, 0, stream, sorted, n, n_experts, offsets);
   return check_launch("cvmm_expert_offsets");
 }
 

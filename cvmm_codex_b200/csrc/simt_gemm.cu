@@ -15,6 +15,7 @@ namespace cvmm {
 __global__ void __launch_bounds__(1024)
 build_tiles_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int bm,
                    int4* __restrict__ tiles, int* __restrict__ n_tiles) {
+  pdl_enter();
   const int t = threadIdx.x;
   const int64_t per = (n_experts + blockDim.x - 1) / blockDim.x;
   const int64_t e0 = min((int64_t)t * per, n_experts), e1 = min(e0 + per, n_experts);
@@ -51,7 +52,7 @@ build_tiles_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int b
 
 int build_tiles(const int64_t* offsets, int64_t n_experts, int bm, int4* tiles, int* n_tiles,
                 cudaStream_t stream) {
-  build_tiles_kernel<<<1, 1024, 0, stream>>>(offsets, n_experts, bm, tiles, n_tiles);
+  launch(build_tiles_kernel, 1, 1024, 0, stream, offsets, n_experts, bm, tiles, n_tiles);
   return check_launch("build_tiles");
 }
 
@@ -88,6 +89,7 @@ constexpr int kUnitSortMaxExperts = 1024;
 __global__ void __launch_bounds__(1024)
 build_units_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int64_t chunk,
                    int4* __restrict__ units, int* __restrict__ n_units, int2* __restrict__ expert_slots) {
+  pdl_enter();
   __shared__ int warp_tot[32];
   __shared__ int tail_len[kUnitSortMaxExperts];  // each expert's tail chunk length (0: none)
   const int t = threadIdx.x;
@@ -143,7 +145,7 @@ build_units_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int64
 
 int build_units(const int64_t* offsets, int64_t n_experts, int64_t chunk, int4* units, int* n_units,
                 int2* expert_slots, cudaStream_t stream) {
-  build_units_kernel<<<1, 1024, 0, stream>>>(offsets, n_experts, chunk, units, n_units, expert_slots);
+  launch(build_units_kernel, 1, 1024, 0, stream, offsets, n_experts, chunk, units, n_units, expert_slots);
   return check_launch("build_units");
 }
 
@@ -151,6 +153,7 @@ int build_units(const int64_t* offsets, int64_t n_experts, int64_t chunk, int4* 
 // tensor-core grad-W, whose index warp bulk-copies them into shared memory).
 __global__ void resolve_route_rows_kernel(SegGemm p, int* __restrict__ xrow, int* __restrict__ grow,
                                           float* __restrict__ wsc, int64_t padded) {
+  pdl_enter();
   for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < padded; r += (int64_t)gridDim.x * blockDim.x) {
     const bool ok = r < p.n_routes;
     int64_t lo = 0;  // expert of sorted position r (padded layouts): first e with offsets[e] > r
@@ -173,7 +176,7 @@ __global__ void resolve_route_rows_kernel(SegGemm p, int* __restrict__ xrow, int
 int resolve_route_rows(const SegGemm& p, int* xrow, int* grow, float* wsc, cudaStream_t stream) {
   const int64_t padded = p.n_routes + kRouteRowsPad;
   const int grid = (int)std::min<int64_t>((padded + 255) / 256, 148 * 8);
-  resolve_route_rows_kernel<<<grid, 256, 0, stream>>>(p, xrow, grow, wsc, padded);
+  launch(resolve_route_rows_kernel, grid, 256, 0, stream, p, xrow, grow, wsc, padded);
   return check_launch("resolve_route_rows");
 }
 
@@ -181,6 +184,7 @@ int resolve_route_rows(const SegGemm& p, int* xrow, int* grow, float* wsc, cudaS
 // Counts and pad starts are below 2^31 (checked by the callers): 32-bit math.
 __global__ void __launch_bounds__(512)
 pad_starts_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int64_t pad, int* __restrict__ pad_start) {
+  pdl_enter();
   __shared__ int warp_tot[32];
   const int t = threadIdx.x, n = (int)n_experts, pd = (int)pad;
   const int per = (n + (int)blockDim.x - 1) / (int)blockDim.x;
@@ -199,7 +203,7 @@ pad_starts_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int64_
 }
 
 int pad_starts(const int64_t* offsets, int64_t n_experts, int64_t pad, int* pad_start, cudaStream_t stream) {
-  pad_starts_kernel<<<1, 512, 0, stream>>>(offsets, n_experts, pad, pad_start);
+  launch(pad_starts_kernel, 1, 512, 0, stream, offsets, n_experts, pad, pad_start);
   return check_launch("pad_starts");
 }
 
@@ -261,6 +265,7 @@ __global__ void __launch_bounds__(256) sort_rows_padded_kernel(
     const void* __restrict__ scale, int scale_dtype, const int32_t* __restrict__ sorted_sel,
     const int64_t* __restrict__ offsets, const int* __restrict__ pad_start, int64_t n_routes, int64_t n_experts,
     int64_t cols, char* __restrict__ dst, int dst_dtype) {
+  pdl_enter();
   __shared__ SortRowMeta meta[ROWS];
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t v0 = blockIdx.x * (int64_t)ROWS;
@@ -392,6 +397,7 @@ __global__ void __launch_bounds__(256) sort_rows_wide_kernel(
     const void* __restrict__ scale, int scale_dtype, const int32_t* __restrict__ sorted_sel,
     const int64_t* __restrict__ offsets, const int* __restrict__ pad_start, int64_t n_routes, int64_t n_experts,
     int64_t cols, char* __restrict__ dst, int dtype) {
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int64_t total = n_routes + n_experts * kPadRows;
@@ -461,16 +467,16 @@ int sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64
   const char* s = static_cast<const char*>(src);
   char* d = static_cast<char*>(dst);
 #define CVMM_SORT_LAUNCH(MODE, ROWS)                                                                              \
-  sort_rows_padded_kernel<MODE, ROWS><<<grid, 256, 0, stream>>>(s, src_dtype, src_ld, index, div, scale,        \
+  launch(sort_rows_padded_kernel<MODE, ROWS>, grid, 256, 0, stream, s, src_dtype, src_ld, index, div, scale,        \
                                                                 scale_dtype, sorted_sel, offsets, pad_start,      \
                                                                 n_routes, n_experts, cols, d, dst_dtype)
   const bool wide = (mode == 0 || mode == 3) && src_dtype != F32 && cols * dsz >= 1024;
   const unsigned wgrid = (unsigned)std::min<int64_t>((rows + 7) / 8, 148 * 8);
   if (wide && mode == 0)
-    sort_rows_wide_kernel<0><<<wgrid, 256, 0, stream>>>(s, src_ld, index, div, scale, scale_dtype, sorted_sel,
+    launch(sort_rows_wide_kernel<0>, wgrid, 256, 0, stream, s, src_ld, index, div, scale, scale_dtype, sorted_sel,
                                                         offsets, pad_start, n_routes, n_experts, cols, d, dst_dtype);
   else if (wide)
-    sort_rows_wide_kernel<3><<<wgrid, 256, 0, stream>>>(s, src_ld, index, div, scale, scale_dtype, sorted_sel,
+    launch(sort_rows_wide_kernel<3>, wgrid, 256, 0, stream, s, src_ld, index, div, scale, scale_dtype, sorted_sel,
                                                         offsets, pad_start, n_routes, n_experts, cols, d, dst_dtype);
   else if (mode == 0 && short_rows) CVMM_SORT_LAUNCH(0, 128);
   else if (mode == 0) CVMM_SORT_LAUNCH(0, 32);
@@ -488,6 +494,7 @@ int sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64
 // written by their unit and are skipped.
 __global__ void seg_reduce_kernel(const int2* __restrict__ expert_slots, const float4* __restrict__ partials,
                                   float4* __restrict__ out, int64_t mn4) {
+  pdl_enter();
   const int64_t e = blockIdx.y;
   const int2 es = expert_slots[e];
   if (es.y == 1) return;
@@ -503,6 +510,7 @@ __global__ void seg_reduce_kernel(const int2* __restrict__ expert_slots, const f
 
 __global__ void seg_reduce_scalar_kernel(const int2* __restrict__ expert_slots, const float* __restrict__ partials,
                                          float* __restrict__ out, int64_t mn) {
+  pdl_enter();
   const int64_t e = blockIdx.y;
   const int2 es = expert_slots[e];
   if (es.y == 1) return;
@@ -519,10 +527,10 @@ int seg_reduce(const int2* expert_slots, const float* partials, float* out, int6
   const int64_t work = vec ? mn / 4 : mn;
   dim3 grid((unsigned)std::min<int64_t>((work + 255) / 256, 64), (unsigned)n_experts);
   if (vec)
-    seg_reduce_kernel<<<grid, 256, 0, stream>>>(expert_slots, reinterpret_cast<const float4*>(partials),
+    launch(seg_reduce_kernel, grid, 256, 0, stream, expert_slots, reinterpret_cast<const float4*>(partials),
                                                 reinterpret_cast<float4*>(out), mn / 4);
   else
-    seg_reduce_scalar_kernel<<<grid, 256, 0, stream>>>(expert_slots, partials, out, mn);
+    launch(seg_reduce_scalar_kernel, grid, 256, 0, stream, expert_slots, partials, out, mn);
   return check_launch("seg_reduce");
 }
 
@@ -532,6 +540,7 @@ namespace simt {
 constexpr int TM = 64, TN = 64, TK = 16, THREADS = 256;
 
 __global__ void __launch_bounds__(THREADS) row_gemm_kernel(RowGemm p) {
+  pdl_enter();
   if ((int)blockIdx.x >= *p.n_tiles) return;
   const int4 tile = p.tiles[blockIdx.x];
   const int64_t e = tile.x, r0 = tile.y;
@@ -622,6 +631,7 @@ __global__ void __launch_bounds__(THREADS) row_gemm_kernel(RowGemm p) {
 // Split-K like the tensor-core kernel: one CTA per (work unit, m tile, n tile),
 // writing grad_w directly or the unit's partial slot.
 __global__ void __launch_bounds__(THREADS) seg_gemm_kernel(SegGemm p) {
+  pdl_enter();
   if ((int)blockIdx.x >= *p.n_units) return;
   const int4 unit = p.units[blockIdx.x];
   const int64_t e = unit.x;
@@ -688,14 +698,14 @@ __global__ void __launch_bounds__(THREADS) seg_gemm_kernel(SegGemm p) {
 
 int launch_row_gemm_simt(const RowGemm& p, int64_t max_tiles, cudaStream_t stream) {
   dim3 grid((unsigned)max_tiles, (unsigned)((p.N + simt::TN - 1) / simt::TN));
-  simt::row_gemm_kernel<<<grid, simt::THREADS, 0, stream>>>(p);
+  launch(simt::row_gemm_kernel, grid, simt::THREADS, 0, stream, p);
   return check_launch("row_gemm_simt");
 }
 
 int launch_seg_gemm_simt(const SegGemm& p, int64_t max_units, cudaStream_t stream) {
   dim3 grid((unsigned)max_units, (unsigned)((p.M + simt::TM - 1) / simt::TM),
             (unsigned)((p.N + simt::TN - 1) / simt::TN));
-  simt::seg_gemm_kernel<<<grid, simt::THREADS, 0, stream>>>(p);
+  launch(simt::seg_gemm_kernel, grid, simt::THREADS, 0, stream, p);
   return check_launch("seg_gemm_simt");
 }
 

@@ -408,6 +408,7 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
   // expert e, sbeg[e] = its first sorted route (sbeg[E] = n_routes).
   int* tstart = reinterpret_cast<int*>(smem + L::plan);
   int* sbeg = tstart + kPlanExperts + 1;
+  pdl_wait();  // before the first global access (the offsets below)
   const bool own_tiles = p.tiles == nullptr;
   const int n_exp = (int)p.n_experts;
   if (own_tiles) {
@@ -429,11 +430,11 @@ row_gemm_kernel(const RowGemm p, const __grid_constant__ CUtensorMap tmap_b,
     __syncthreads();
   }
   const int total = (own_tiles ? tstart[n_exp] : *p.n_tiles) * n_n;
+  const uint32_t tmem = setup<BN, S>(bar, EPI2 ? 1 : (A_TMA ? 2 : kProducers + (B_TMA ? 1 : 0)), kProducers, 1,
+                                     EPI2 ? 2 * kEpilogue : kEpilogue, (flags & kFlagACopy) ? 2 : 1);
   const int nkb = (int)((p.K + BK - 1) / BK);
   const int op = p.op_dtype;
   const bool a_fast = flags & 1, b_fast = flags & 2, c_vec = flags & 4;
-  const uint32_t tmem = setup<BN, S>(bar, EPI2 ? 1 : (A_TMA ? 2 : kProducers + (B_TMA ? 1 : 0)), kProducers, 1,
-                                     EPI2 ? 2 * kEpilogue : kEpilogue, (flags & kFlagACopy) ? 2 : 1);
 
   auto entry = [&](int tt) -> int4 {
     if (tt >= total) return make_int4(0, 0, 0, 0);
@@ -879,12 +880,13 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
   IdxSlot* ring = reinterpret_cast<IdxSlot*>(smem + L::ring);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per_unit = n_m * n_n;
-  const int total = *p.n_units * per_unit;
-  const int op = p.op_dtype;
-  const bool x_fast = flags & 1, g_fast = flags & 2, o_vec = flags & 4;
   constexpr int kTransform = kProducers - 32;  // warps 1-3 scale weighted grad rows
   const uint32_t tmem = G_TMA ? setup<BN, S>(bar, 1, WEIGHTED ? kProducers : 32, kTransform)
                               : setup<BN, S>(bar, kProducers);
+  pdl_wait();
+  const int total = *p.n_units * per_unit;
+  const int op = p.op_dtype;
+  const bool x_fast = flags & 1, g_fast = flags & 2, o_vec = flags & 4;
 
   auto entry = [&](int tt) -> int4 {
     return tt < total ? p.units[tt / per_unit] : make_int4(0, 0, -1, 0);
@@ -1278,32 +1280,32 @@ static int row_launch(const RowGemm& p, int64_t max_tiles, int flags, cudaStream
     auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true, true, (BN >= 128)>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
-    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, cmap, flags, n_n);
+    launch(kern, grid, kThreads, L::alloc, stream, p, map, amap, cmap, flags, n_n);
   } else if (a_tma) {
     auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true, true>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
-    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, cmap, flags, n_n);
+    launch(kern, grid, kThreads, L::alloc, stream, p, map, amap, cmap, flags, n_n);
   } else if (tma && p.act == 1) {
     auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true, false, false, true>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
-    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, cmap, flags, n_n);
+    launch(kern, grid, kThreads, L::alloc, stream, p, map, amap, cmap, flags, n_n);
   } else if (tma) {
     auto kern = row_gemm_kernel<BN, S, BK_MAJOR, true, false>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
-    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, cmap, flags, n_n);
+    launch(kern, grid, kThreads, L::alloc, stream, p, map, amap, cmap, flags, n_n);
   } else if (p.act == 1) {
     auto kern = row_gemm_kernel<BN, S, BK_MAJOR, false, false, false, true>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
-    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, cmap, flags, n_n);
+    launch(kern, grid, kThreads, L::alloc, stream, p, map, amap, cmap, flags, n_n);
   } else {
     auto kern = row_gemm_kernel<BN, S, BK_MAJOR, false, false>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
-    kern<<<grid, kThreads, L::alloc, stream>>>(p, map, amap, cmap, flags, n_n);
+    launch(kern, grid, kThreads, L::alloc, stream, p, map, amap, cmap, flags, n_n);
   }
   return check_launch("row_gemm_umma");
 }
@@ -1339,12 +1341,12 @@ static int seg_launch(const SegGemm& p, int64_t max_units, int flags, cudaStream
     auto kern = seg_gemm_kernel<BN, S, W, true>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
-    kern<<<grid, kThreads, L::alloc, stream>>>(p, xmap, gmap, flags, n_m, n_n);
+    launch(kern, grid, kThreads, L::alloc, stream, p, xmap, gmap, flags, n_m, n_n);
   } else {
     auto kern = seg_gemm_kernel<BN, S, W, false>;
     int rc = set_smem(kern, L::alloc);
     if (rc) return rc;
-    kern<<<grid, kThreads, L::alloc, stream>>>(p, xmap, gmap, flags, n_m, n_n);
+    launch(kern, grid, kThreads, L::alloc, stream, p, xmap, gmap, flags, n_m, n_n);
   }
   return check_launch("seg_gemm_umma");
 }

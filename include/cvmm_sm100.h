@@ -52,7 +52,7 @@ typedef struct CUstream_st* cvmm_stream_t; /* == cudaStream_t */
 #define CVMM_DEV_BAD_INDEX 2
 
 /* ABI version of this header; bumped on any signature change. */
-int cvmm_abi_version(void);  /* 6 */
+int cvmm_abi_version(void);  /* 7 */
 
 /* Caps the number of SMs the persistent tensor-core GEMMs launched from now on
  * may occupy (one CTA per SM, nearly all of its shared memory); 0 removes the
@@ -61,6 +61,15 @@ int cvmm_abi_version(void);  /* 6 */
  * kernels, so the collective's CTAs find free SMs instead of waiting for the
  * GEMM to end. No reference counterpart (the reference is single-GPU). */
 int cvmm_set_sm_limit(int n_sms);
+
+/* Turns programmatic dependent launch on (1) or off (0) for the kernels
+ * launched from now on; returns the previous setting. On by default unless the
+ * environment sets CVMM_B200_PDL=0. With it on, each kernel's CTAs may be
+ * scheduled while the previous kernel on the stream drains and wait on the
+ * device for its completion, which hides launch latency and kernel prologues
+ * between the back-to-back kernels of one CVMM call (and in captured graphs).
+ * Results are identical either way. No reference counterpart. */
+int cvmm_set_pdl(int enable);
 
 /* Message for the last failed call on the calling host thread. */
 const char* cvmm_last_error(void);

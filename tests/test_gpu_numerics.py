@@ -274,3 +274,33 @@ def test_shared_head_rows_match_repeated_route_rows(weighted):
         torch.testing.assert_close(a.float(), b.float(), rtol=1e-2, atol=1e-2 * b.float().abs().max().item())
         if name != "x_grad":
             assert torch.equal(a, b), name
+
+
+@pytest.mark.parametrize("route_input,weighted", [(False, False), (True, True)])
+def test_programmatic_launch_matches_plain_launch(route_input, weighted):
+    """Programmatic dependent launch changes only when CTAs are scheduled: the
+    outputs and gradients equal those of plain launches bit for bit (the
+    sel-weight grad, an fp32 atomic sum, to rounding)."""
+    from cvmm_codex_b200 import _lib
+    lib = _lib.load()
+    g = torch.Generator().manual_seed(31)
+    T, k, E, d_in, d_out = 2000, 4, 16, 256, 512
+    x = torch.randn(*((T, k, d_in) if route_input else (T, d_in)), generator=g).bfloat16()
+    keys = torch.randn(E, d_in, d_out, generator=g) / d_in ** 0.5
+    sel = torch.randint(0, E, (T, k), generator=g)
+    w = torch.rand(T, k, generator=g) if weighted else None
+    grad = torch.randn(*((T, d_out) if weighted else (T, k, d_out)), generator=g)
+    res = []
+    prev = lib.cvmm_set_pdl(0)
+    try:
+        for pdl in (0, 1):
+            lib.cvmm_set_pdl(pdl)
+            res.append(run_case(x, keys, sel, w, grad, route_input, torch.bfloat16))
+            torch.cuda.synchronize()
+    finally:
+        lib.cvmm_set_pdl(prev)
+    (o0, gx0, gk0, gw0), (o1, gx1, gk1, gw1) = res
+    for a, b in ((o0, o1), (gx0, gx1), (gk0, gk1)):
+        assert torch.equal(a, b)
+    if weighted:
+        torch.testing.assert_close(gw0, gw1, rtol=1e-5, atol=1e-6)
