@@ -120,6 +120,10 @@ cvmm_sorted_operands = os.environ.get("CVMM_B200_SORTED_OPERANDS", "1").lower() 
 # sorted copy of the token grads (True) instead of gathering and scaling the
 # token grad rows inside the GEMM (False). Both give bit-identical results.
 cvmm_weighted_grad_copy = os.environ.get("CVMM_B200_WEIGHTED_GRAD_COPY", "1").lower() not in ("0", "false", "no", "off")
+# sm_100a engine knob: the unweighted forward writes the sorted padded copy of
+# the x rows it gathers, for the grad-W's dense x tiles (True), or writes none
+# and the grad-W gathers x rows itself (False). Same results either way.
+cvmm_forward_x_copy = os.environ.get("CVMM_B200_FORWARD_X_COPY", "1").lower() not in ("0", "false", "no", "off")
 # Data-parallel hook (None, or an object with grad_keys_ready(grad_keys) and
 # backward_done()): CVMM.backward calls grad_keys_ready on the compute stream
 # as soon as the fp32 expert-weight gradient is written, before the grad-x
@@ -248,7 +252,7 @@ class CVMM(torch.autograd.Function):
             # grouped-x copy, cvmm.py:1123-1138).
             xs, xpad = ops.sort_rows_padded(x, sel_index, rph, sel, offsets, n_experts, dtype=op_dtype)
         a = x if xs is None else xs
-        if reduction_weight is None and _sortable(x, op_dtype):
+        if reduction_weight is None and _sortable(x, op_dtype) and cvmm_forward_x_copy:
             # The forward gathers x's rows anyway: it writes that sorted padded
             # copy for the grad-W as it goes, instead of a separate copy pass.
             # Its pad starts depend only on the offsets; the backward takes them
