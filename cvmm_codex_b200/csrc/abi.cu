@@ -756,9 +756,18 @@ int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_i
   p.chunk = segw_chunk(n_routes, n_experts, m_dim, n_dim, tensor);
   p.units = static_cast<int4*>(ws.tiles);
   p.n_units = ws.count;
+  p.expert_slots = ws.expert_slots;
   p.partials = ws.partials;
-  rc = build_units(offsets, n_experts, p.chunk, static_cast<int4*>(ws.tiles), ws.count, ws.expert_slots, s);
-  if (rc) return rc;
+  // The tensor-core kernel builds a short unit list itself (one launch less);
+  // seg_reduce then reads the expert slots its CTA 0 wrote.
+  const bool own_units = tensor && n_routes > 0 && n_experts <= kOwnUnitExperts &&
+                         max_row_tiles(n_routes, n_experts, (int)p.chunk) <= kOwnUnits;
+  if (own_units) {
+    p.units = nullptr;
+  } else {
+    rc = build_units(offsets, n_experts, p.chunk, static_cast<int4*>(ws.tiles), ws.count, ws.expert_slots, s);
+    if (rc) return rc;
+  }
   // Both operands padded: the GEMM derives every row from its unit and needs
   // no resolved route rows.
   if (tensor && n_routes > 0 && (!(x_pad_start && g_pad_start) || w)) {

@@ -63,8 +63,10 @@ struct SegGemm {
   float* out;
   int op_dtype;
   int64_t chunk;        // routes per work unit (split-K)
-  const int4* units;    // (expert, first sorted position, partial slot or -1, end position)
+  const int4* units;    // (expert, first sorted position, partial slot or -1, end position);
+                        // nullptr: the tensor-core kernel builds the list in shared memory
   const int* n_units;
+  int2* expert_slots;   // written by CTA 0 when the kernel builds its own unit list
   float* partials;      // [slots][M][N] partial sums of split experts
   // Per sorted route, resolved before the GEMM (tensor-core path): x row,
   // grad row (int32) and op-rounded route weight (fp32); padded by
@@ -82,6 +84,10 @@ constexpr int64_t kPadRows = CVMM_PAD_ROWS;
 // Experts up to which the tensor-core row GEMM builds its tile table in the
 // kernel (RowGemm::tiles == nullptr) instead of reading one from build_tiles.
 constexpr int64_t kRowPlanExperts = 1024;
+// The tensor-core grad-W builds its unit list in shared memory (no
+// build_units launch) for at most this many experts and units.
+constexpr int64_t kOwnUnitExperts = 128;
+constexpr int64_t kOwnUnits = 384;
 int pad_starts(const int64_t* offsets, int64_t n_experts, int64_t pad, int* pad_start, cudaStream_t stream);
 int sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64_t* index, int64_t div,
                      const void* scale, int scale_dtype, const int32_t* sorted_sel, const int64_t* offsets,

@@ -86,12 +86,16 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot) {
 // depend on scheduling.
 constexpr int kUnitSortMaxExperts = 1024;
 
-__global__ void __launch_bounds__(1024)
-build_units_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int64_t chunk,
-                   int4* __restrict__ units, int* __restrict__ n_units, int2* __restrict__ expert_slots) {
-  pdl_enter();
-  __shared__ int warp_tot[32];
-  __shared__ int tail_len[kUnitSortMaxExperts];  // each expert's tail chunk length (0: none)
+// Builds the unit list of all experts into `units` (global or shared memory;
+// room for max_row_tiles(n_routes, n_experts, chunk) entries) with every
+// thread of the block, writes expert_slots when non-null, and returns the
+// number of units in every thread. tail_len: n_experts ints of scratch (used
+// up to kUnitSortMaxExperts experts), scratch: 34 ints. Ends with a barrier,
+// so shared-memory units are visible to the whole block on return.
+__device__ __noinline__ int build_unit_list(const int64_t* __restrict__ offsets, int64_t n_experts, int64_t chunk,
+                                            int4* units, int2* __restrict__ expert_slots, int* tail_len,
+                                            int* scratch) {
+  int* warp_tot = scratch;
   const int t = threadIdx.x;
   const int64_t per = (n_experts + blockDim.x - 1) / blockDim.x;
   const int64_t e0 = min((int64_t)t * per, n_experts), e1 = min(e0 + per, n_experts);
@@ -114,14 +118,16 @@ build_units_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int64
   int fpos = block_exclusive_scan(full, warp_tot);
   int tpos = block_exclusive_scan(tails, warp_tot);
   int sbase = block_exclusive_scan(slots, warp_tot);
-  __shared__ int full_total;
-  if (t == blockDim.x - 1) full_total = fpos + full;
+  if (t == blockDim.x - 1) {
+    scratch[32] = fpos + full;
+    scratch[33] = tpos + tails;
+  }
   __syncthreads();
-  const int n_full = full_total;
+  const int n_full = scratch[32], n_total = n_full + scratch[33];
   for (int64_t e = e0; e < e1; ++e) {
     const int64_t b = seg_begin(offsets, e), end = offsets[e];
     const int nch = (int)((end - b + chunk - 1) / chunk);
-    expert_slots[e] = make_int2(nch > 1 ? sbase : -1, nch);
+    if (expert_slots) expert_slots[e] = make_int2(nch > 1 ? sbase : -1, nch);
     int c = 0;
     for (int64_t r = b; r < end; r += chunk, ++c) {
       const int4 u = make_int4((int)e, (int)r, nch > 1 ? sbase + c : -1, (int)min(r + chunk, end));
@@ -140,7 +146,18 @@ build_units_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int64
     }
     if (nch > 1) sbase += nch;
   }
-  if (t == blockDim.x - 1) *n_units = n_full + tpos;
+  __syncthreads();
+  return n_total;
+}
+
+__global__ void __launch_bounds__(1024)
+build_units_kernel(const int64_t* __restrict__ offsets, int64_t n_experts, int64_t chunk,
+                   int4* __restrict__ units, int* __restrict__ n_units, int2* __restrict__ expert_slots) {
+  pdl_enter();
+  __shared__ int scratch[34];
+  __shared__ int tail_len[kUnitSortMaxExperts];  // each expert's tail chunk length (0: none)
+  const int n = build_unit_list(offsets, n_experts, chunk, units, expert_slots, tail_len, scratch);
+  if (threadIdx.x == 0) *n_units = n;
 }
 
 int build_units(const int64_t* offsets, int64_t n_experts, int64_t chunk, int4* units, int* n_units,

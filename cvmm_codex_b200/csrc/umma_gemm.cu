@@ -884,12 +884,23 @@ seg_gemm_kernel(const SegGemm p, const __grid_constant__ CUtensorMap tmap_x, con
   const uint32_t tmem = G_TMA ? setup<BN, S>(bar, 1, WEIGHTED ? kProducers : 32, kTransform)
                               : setup<BN, S>(bar, kProducers);
   pdl_wait();
-  const int total = *p.n_units * per_unit;
+  // Unit list: from build_units, or built here in the (otherwise unused) tile
+  // plan region when the host passes none (few experts and units).
+  int4* own_units = reinterpret_cast<int4*>(smem + L::plan);
+  static_assert(kOwnUnits * 16 + (kOwnUnitExperts + 34) * 4 <= (2 * (kPlanExperts + 1) + 32) * 4,
+                "own unit list exceeds the plan region");
+  const int n_units =
+      p.units ? *p.n_units
+              : build_unit_list(p.offsets, p.n_experts, p.chunk, own_units, blockIdx.x == 0 ? p.expert_slots : nullptr,
+                                reinterpret_cast<int*>(own_units + kOwnUnits),
+                                reinterpret_cast<int*>(own_units + kOwnUnits) + kOwnUnitExperts);
+  const int4* units = p.units ? p.units : own_units;
+  const int total = n_units * per_unit;
   const int op = p.op_dtype;
   const bool x_fast = flags & 1, g_fast = flags & 2, o_vec = flags & 4;
 
   auto entry = [&](int tt) -> int4 {
-    return tt < total ? p.units[tt / per_unit] : make_int4(0, 0, -1, 0);
+    return tt < total ? units[tt / per_unit] : make_int4(0, 0, -1, 0);
   };
   auto nkb_of = [&](const int4& u) -> int { return (int)((u.w - u.y + BK - 1) / BK); };
 
