@@ -504,14 +504,15 @@ def run_ours(args, rank, world, local_rank):
 
 def gemm_bytes(w):
     """Algorithmic HBM bytes of the three GEMMs of one fw+bw step, as the
-    benchmark contract counts them: 16-bit activations and fp32 weights, every
+    benchmark contract counts them: 16-bit activations and fp32 weights (16-bit
+    weights in the bf16_params mode), every
     input read once and every output written once per GEMM (no padding, no
     intermediate copies). For ff_up_1024 each GEMM is 83.9 MB (x 33.5 + W 33.5
     + Y 16.8), 252 MB per step; ff_down_1024_weighted moves 269 MB (its grad-x
     also reads the route rows of x for the sel-weight grad)."""
     R, T, E, di, do = w.R, w.T, w.E, w.d_in, w.d_out
-    act = 2 if w.amp else 4
-    wts = E * di * do * 4
+    act = 2 if (w.amp or w.bf16_params) else 4
+    wts = E * di * do * (2 if w.bf16_params else 4)
     x_rows = w.x_rows                         # unique input rows
     g_rows = T if w.weighted else R           # unique grad rows
     fw = x_rows * di * act + wts + g_rows * do * act + (R * 4 if w.weighted else 0)

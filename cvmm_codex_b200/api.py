@@ -252,6 +252,15 @@ class CVMM(torch.autograd.Function):
             # grouped-x copy, cvmm.py:1123-1138).
             xs, xpad = ops.sort_rows_padded(x, sel_index, rph, sel, offsets, n_experts, dtype=op_dtype)
         a = x if xs is None else xs
+        # fp32 op dtype (no autocast) over 16-bit x and keys (the reference's
+        # bf16_params mode): every product of two 16-bit values is exact in
+        # fp32, so the 16-bit tensor-core GEMM with fp32 accumulation and fp32
+        # output computes the reference's fp32 dot (allow_tf32=False) up to the
+        # order of the fp32 sums, instead of the SIMT fp32 GEMM.
+        fwd_op, fwd_keys = op_dtype, keys_op
+        if (op_dtype == torch.float32 and xs is None and x.dtype == keys.dtype
+                and x.dtype in (torch.bfloat16, torch.float16)):
+            fwd_op, fwd_keys = x.dtype, keys
         if reduction_weight is None and _sortable(x, op_dtype) and cvmm_forward_x_copy:
             # The forward gathers x's rows anyway: it writes that sorted padded
             # copy for the grad-W as it goes, instead of a separate copy pass.
@@ -266,12 +275,12 @@ class CVMM(torch.autograd.Function):
                 # stores); the weighted combine gathers them per token.
                 out_pad = xpad
                 rows = ops.padded_route_rows(out_index if out_index is not None else sel_index, sel, offsets, xpad)
-            y = ops.forward(a, x_index, offsets, keys_op, oi, op_dtype, op_dtype, x_pad_start=xpad,
+            y = ops.forward(a, x_index, offsets, fwd_keys, oi, op_dtype, fwd_op, x_pad_start=xpad,
                             out_pad_start=out_pad)
             res = ops.weighted_combine(y, reduction_weight, op_dtype, y_rows=rows)
             res = res.view(*reduction_weight.shape[:-1], res.shape[-1])
         else:
-            res = ops.forward(a, x_index, offsets, keys_op, oi, op_dtype, op_dtype, x_pad_start=xpad)
+            res = ops.forward(a, x_index, offsets, fwd_keys, oi, op_dtype, fwd_op, x_pad_start=xpad)
             res = res.view(*sel.shape, res.shape[-1])
         ctx.save_for_backward(x, keys_op, raw_sel, sel, sel_index, out_index, reduction_weight, offsets, xs, xpad)
         ctx.op_type = op_dtype

@@ -29,6 +29,7 @@ class Workload:
     amp: bool           # bf16 autocast (False: fp32 throughout)
     skew: str = "bias"  # "none", "bias" (logit bias ~N(0, 0.5)), "zipf", "heads"
     heads: int = 0      # SwitchHead: experts grouped per head
+    bf16_params: bool = False  # everything bf16 without autocast (the reference's bf16_params mode)
 
     @property
     def R(self) -> int:
@@ -66,6 +67,12 @@ WORKLOADS = {
     # stress, d_model 4096, 128 experts of width 512, Zipf(1.1) skew.
     "stress_up_4096_h512": Workload("stress_up_4096_h512", 32768, 4096, 512, 128, 8, False, False, True, "zipf"),
     "stress_down_4096_h512": Workload("stress_down_4096_h512", 32768, 512, 4096, 128, 8, True, True, True, "zipf"),
+    # Parity cases beyond the benchmark list: the reference's lowmem regime
+    # (top-32 of 64 experts, cvmm.py:1228-1338) and its bf16_params mode
+    # (x, keys and grads bf16, no autocast) at the ff_up shape.
+    "top32_up_1024": Workload("top32_up_1024", 4096, 1024, 128, 64, 32, False, False, True, "bias"),
+    "bf16_params_ff_up_1024": Workload("bf16_params_ff_up_1024", 16384, 1024, 128, 64, 4, False, False, False, "bias",
+                                       bf16_params=True),
 }
 
 
@@ -78,7 +85,7 @@ def make_inputs(w: Workload, device="cuda", seed: int = 0, token_slice: Optional
     multi-GPU token sharding uses."""
     dev = torch.device(device)
     g = torch.Generator(device=dev).manual_seed(seed)
-    act = torch.bfloat16 if w.amp else torch.float32
+    act = torch.bfloat16 if (w.amp or w.bf16_params) else torch.float32
     T = w.T
     x_shape = (T, w.k, w.d_in) if w.route_input else (T, w.d_in)
     if w.skew == "heads":
@@ -124,7 +131,7 @@ def make_inputs(w: Workload, device="cuda", seed: int = 0, token_slice: Optional
         weights = None if weights is None else weights[token_slice]
     return {
         "x": x.to(act).contiguous(),
-        "keys": keys.contiguous(),
+        "keys": (keys.bfloat16() if w.bf16_params else keys).contiguous(),
         "sel": sel.contiguous(),
         "weights": None if weights is None else weights.float().contiguous(),
         "grad_out": grad_out.to(act).contiguous(),

@@ -19,7 +19,7 @@ from cvmm_codex_b200.workloads import WORKLOADS, make_inputs
 pytestmark = pytest.mark.gpu
 
 CONFIGS = ["cpu_plumbing", "ff_up_1024", "ff_down_1024_weighted", "switch_o_2048_h32_weighted",
-           "stress_up_4096_h512", "stress_down_4096_h512"]
+           "stress_up_4096_h512", "stress_down_4096_h512", "top32_up_1024", "bf16_params_ff_up_1024"]
 
 
 def run(w, d, scale=1.0):
@@ -43,7 +43,7 @@ def route_rows(w, t):
 def fp64_reference(w, d):
     """FP64 per-expert evaluation on the GPU of the reference's math
     (cvmm.py:1524-1755) with the reference's operand rounding."""
-    rnd = (lambda t: t.bfloat16().double()) if w.amp else (lambda t: t.float().double())
+    rnd = (lambda t: t.bfloat16().double()) if (w.amp or w.bf16_params) else (lambda t: t.float().double())
     xr = rnd(route_rows(w, d["x"]))
     kr = rnd(d["keys"])
     sel = d["sel"].reshape(-1)
@@ -96,7 +96,7 @@ def test_config_against_fp64(name):
     d = make_inputs(w, "cuda", seed=0)
     got = run(w, d)
     want = fp64_reference(w, d)
-    tol = 2e-2 if w.amp else 1e-3  # BF16-AMP 2e-2, FP32 paths 1e-3
+    tol = 2e-2 if (w.amp or w.bf16_params) else 1e-3  # BF16 2e-2, FP32 paths 1e-3
     names = ("out", "grad_x", "grad_keys", "grad_w")
     for nm, a, e in zip(names, got, want):
         if e is None:
