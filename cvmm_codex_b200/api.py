@@ -124,6 +124,10 @@ cvmm_weighted_grad_copy = os.environ.get("CVMM_B200_WEIGHTED_GRAD_COPY", "1").lo
 # the x rows it gathers, for the grad-W's dense x tiles (True), or writes none
 # and the grad-W gathers x rows itself (False). Same results either way.
 cvmm_forward_x_copy = os.environ.get("CVMM_B200_FORWARD_X_COPY", "1").lower() not in ("0", "false", "no", "off")
+# sm_100a engine knob: in the bf16_params mode (bf16 x and keys, no autocast)
+# the unweighted backward runs on the bf16 tensor cores with the fp32 grad
+# split into two bf16 parts (True) instead of the fp32 SIMT GEMMs (False).
+cvmm_split_fp32_grad = os.environ.get("CVMM_B200_SPLIT_FP32_GRAD", "1").lower() not in ("0", "false", "no", "off")
 # Data-parallel hook (None, or an object with grad_keys_ready(grad_keys) and
 # backward_done()): CVMM.backward calls grad_keys_ready on the compute stream
 # as soon as the fp32 expert-weight gradient is written, before the grad-x
@@ -261,12 +265,16 @@ class CVMM(torch.autograd.Function):
         if (op_dtype == torch.float32 and xs is None and x.dtype == keys.dtype
                 and x.dtype in (torch.bfloat16, torch.float16)):
             fwd_op, fwd_keys = x.dtype, keys
-        if reduction_weight is None and _sortable(x, op_dtype) and cvmm_forward_x_copy:
+        # The bf16_params backward (_split_bf16_backward) reads the same sorted
+        # x copy as the autocast path.
+        split_copy = (fwd_op == torch.bfloat16 and op_dtype == torch.float32 and cvmm_split_fp32_grad
+                      and reduction_weight is None and _sortable(x, fwd_op) and cvmm_forward_x_copy)
+        if reduction_weight is None and ((_sortable(x, op_dtype) and cvmm_forward_x_copy) or split_copy):
             # The forward gathers x's rows anyway: it writes that sorted padded
             # copy for the grad-W as it goes, instead of a separate copy pass.
             # Its pad starts depend only on the offsets; the backward takes them
             # from the grad copy it makes anyway.
-            res, xs = ops.forward(x, x_index, offsets, keys_op, oi, op_dtype, op_dtype, x_copy=True)
+            res, xs = ops.forward(x, x_index, offsets, fwd_keys, oi, op_dtype, fwd_op, x_copy=True)
             res = res.view(*sel.shape, res.shape[-1])
         elif reduction_weight is not None:
             rows = out_pad = None
@@ -296,6 +304,54 @@ class CVMM(torch.autograd.Function):
         return _cvmm_backward(ctx, ctx.saved_tensors, grad_output)
 
 
+def _split_bf16_backward(ctx, x, keys_op, sel, sel_index, route, offsets, g, need_x, need_keys, n_routes, rph,
+                         xs=None):
+    """Unweighted backward of the bf16_params mode (bf16 x and keys, no
+    autocast: fp32 op dtype, fp32 output grad) on the bf16 tensor cores.
+
+    x and keys hold bf16 values; the fp32 grad is split as g = hi + lo with hi =
+    bf16(g) and lo = bf16(g - hi) (g - hi is exact in fp32, lo keeps its next 8
+    mantissa bits, a residual below 2^-16 |g|). Every product of two bf16
+    values is exact in fp32, so grad-W = x^T [hi | lo] (one GEMM over 2 d_out
+    columns, the halves summed in fp32) and grad-x = [hi | lo] [W | W]^T (one
+    GEMM over 2 d_out of K) are the reference's fp32 results (cvmm.py:1141-1225,
+    allow_tf32=False) up to fp32 summation order and that residual."""
+    n_experts, _, d_out = keys_op.shape
+    g2 = g.reshape(n_routes, d_out)
+    hi = g2.to(torch.bfloat16)
+    lo = (g2 - hi.float()).to(torch.bfloat16)
+    gcat = torch.cat([hi, lo], dim=1)
+    # One expert-padded sorted copy of [hi | lo] feeds both GEMMs dense TMA tiles.
+    bf = torch.bfloat16
+    gs, gpad = ops.sort_rows_padded(gcat, route, 1, sel, offsets, n_experts, dtype=bf)
+    grad_x = grad_keys = None
+    if need_keys:
+        if xs is not None:  # the forward's sorted x copy: both operands dense
+            gw = ops.backward_w(xs, None, 1, gs, None, 1, offsets, n_experts, bf, g_pad_start=gpad,
+                                x_pad_start=gpad, n_routes=n_routes)
+        else:
+            gw = ops.backward_w(x, sel_index, rph, gs, None, 1, offsets, n_experts, bf, g_pad_start=gpad)
+        grad_keys = (gw[..., :d_out] + gw[..., d_out:]).to(ctx.keys_type)
+    if need_x:
+        kh = keys_op.to(bf)
+        kcat = torch.cat([kh, kh], dim=-1)
+        x_rows = x.reshape(-1, x.shape[-1]).shape[0]
+        if x_rows == n_routes:
+            grad_x = ops.backward_x(gs, None, 1, route, offsets, kcat, x.dtype, bf, g_pad_start=gpad).view_as(x)
+        else:
+            gxs = ops.backward_x(gs, None, 1, None, offsets, kcat, x.dtype, bf, g_pad_start=gpad,
+                                 out_pad_start=gpad, n_routes=n_routes)
+            rows = ops.padded_route_rows(route, sel, offsets, gpad)
+            grad_x = ops.sum_routes(gxs, n_routes // x_rows, x.dtype, src_rows=rows).view_as(x)
+    if cvmm_backward_hook is not None:
+        if grad_keys is not None:
+            cvmm_backward_hook.grad_keys_ready(grad_keys)
+        cvmm_backward_hook.backward_done()
+    if cvmm_check_device_status:
+        _raise_on_device_status("CVMM.backward")
+    return grad_x, None, None, None, grad_keys, None, None
+
+
 def _cvmm_backward(ctx, saved, grad_output):
     """CVMM.backward on the tensors saved by the forward (shared with CVMMGelu)."""
     x, keys_op, raw_sel, sel, sel_index, out_index, w, offsets, xs, xpad = saved
@@ -315,6 +371,12 @@ def _cvmm_backward(ctx, saved, grad_output):
     x_rows = x.reshape(-1, x.shape[-1]).shape[0]
 
     grad_x = grad_keys = grad_w = None
+    if (w is None and op == torch.float32 and x.dtype == torch.bfloat16 and ctx.keys_type == torch.bfloat16
+            and g.dtype == torch.float32 and cvmm_split_fp32_grad):
+        return _split_bf16_backward(ctx, x, keys_op, sel, sel_index, route, offsets, g, need_x, need_keys,
+                                    n_routes, rph, xs)
+    if op == torch.float32:
+        xs = xpad = None  # a 16-bit x copy only feeds the bf16 split path
     if w is None:
         g2 = g.reshape(n_routes, g.shape[-1])
         g_rows, g_idx, g_pad = g2, route, None

@@ -304,3 +304,34 @@ def test_programmatic_launch_matches_plain_launch(route_input, weighted):
         assert torch.equal(a, b)
     if weighted:
         torch.testing.assert_close(gw0, gw1, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("route_input", [False, True])
+def test_bf16_params_split_backward_matches_fp32_kernels(route_input, monkeypatch):
+    """bf16 x and keys without autocast (the reference's bf16_params mode, fp32
+    op dtype): the backward on the bf16 tensor cores with the fp32 grad split
+    into two bf16 parts agrees with the fp32 SIMT kernels and with the fp64
+    oracle (bf16 leaf grads: the bf16 bound)."""
+    from cvmm_codex_b200 import api
+    g = torch.Generator().manual_seed(41)
+    T, k, E, d_in, d_out = 700, 4, 12, 256, 192
+    x = torch.randn(*((T, k, d_in) if route_input else (T, d_in)), generator=g).bfloat16()
+    keys = (torch.randn(E, d_in, d_out, generator=g) / d_in ** 0.5).bfloat16()
+    sel = torch.randint(0, E, (T, k), generator=g)
+    grad = torch.randn(T, k, d_out, generator=g)
+    res = {}
+    for split in (True, False):
+        monkeypatch.setattr(api, "cvmm_split_fp32_grad", split)
+        res[split] = run_case(x, keys, sel, None, grad, route_input, None)
+    for a, b in zip(res[True], res[False]):
+        if a is None:
+            continue
+        assert a.dtype == b.dtype and a.shape == b.shape
+        assert O.rel_max_err(_np(a), _np(b)) < 1e-2
+    out, gx, gk, _ = res[True]
+    assert out.dtype == torch.float32 and gx.dtype == torch.bfloat16 and gk.dtype == torch.bfloat16
+    eo = O.forward(_np(x), sel.numpy(), _np(keys), None, op="float32")
+    ex, ek, _ = O.backward(_np(x), sel.numpy(), _np(keys), _np(grad), None, op="float32")
+    for name, a, e in (("out", out, eo), ("x_grad", gx, ex), ("keys_grad", gk, ek)):
+        assert O.rel_max_err(_np(a), e) <= MAX_TOL["bfloat16"], name
+        assert O.rel_rms_err(_np(a), e) <= RMS_TOL["bfloat16"], name
