@@ -37,6 +37,7 @@ SIGNATURES = {
     "cvmm_last_error": (ctypes.c_char_p, []),
     "cvmm_set_sm_limit": (_I, [_I]),
     "cvmm_set_pdl": (_I, [_I]),
+    "cvmm_backward_w_launches": (_I, [_L, _L, _L, _L, _I, _I, _I]),
     "cvmm_device_status": (_I, [_I, ctypes.POINTER(_I), ctypes.POINTER(ctypes.c_longlong), _P]),
     "cvmm_sel_prepare_workspace_size": (_S, [_L]),
     "cvmm_sel_prepare": (_I, [_P, _I, _L, _L, _I, _P, _P, _P, _P, _P, _S, _P]),
@@ -88,7 +89,7 @@ def load():
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if lib.cvmm_abi_version() != 7:
+        if lib.cvmm_abi_version() != 8:
             raise CvmmLibraryError("libcvmm_sm100.so ABI version mismatch; rebuild it")
         _lib = lib
     return _lib

@@ -482,7 +482,7 @@ using namespace cvmm;
 // ================================================================== C ABI
 extern "C" {
 
-int cvmm_abi_version(void) { return 7; }
+int cvmm_abi_version(void) { return 8; }
 
 int cvmm_set_pdl(int enable) {
   const int prev = pdl_enabled() ? 1 : 0;
@@ -791,6 +791,16 @@ int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_i
   // Sums split experts' partial slots in chunk order and zero-fills experts
   // without routes (the reference writes 0 for them, cvmm.py:476-478).
   return seg_reduce(ws.expert_slots, ws.partials, grad_w, n_experts, m_dim * n_dim, s);
+}
+
+int cvmm_backward_w_launches(int64_t n_routes, int64_t n_experts, int64_t m_dim, int64_t n_dim, int op_dtype,
+                             int both_padded, int weighted) {
+  const bool tensor = op_dtype != F32;
+  if (n_routes <= 0) return 2;  // unit list + reduction (zero fill)
+  const int64_t chunk = segw_chunk(n_routes, n_experts, m_dim, n_dim, tensor);
+  const bool own_units = tensor && n_experts <= kOwnUnitExperts && max_row_tiles(n_routes, n_experts, (int)chunk) <= kOwnUnits;
+  const bool resolve = tensor && (!both_padded || weighted);
+  return (own_units ? 0 : 1) + (resolve ? 1 : 0) + 1 + 1;
 }
 
 int cvmm_pad_starts(const int64_t* offsets, int64_t n_experts, int32_t* pad_start, cvmm_stream_t stream) {

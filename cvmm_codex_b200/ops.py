@@ -300,7 +300,9 @@ def backward_w(x: torch.Tensor, x_index: torch.Tensor, x_div: int, g: torch.Tens
                                  ptr(w2), dtype_code(w2.dtype) if w2 is not None else 0, ptr(w_index),
                                  ptr(offsets), n_routes, int(n_experts), M, N, ptr(out),
                                  dtype_code(op_dtype), ptr(x_pad_start), ptr(g_pad_start), ptr(ws), ws.numel(),
-                                 stream, kernels=3 if (x_pad_start is not None and g_pad_start is not None) else 4)
+                                 stream, kernels=lib.cvmm_backward_w_launches(
+                                     n_routes, int(n_experts), M, N, dtype_code(op_dtype),
+                                     int(x_pad_start is not None and g_pad_start is not None), int(w2 is not None)))
     check(rc, "cvmm_backward_w")
     return out
 

@@ -52,7 +52,7 @@ typedef struct CUstream_st* cvmm_stream_t; /* == cudaStream_t */
 #define CVMM_DEV_BAD_INDEX 2
 
 /* ABI version of this header; bumped on any signature change. */
-int cvmm_abi_version(void);  /* 7 */
+int cvmm_abi_version(void);  /* 8 */
 
 /* Caps the number of SMs the persistent tensor-core GEMMs launched from now on
  * may occupy (one CTA per SM, nearly all of its shared memory); 0 removes the
@@ -266,6 +266,12 @@ int cvmm_backward_w(const void* x, int x_dtype, int64_t x_ld, const int64_t* x_i
                     int64_t n_experts, int64_t m_dim, int64_t n_dim, float* grad_w,
                     int op_dtype, const int32_t* x_pad_start, const int32_t* g_pad_start,
                     void* workspace, size_t workspace_bytes, cvmm_stream_t stream);
+/* Kernels one cvmm_backward_w call with these arguments launches (for launch
+ * accounting): the unit-list build (unless the tensor-core GEMM builds it in
+ * shared memory), the route-row resolve (unless both operands are padded and
+ * unweighted), the GEMM and the split-K reduction. No reference counterpart. */
+int cvmm_backward_w_launches(int64_t n_routes, int64_t n_experts, int64_t m_dim, int64_t n_dim, int op_dtype,
+                             int both_padded, int weighted);
 
 /* ------------------------------------------------------------------------
  * Expert-padded sorted copy of route rows. Replaces the reference's grouping
