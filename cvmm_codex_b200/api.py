@@ -124,6 +124,10 @@ cvmm_weighted_grad_copy = os.environ.get("CVMM_B200_WEIGHTED_GRAD_COPY", "1").lo
 # the x rows it gathers, for the grad-W's dense x tiles (True), or writes none
 # and the grad-W gathers x rows itself (False). Same results either way.
 cvmm_forward_x_copy = os.environ.get("CVMM_B200_FORWARD_X_COPY", "1").lower() not in ("0", "false", "no", "off")
+# sm_100a engine knob: the unweighted forward makes the sorted x copy in a separate
+# copy pass (warp-per-row gathers) and then reads it as dense tiles (True), instead
+# of writing it from its own cp.async gathers (False). Same results either way.
+cvmm_forward_sort_first = os.environ.get("CVMM_B200_FORWARD_SORT_FIRST", "0").lower() in ("1", "true", "yes", "on")
 # sm_100a engine knob: in the bf16_params mode (bf16 x and keys, no autocast)
 # the unweighted backward runs on the bf16 tensor cores with the fp32 grad
 # split into two bf16 parts (True) instead of the fp32 SIMT GEMMs (False).
@@ -269,7 +273,14 @@ class CVMM(torch.autograd.Function):
         # x copy as the autocast path.
         split_copy = (fwd_op == torch.bfloat16 and op_dtype == torch.float32 and cvmm_split_fp32_grad
                       and reduction_weight is None and _sortable(x, fwd_op) and cvmm_forward_x_copy)
-        if reduction_weight is None and ((_sortable(x, op_dtype) and cvmm_forward_x_copy) or split_copy):
+        if (reduction_weight is None and cvmm_forward_sort_first and cvmm_forward_x_copy
+                and _sortable(x, op_dtype) and fwd_op == op_dtype):
+            # Copy pass first (warp-per-row gathers), then the forward over
+            # dense A tiles of that copy; the backward reads the same copy.
+            xs, xpad = ops.sort_rows_padded(x, sel_index, rph, sel, offsets, n_experts, dtype=op_dtype)
+            res = ops.forward(xs, x_index, offsets, fwd_keys, oi, op_dtype, fwd_op, x_pad_start=xpad)
+            res = res.view(*sel.shape, res.shape[-1])
+        elif reduction_weight is None and ((_sortable(x, op_dtype) and cvmm_forward_x_copy) or split_copy):
             # The forward gathers x's rows anyway: it writes that sorted padded
             # copy for the grad-W as it goes, instead of a separate copy pass.
             # Its pad starts depend only on the offsets; the backward takes them
