@@ -636,10 +636,15 @@ def call_work(w, name):
         return 0.0, 0.0, float(R * 4 + E * 8)
     if name == "cvmm_cast":
         return 0.0, 0.0, float(wts * (4 + 2))
-    if name == "cvmm_sort_rows_padded":
+    if name in ("cvmm_sort_rows_padded", "cvmm_sort_rows_padded_ex"):
+        # weighted steps: the forward's x copy (plain call) and the grad copy
+        # (_ex, pad starts reused); unweighted: the grad copy, with the route
+        # row map (_ex) when the k-sum follows.
         x_copy = w.x_rows * di * 2 + R * di * 2
         g_copy = (T * do * 2 + R * 4 if w.weighted else R * do * 2) + R * do * 2
-        return 0.0, 0.0, float((x_copy + g_copy) / 2 if w.weighted else g_copy)
+        if w.weighted:
+            return 0.0, 0.0, float(x_copy if name == "cvmm_sort_rows_padded" else g_copy)
+        return 0.0, 0.0, float(g_copy + (R * 4 if name == "cvmm_sort_rows_padded_ex" else 0))
     if name == "cvmm_pad_starts":
         return 0.0, 0.0, float(E * 12)
     if name == "cvmm_padded_route_rows":

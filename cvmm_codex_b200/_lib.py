@@ -52,6 +52,7 @@ SIGNATURES = {
     "cvmm_backward_w": (_I, [_P, _I, _L, _P, _L, _P, _I, _L, _P, _L, _P, _I, _P, _P, _L, _L,
                              _L, _L, _P, _I, _P, _P, _P, _S, _P]),
     "cvmm_sort_rows_padded": (_I, [_P, _I, _L, _P, _L, _P, _I, _P, _P, _L, _L, _L, _P, _I, _P, _P]),
+    "cvmm_sort_rows_padded_ex": (_I, [_P, _I, _L, _P, _L, _P, _I, _P, _P, _L, _L, _L, _P, _I, _P, _I, _P, _P]),
     "cvmm_sum_routes": (_I, [_P, _I, _P, _I, _L, _L, _L, _P, _P]),
     "cvmm_pad_starts": (_I, [_P, _L, _P, _P]),
     "cvmm_padded_route_rows": (_I, [_P, _P, _P, _P, _L, _L, _P, _P]),
@@ -89,7 +90,7 @@ def load():
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if lib.cvmm_abi_version() != 8:
+        if lib.cvmm_abi_version() != 9:
             raise CvmmLibraryError("libcvmm_sm100.so ABI version mismatch; rebuild it")
         _lib = lib
     return _lib

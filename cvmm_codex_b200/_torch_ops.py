@@ -90,6 +90,22 @@ def _(src, index, div, sorted_sel, offsets, n_experts, dtype, scale):
             src.new_empty((n_experts,), dtype=torch.int32))
 
 
+@torch.library.custom_op("cvmm_b200::sort_rows_padded_rows", mutates_args=())
+def sort_rows_padded_rows(src: torch.Tensor, index: torch.Tensor, div: int, sorted_sel: torch.Tensor,
+                          offsets: torch.Tensor, n_experts: int, dtype: Optional[torch.dtype],
+                          scale: Optional[torch.Tensor]) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    return ops.sort_rows_padded(src, index, div, sorted_sel, offsets, n_experts, dtype=dtype, scale=scale,
+                                route_rows=True)
+
+
+@sort_rows_padded_rows.register_fake
+def _(src, index, div, sorted_sel, offsets, n_experts, dtype, scale):
+    dt = src.dtype if dtype is None else dtype
+    return (src.new_empty((index.numel() + n_experts * PAD, src.shape[-1]), dtype=dt),
+            src.new_empty((n_experts,), dtype=torch.int32),
+            src.new_empty((index.numel(),), dtype=torch.int32))
+
+
 @torch.library.custom_op("cvmm_b200::padded_route_rows", mutates_args=())
 def padded_route_rows(route: torch.Tensor, sorted_sel: torch.Tensor, offsets: torch.Tensor,
                       pad_start: torch.Tensor) -> torch.Tensor:
@@ -298,10 +314,17 @@ class _Calls:
             return torch.ops.cvmm_b200.cast(src, dtype)
         return ops.cast(src, dtype)
 
-    def sort_rows_padded(self, src, index, div, sorted_sel, offsets, n_experts, dtype=None, scale=None):
+    def sort_rows_padded(self, src, index, div, sorted_sel, offsets, n_experts, dtype=None, scale=None,
+                         route_rows=False, pad_start=None):
         if self._tracing():
+            # A custom op may not return its input, so traced graphs recompute
+            # the pad starts instead of reusing pad_start.
+            if route_rows:
+                return torch.ops.cvmm_b200.sort_rows_padded_rows(src, index, div, sorted_sel, offsets, n_experts,
+                                                                 dtype, scale)
             return torch.ops.cvmm_b200.sort_rows_padded(src, index, div, sorted_sel, offsets, n_experts, dtype, scale)
-        return ops.sort_rows_padded(src, index, div, sorted_sel, offsets, n_experts, dtype=dtype, scale=scale)
+        return ops.sort_rows_padded(src, index, div, sorted_sel, offsets, n_experts, dtype=dtype, scale=scale,
+                                    route_rows=route_rows, pad_start=pad_start)
 
     def padded_route_rows(self, route, sorted_sel, offsets, pad_start):
         if self._tracing():

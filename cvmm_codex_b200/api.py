@@ -390,12 +390,17 @@ def _cvmm_backward(ctx, saved, grad_output):
         xs = xpad = None  # a 16-bit x copy only feeds the bf16 split path
     if w is None:
         g2 = g.reshape(n_routes, g.shape[-1])
-        g_rows, g_idx, g_pad = g2, route, None
+        g_rows, g_idx, g_pad, g_route_rows = g2, route, None, None
         if _sortable(g2, op):
             # One expert-padded sorted copy of the route grads (the
             # reference's grouping copy, cvmm.py:1161) lets both GEMMs read
             # them as dense tensor-core tiles.
-            g_rows, g_pad = ops.sort_rows_padded(g2, route, 1, sel, offsets, n_experts, dtype=op)
+            if need_x and x_rows != n_routes and x.dtype == op and x.shape[-1] % 8 == 0:
+                # The copy also writes the route -> padded row map the k-sum reads.
+                g_rows, g_pad, g_route_rows = ops.sort_rows_padded(g2, route, 1, sel, offsets, n_experts, dtype=op,
+                                                                   route_rows=True, pad_start=xpad)
+            else:
+                g_rows, g_pad = ops.sort_rows_padded(g2, route, 1, sel, offsets, n_experts, dtype=op, pad_start=xpad)
             g_idx = None
         if xs is not None and xpad is None:
             xpad = g_pad if g_pad is not None else ops.pad_starts(offsets, n_experts)
@@ -419,7 +424,7 @@ def _cvmm_backward(ctx, saved, grad_output):
                 # tile stores); the k-sum gathers them per token.
                 gxs = ops.backward_x(g_rows, None, 1, None, offsets, keys_op, x.dtype, op, g_pad_start=g_pad,
                                      out_pad_start=g_pad, n_routes=n_routes)
-                rows = ops.padded_route_rows(route, sel, offsets, g_pad)
+                rows = g_route_rows if g_route_rows is not None else ops.padded_route_rows(route, sel, offsets, g_pad)
                 grad_x = ops.sum_routes(gxs, n_routes // x_rows, x.dtype, src_rows=rows).view_as(x)
             else:
                 gxr = ops.backward_x(g_rows, g_idx, 1, route, offsets, keys_op, x.dtype, op, g_pad_start=g_pad)
@@ -434,12 +439,14 @@ def _cvmm_backward(ctx, saved, grad_output):
                 # One unscaled expert-padded sorted copy of the token grads feeds
                 # both GEMMs as dense TMA boxes: grad-W applies op(op(g) op(w))
                 # in shared memory (cvmm.py:591-599), grad-x reads it as A.
-                gs, gpad = ops.sort_rows_padded(gt, route, k, sel, offsets, n_experts, dtype=op)
+                gs, gpad = ops.sort_rows_padded(gt, route, k, sel, offsets, n_experts, dtype=op, pad_start=xpad)
                 grad_keys = ops.backward_w(xs, None, 1, gs, None, 1, offsets, n_experts, op, w=w,
                                            w_index=route, g_pad_start=gpad, x_pad_start=xpad, n_routes=n_routes)
             elif xs is not None and _sortable(gt, op) and cvmm_weighted_grad_copy:
                 # The weight product is applied (and rounded) in a sorted copy.
-                gs, gpad = ops.sort_rows_padded(gt, route, k, sel, offsets, n_experts, dtype=op, scale=w)
+                # Same offsets as the forward's x copy: its pad starts are reused.
+                gs, gpad = ops.sort_rows_padded(gt, route, k, sel, offsets, n_experts, dtype=op, scale=w,
+                                                pad_start=xpad)
                 grad_keys = ops.backward_w(xs, None, 1, gs, None, 1, offsets, n_experts, op,
                                            g_pad_start=gpad, x_pad_start=xpad, n_routes=n_routes)
                 gs = None  # weight-scaled: not the operand grad-x needs

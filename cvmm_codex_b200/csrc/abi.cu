@@ -362,19 +362,35 @@ __global__ void cast_kernel(const void* __restrict__ src, int s_dtype, void* __r
     store_from_float(dst, d_dtype, i, load_as_float(src, s_dtype, i));
 }
 
-// fp32 -> bf16/fp16, 8 elements per thread with 32-byte loads / 16-byte stores.
+// fp32 -> bf16/fp16, two groups of 8 elements per thread (a block's groups
+// are blockDim.x apart, so every warp access stays coalesced): four 16-byte
+// loads in flight per thread before the two 16-byte stores.
 __global__ void cast_f32_to_16_vec(const float4* __restrict__ src, uint4* __restrict__ dst,
                                    int d_dtype, int64_t n8) {
   pdl_enter();
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8;
-       i += (int64_t)gridDim.x * blockDim.x) {
+  for (int64_t i = blockIdx.x * 2 * (int64_t)blockDim.x + threadIdx.x; i < n8;
+       i += (int64_t)gridDim.x * 2 * blockDim.x) {
+    const int64_t j = i + blockDim.x;
+    const bool two = j < n8;
     const float4 a = src[2 * i], b = src[2 * i + 1];
+    float4 c = a, d = b;
+    if (two) {
+      c = src[2 * j];
+      d = src[2 * j + 1];
+    }
     uint4 o;
     o.x = pack2(a.x, a.y, d_dtype);
     o.y = pack2(a.z, a.w, d_dtype);
     o.z = pack2(b.x, b.y, d_dtype);
     o.w = pack2(b.z, b.w, d_dtype);
     dst[i] = o;
+    if (two) {
+      o.x = pack2(c.x, c.y, d_dtype);
+      o.y = pack2(c.z, c.w, d_dtype);
+      o.z = pack2(d.x, d.y, d_dtype);
+      o.w = pack2(d.z, d.w, d_dtype);
+      dst[j] = o;
+    }
   }
 }
 
@@ -482,7 +498,7 @@ using namespace cvmm;
 // ================================================================== C ABI
 extern "C" {
 
-int cvmm_abi_version(void) { return 8; }
+int cvmm_abi_version(void) { return 9; }
 
 int cvmm_set_pdl(int enable) {
   const int prev = pdl_enabled() ? 1 : 0;
@@ -809,10 +825,11 @@ int cvmm_pad_starts(const int64_t* offsets, int64_t n_experts, int32_t* pad_star
                     reinterpret_cast<cudaStream_t>(stream));
 }
 
-int cvmm_sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64_t* index, int64_t div,
+static int sort_rows_padded_abi(const void* src, int src_dtype, int64_t src_ld, const int64_t* index, int64_t div,
                           const void* scale, int scale_dtype, const int32_t* sorted_sel, const int64_t* offsets,
                           int64_t n_routes, int64_t n_experts, int64_t cols, void* dst, int dst_dtype,
-                          int32_t* pad_start, cvmm_stream_t stream) {
+                          int32_t* pad_start, bool pad_ready, int32_t* route_rows,
+                                cvmm_stream_t stream) {
   if (!is_float_dtype(src_dtype) || !is_float_dtype(dst_dtype) || (scale && !is_float_dtype(scale_dtype)))
     return fail(CVMM_ERR_UNSUPPORTED_DTYPE, "cvmm_sort_rows_padded: unsupported dtype");
   if (n_routes < 0 || n_experts <= 0 || cols <= 0 || div <= 0 || src_ld < cols ||
@@ -821,10 +838,27 @@ int cvmm_sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const 
   if (!dst || !pad_start || !offsets || (n_routes > 0 && (!src || !index || !sorted_sel)))
     return fail(CVMM_ERR_INVALID_ARG, "cvmm_sort_rows_padded: null pointer");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  int rc = pad_starts(offsets, n_experts, kPadRows, reinterpret_cast<int*>(pad_start), s);
+  int rc = pad_ready ? 0 : pad_starts(offsets, n_experts, kPadRows, reinterpret_cast<int*>(pad_start), s);
   if (rc || n_routes == 0) return rc;
   return sort_rows_padded(src, src_dtype, src_ld, index, div, scale, scale_dtype, sorted_sel, offsets,
-                          reinterpret_cast<int*>(pad_start), n_routes, n_experts, cols, dst, dst_dtype, s);
+                          reinterpret_cast<int*>(pad_start), n_routes, n_experts, cols, dst, dst_dtype, s,
+                          route_rows);
+}
+
+int cvmm_sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64_t* index, int64_t div,
+                          const void* scale, int scale_dtype, const int32_t* sorted_sel, const int64_t* offsets,
+                          int64_t n_routes, int64_t n_experts, int64_t cols, void* dst, int dst_dtype,
+                          int32_t* pad_start, cvmm_stream_t stream) {
+  return sort_rows_padded_abi(src, src_dtype, src_ld, index, div, scale, scale_dtype, sorted_sel, offsets, n_routes,
+                              n_experts, cols, dst, dst_dtype, pad_start, false, nullptr, stream);
+}
+
+int cvmm_sort_rows_padded_ex(const void* src, int src_dtype, int64_t src_ld, const int64_t* index, int64_t div,
+                             const void* scale, int scale_dtype, const int32_t* sorted_sel, const int64_t* offsets,
+                             int64_t n_routes, int64_t n_experts, int64_t cols, void* dst, int dst_dtype,
+                             int32_t* pad_start, int pad_start_ready, int32_t* route_rows, cvmm_stream_t stream) {
+  return sort_rows_padded_abi(src, src_dtype, src_ld, index, div, scale, scale_dtype, sorted_sel, offsets, n_routes,
+                              n_experts, cols, dst, dst_dtype, pad_start, pad_start_ready != 0, route_rows, stream);
 }
 
 int cvmm_weighted_token_backward(const void* route_grad, int rg_dtype, const void* w, int w_dtype,
@@ -853,7 +887,7 @@ int cvmm_cast(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t 
   if (!src || !dst) return fail(CVMM_ERR_INVALID_ARG, "cvmm_cast: null pointer");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (src_dtype == F32 && dst_dtype != F32 && n % 8 == 0 && al16(src) && al16(dst)) {
-    launch(cast_f32_to_16_vec, grid_for(n / 8, 256), 256, 0, s, static_cast<const float4*>(src),
+    launch(cast_f32_to_16_vec, grid_for((n / 8 + 1) / 2, 256), 256, 0, s, static_cast<const float4*>(src),
                                                             static_cast<uint4*>(dst), dst_dtype, n / 8);
   } else {
     launch(cast_kernel, grid_for(n, 256), 256, 0, s, src, src_dtype, dst, dst_dtype, n);

@@ -92,7 +92,7 @@ int pad_starts(const int64_t* offsets, int64_t n_experts, int64_t pad, int* pad_
 int sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64_t* index, int64_t div,
                      const void* scale, int scale_dtype, const int32_t* sorted_sel, const int64_t* offsets,
                      const int* pad_start, int64_t n_routes, int64_t n_experts, int64_t cols, void* dst,
-                     int dst_dtype, cudaStream_t stream);
+                     int dst_dtype, cudaStream_t stream, int32_t* route_rows = nullptr);
 int resolve_route_rows(const SegGemm& p, int* xrow, int* grow, float* wsc, cudaStream_t stream);
 
 __device__ __forceinline__ int64_t seg_begin(const int64_t* offsets, int64_t e) {

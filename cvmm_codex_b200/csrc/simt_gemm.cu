@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(256) sort_rows_padded_kernel(
     const char* __restrict__ src, int src_dtype, int64_t src_ld, const int64_t* __restrict__ index, int64_t div,
     const void* __restrict__ scale, int scale_dtype, const int32_t* __restrict__ sorted_sel,
     const int64_t* __restrict__ offsets, const int* __restrict__ pad_start, int64_t n_routes, int64_t n_experts,
-    int64_t cols, char* __restrict__ dst, int dst_dtype) {
+    int64_t cols, char* __restrict__ dst, int dst_dtype, int32_t* __restrict__ route_rows) {
   pdl_enter();
   __shared__ SortRowMeta meta[ROWS];
   const int tid = threadIdx.x, lane = tid & 31;
@@ -294,7 +294,9 @@ __global__ void __launch_bounds__(256) sort_rows_padded_kernel(
       const int64_t r = index[v];
       const int64_t e = sorted_sel[v];
       m.src = idx_div(r, div) * src_ld;
-      m.dst = (pad_start[e] + v - seg_begin(offsets, e)) * cols;
+      const int64_t row = pad_start[e] + v - seg_begin(offsets, e);
+      m.dst = row * cols;
+      if (route_rows) route_rows[r] = (int32_t)row;
       if (scale) m.scale = round_to(load_as_float(scale, scale_dtype, r), dst_dtype);
     } else if (v < total) {
       const int64_t e = (v - n_routes) / kPadRows, i = (v - n_routes) % kPadRows;
@@ -413,7 +415,7 @@ __global__ void __launch_bounds__(256) sort_rows_wide_kernel(
     const char* __restrict__ src, int64_t src_ld, const int64_t* __restrict__ index, int64_t div,
     const void* __restrict__ scale, int scale_dtype, const int32_t* __restrict__ sorted_sel,
     const int64_t* __restrict__ offsets, const int* __restrict__ pad_start, int64_t n_routes, int64_t n_experts,
-    int64_t cols, char* __restrict__ dst, int dtype) {
+    int64_t cols, char* __restrict__ dst, int dtype, int32_t* __restrict__ route_rows) {
   pdl_enter();
   const int lane = threadIdx.x & 31;
   const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -425,7 +427,9 @@ __global__ void __launch_bounds__(256) sort_rows_wide_kernel(
       const int64_t r = index[v];
       const int64_t e = sorted_sel[v];
       m.src = idx_div(r, div) * src_ld;
-      m.dst = (pad_start[e] + v - seg_begin(offsets, e)) * cols;
+      const int64_t row = pad_start[e] + v - seg_begin(offsets, e);
+      m.dst = row * cols;
+      if (route_rows) route_rows[r] = (int32_t)row;
       if (MODE == 3) m.scale = round_to(load_as_float(scale, scale_dtype, r), dtype);
     } else if (v < total) {
       const int64_t e = (v - n_routes) / kPadRows, i = (v - n_routes) % kPadRows;
@@ -471,7 +475,7 @@ __global__ void __launch_bounds__(256) sort_rows_wide_kernel(
 int sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64_t* index, int64_t div,
                      const void* scale, int scale_dtype, const int32_t* sorted_sel, const int64_t* offsets,
                      const int* pad_start, int64_t n_routes, int64_t n_experts, int64_t cols, void* dst,
-                     int dst_dtype, cudaStream_t stream) {
+                     int dst_dtype, cudaStream_t stream, int32_t* route_rows) {
   const int ssz = dtype_bytes(src_dtype), dsz = dtype_bytes(dst_dtype);
   const bool aligned = ((cols * ssz) % 16 == 0) && ((src_ld * ssz) % 16 == 0) && ((cols * dsz) % 16 == 0) &&
                        (((uintptr_t)src & 15u) == 0) && (((uintptr_t)dst & 15u) == 0) && cols % 8 == 0;
@@ -486,15 +490,15 @@ int sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const int64
 #define CVMM_SORT_LAUNCH(MODE, ROWS)                                                                              \
   launch(sort_rows_padded_kernel<MODE, ROWS>, grid, 256, 0, stream, s, src_dtype, src_ld, index, div, scale,        \
                                                                 scale_dtype, sorted_sel, offsets, pad_start,      \
-                                                                n_routes, n_experts, cols, d, dst_dtype)
+                                                                n_routes, n_experts, cols, d, dst_dtype, route_rows)
   const bool wide = (mode == 0 || mode == 3) && src_dtype != F32 && cols * dsz >= 1024;
   const unsigned wgrid = (unsigned)std::min<int64_t>((rows + 7) / 8, 148 * 8);
   if (wide && mode == 0)
     launch(sort_rows_wide_kernel<0>, wgrid, 256, 0, stream, s, src_ld, index, div, scale, scale_dtype, sorted_sel,
-                                                        offsets, pad_start, n_routes, n_experts, cols, d, dst_dtype);
+                                                        offsets, pad_start, n_routes, n_experts, cols, d, dst_dtype, route_rows);
   else if (wide)
     launch(sort_rows_wide_kernel<3>, wgrid, 256, 0, stream, s, src_ld, index, div, scale, scale_dtype, sorted_sel,
-                                                        offsets, pad_start, n_routes, n_experts, cols, d, dst_dtype);
+                                                        offsets, pad_start, n_routes, n_experts, cols, d, dst_dtype, route_rows);
   else if (mode == 0 && short_rows) CVMM_SORT_LAUNCH(0, 128);
   else if (mode == 0) CVMM_SORT_LAUNCH(0, 32);
   else if (mode == 3 && short_rows) CVMM_SORT_LAUNCH(3, 128);

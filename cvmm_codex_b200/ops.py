@@ -19,7 +19,7 @@ from ._lib import check, dtype_code, ptr
 KERNELS_PER_CALL = {
     "cvmm_sel_prepare": 1, "cvmm_expert_offsets": 1, "cvmm_forward": 2, "cvmm_backward_x": 2,
     "cvmm_backward_w": 4, "cvmm_weighted_combine": 1, "cvmm_sum_routes": 1,
-    "cvmm_weighted_token_backward": 1, "cvmm_cast": 1, "cvmm_sort_rows_padded": 2, "cvmm_pad_starts": 1,
+    "cvmm_weighted_token_backward": 1, "cvmm_cast": 1, "cvmm_sort_rows_padded": 2, "cvmm_sort_rows_padded_ex": 2, "cvmm_pad_starts": 1,
     "cvmm_forward_gelu": 1, "cvmm_gelu_backward": 1, "cvmm_router_topk": 1, "cvmm_padded_route_rows": 1,
 }
 
@@ -323,12 +323,17 @@ def pad_starts(offsets: torch.Tensor, n_experts: int) -> torch.Tensor:
 
 def sort_rows_padded(src: torch.Tensor, index: torch.Tensor, div: int, sorted_sel: torch.Tensor,
                      offsets: torch.Tensor, n_experts: int, dtype: Optional[torch.dtype] = None,
-                     scale: Optional[torch.Tensor] = None):
+                     scale: Optional[torch.Tensor] = None, route_rows: bool = False,
+                     pad_start: Optional[torch.Tensor] = None):
     """Expert-padded sorted copy of route rows (the reference's grouping copy,
     cvmm.py:338-360), rounded to `dtype` (default: src's) and, with `scale`,
     multiplied by the op-rounded scale[index[p]] and rounded again (cvmm.py:591-599).
-    Returns (dst [n_routes + n_experts*PAD_ROWS, cols], pad_start int32 [E])."""
-    _require_cuda(src, index, sorted_sel, offsets, scale)
+    Returns (dst [n_routes + n_experts*PAD_ROWS, cols], pad_start int32 [E]).
+    pad_start: the pad starts of these offsets, already made (by pad_starts or an
+    earlier copy over the same selector); they are read, not recomputed.
+    route_rows: also return the int32 [n_routes] map padded_route_rows would
+    make (route_rows[index[p]] = padded row of p), written by the same launch."""
+    _require_cuda(src, index, sorted_sel, offsets, scale, pad_start)
     lib = _lib.load()
     s2 = _rows(src)
     n_routes = index.numel()
@@ -339,14 +344,29 @@ def sort_rows_padded(src: torch.Tensor, index: torch.Tensor, div: int, sorted_se
     dtype = s2.dtype if dtype is None else dtype
     sc = None if scale is None else scale.reshape(-1).contiguous()
     dst = torch.empty((n_routes + int(n_experts) * PAD_ROWS, cols), dtype=dtype, device=s2.device)
-    pstart = torch.empty(int(n_experts), dtype=torch.int32, device=s2.device)
+    ready = pad_start is not None
+    if ready:
+        if pad_start.dtype != torch.int32 or pad_start.numel() != int(n_experts) or not pad_start.is_contiguous():
+            raise ValueError("sort_rows_padded: pad_start must be a contiguous int32 [n_experts] tensor")
+        pstart = pad_start
+    else:
+        pstart = torch.empty(int(n_experts), dtype=torch.int32, device=s2.device)
+    rows = torch.empty(n_routes, dtype=torch.int32, device=s2.device) if route_rows else None
     with _Device(s2.device) as stream:
-        rc = _invoke("cvmm_sort_rows_padded", lib.cvmm_sort_rows_padded, ptr(s2), dtype_code(s2.dtype), s2.stride(0),
-                     ptr(index), int(div), ptr(sc), dtype_code(sc.dtype) if sc is not None else 0,
-                     ptr(ss), ptr(offsets), n_routes, int(n_experts), cols,
-                     ptr(dst), dtype_code(dtype), ptr(pstart), stream)
-    check(rc, "cvmm_sort_rows_padded")
-    return dst, pstart
+        if ready or route_rows:
+            rc = _invoke("cvmm_sort_rows_padded_ex", lib.cvmm_sort_rows_padded_ex, ptr(s2), dtype_code(s2.dtype),
+                         s2.stride(0), ptr(index), int(div), ptr(sc), dtype_code(sc.dtype) if sc is not None else 0,
+                         ptr(ss), ptr(offsets), n_routes, int(n_experts), cols, ptr(dst), dtype_code(dtype),
+                         ptr(pstart), int(ready), ptr(rows), stream, kernels=1 if ready else 2)
+            name = "cvmm_sort_rows_padded_ex"
+        else:
+            rc = _invoke("cvmm_sort_rows_padded", lib.cvmm_sort_rows_padded, ptr(s2), dtype_code(s2.dtype),
+                         s2.stride(0), ptr(index), int(div), ptr(sc), dtype_code(sc.dtype) if sc is not None else 0,
+                         ptr(ss), ptr(offsets), n_routes, int(n_experts), cols,
+                         ptr(dst), dtype_code(dtype), ptr(pstart), stream)
+            name = "cvmm_sort_rows_padded"
+    check(rc, name)
+    return (dst, pstart, rows) if route_rows else (dst, pstart)
 
 
 def padded_route_rows(route: torch.Tensor, sorted_sel: torch.Tensor, offsets: torch.Tensor,

@@ -52,7 +52,7 @@ typedef struct CUstream_st* cvmm_stream_t; /* == cudaStream_t */
 #define CVMM_DEV_BAD_INDEX 2
 
 /* ABI version of this header; bumped on any signature change. */
-int cvmm_abi_version(void);  /* 8 */
+int cvmm_abi_version(void);  /* 9 */
 
 /* Caps the number of SMs the persistent tensor-core GEMMs launched from now on
  * may occupy (one CTA per SM, nearly all of its shared memory); 0 removes the
@@ -296,6 +296,17 @@ int cvmm_sort_rows_padded(const void* src, int src_dtype, int64_t src_ld, const 
                           const int32_t* sorted_sel, const int64_t* offsets, int64_t n_routes,
                           int64_t n_experts, int64_t cols, void* dst, int dst_dtype,
                           int32_t* pad_start, cvmm_stream_t stream);
+/* cvmm_sort_rows_padded with two additions, each saving a launch:
+ * pad_start_ready != 0: pad_start already holds the pad starts of these
+ * offsets (from cvmm_pad_starts or an earlier copy over the same selector)
+ * and is only read; route_rows != NULL: also writes
+ * route_rows[index[p]] = the padded row of sorted position p, the map
+ * cvmm_padded_route_rows makes (the row map of the k-sum, cvmm.py:1199-1223).
+ * Same copy as the reference's grouping copy (cvmm.py:338-360). */
+int cvmm_sort_rows_padded_ex(const void* src, int src_dtype, int64_t src_ld, const int64_t* index, int64_t div,
+                             const void* scale, int scale_dtype, const int32_t* sorted_sel, const int64_t* offsets,
+                             int64_t n_routes, int64_t n_experts, int64_t cols, void* dst, int dst_dtype,
+                             int32_t* pad_start, int pad_start_ready, int32_t* route_rows, cvmm_stream_t stream);
 
 /* Sum over the top-k routes of each token: out[t] = cast( sum_j src[t*top_k+j] ),
  * fp32 accumulate. Replaces grouped_x.view(..., top_k, d).sum(-2) (cvmm.py:1223). */

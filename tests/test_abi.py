@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(lib, name), name
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
     assert set(_lib.SIGNATURES) == set(declared_functions())
-    assert lib.cvmm_abi_version() == 8
+    assert lib.cvmm_abi_version() == 9
 
 
 def test_workspace_queries_need_no_device():
@@ -48,6 +48,7 @@ def test_workspace_queries_need_no_device():
     (lambda l: l.cvmm_backward_x(None, 2, 4, None, 1, None, None, 4, None, 2, 1, 4, 4, 0, 0, 0, None, 2, 4, 3, None, 0, None, 0, 0, 1, None, 2, None, None, None, 0, None), -1),
     (lambda l: l.cvmm_backward_w(None, 2, 4, None, 0, None, 2, 4, None, 1, None, 0, None, None, 4, 1, 4, 4, None, 2, None, None, None, 0, None), -1),
     (lambda l: l.cvmm_sort_rows_padded(None, 2, 4, None, 1, None, 0, None, None, 4, 2, 8, None, 2, None, None), -1),
+    (lambda l: l.cvmm_sort_rows_padded_ex(None, 2, 4, None, 1, None, 0, None, None, 4, 2, 8, None, 2, None, 1, None, None), -1),
     # padded sorted x needs a 16-bit op dtype; a workspace is required
     (lambda l: l.cvmm_forward(16, 2, 4, 8, 16, None, 16, 4, 16, 2, 1, 8, 8, 64, 8, 1, 16, 2, 8, 0, 16, None, None, None, 0, None), -1),
     (lambda l: l.cvmm_backward_w(16, 2, 8, None, 1, 16, 2, 8, None, 1, 16, 0, 16, 16, 4, 1, 8, 8, 16, 2, 16, 16, None, 0, None), -4),

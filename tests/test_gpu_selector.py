@@ -162,6 +162,38 @@ def test_sort_rows_padded_matches_oracle(src_dtype, dst_dtype, scaled, cols):
     np.testing.assert_array_equal(got, want)
 
 
+@pytest.mark.parametrize("cols,scaled", [(128, False), (136, True), (1024, False), (1024, True)])
+def test_sort_rows_padded_route_rows_matches_map_kernel(cols, scaled):
+    """cvmm_sort_rows_padded_ex: the same copy and pad starts as cvmm_sort_rows_padded, and a
+    route -> padded row map equal to cvmm_padded_route_rows' (the k-sum's row map), for the
+    short-row kernel (128, 136 columns) and the warp-per-row kernel (1024)."""
+    g = torch.Generator().manual_seed(5)
+    T, k, E = 1500, 4, 13
+    sel = torch.randint(0, E, (T, k), generator=g)
+    sel[:, 0] = 2  # a segment over several 128-row tiles
+    src = torch.randn(T * k, cols, generator=g).to(torch.bfloat16).cuda()
+    w = torch.rand(T * k, generator=g).cuda() if scaled else None
+    s = C.cvmm_prepare_sel2(sel.cuda())
+    offs = ops.expert_offsets(s.sel, E)
+    route = s.out_index
+    d0, p0 = ops.sort_rows_padded(src, route, 1, s.sel, offs, E, dtype=torch.bfloat16, scale=w)
+    d1, p1, rows = ops.sort_rows_padded(src, route, 1, s.sel, offs, E, dtype=torch.bfloat16, scale=w,
+                                        route_rows=True)
+    used = int(p0[-1].item()) + ((int((offs[-1] - offs[-2]).item()) + 127) // 128) * 128
+    assert torch.equal(p0, p1)
+    assert torch.equal(d0[:used], d1[:used])
+    want = ops.padded_route_rows(route, s.sel, offs, p0)
+    assert torch.equal(rows, want)
+    # every route's row holds that route's source row
+    assert torch.equal(d1[rows.long()], d0[want.long()])
+    if w is None:
+        assert torch.equal(d1[rows.long()], src)
+    # pad starts given, not recomputed: the same copy again
+    d2, p2 = ops.sort_rows_padded(src, route, 1, s.sel, offs, E, dtype=torch.bfloat16, scale=w, pad_start=p0)
+    assert p2 is p0
+    assert torch.equal(d2[:used], d0[:used])
+
+
 @pytest.mark.parametrize("x_dtype,d_in", [(torch.bfloat16, 256), (torch.float32, 136), (torch.bfloat16, 72)])
 def test_forward_x_copy_equals_sorted_copy(x_dtype, d_in):
     """The forward's store-back of the rows it gathers (x_copy) is the

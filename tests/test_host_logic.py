@@ -66,3 +66,18 @@ def test_expert_offsets_reference_formula_matches_oracle():
             s = np.sort(rng.integers(0, E, R)).astype(np.int32)
             got = C._cvmm_expert_offsets(torch.from_numpy(s), E)
             np.testing.assert_array_equal(got.numpy(), O.expert_offsets(s, E))
+
+
+def test_traced_call_layer_mirrors_ops_signatures():
+    """Every call api.CVMM makes through the custom-op layer takes the same
+    parameters as the ops.py function it forwards to (a keyword missing there
+    only shows up on a GPU)."""
+    import inspect
+
+    from cvmm_codex_b200 import _torch_ops, ops
+    for name, fn in vars(_torch_ops._Calls).items():
+        if name.startswith("_") or not callable(fn) or not hasattr(ops, name):
+            continue
+        want = list(inspect.signature(getattr(ops, name)).parameters)
+        got = [p for p in inspect.signature(fn).parameters if p != "self"]
+        assert got == want, f"_Calls.{name}{got} != ops.{name}{want}"
