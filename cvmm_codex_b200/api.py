@@ -253,12 +253,18 @@ class CVMM(torch.autograd.Function):
         if rph > 1:
             x_index = torch.div(sel_index, rph, rounding_mode="floor")
             oi = sel_index  # outputs stay route-indexed
-        xs = xpad = None
+        xs = xpad = x_route_rows = None
         if _sortable(x, op_dtype) and reduction_weight is not None:
             # Expert-sorted, 128-row padded op-dtype copy of the route rows of x:
             # the forward and the grad-W read it as dense tiles (the reference's
             # grouped-x copy, cvmm.py:1123-1138).
-            xs, xpad = ops.sort_rows_padded(x, sel_index, rph, sel, offsets, n_experts, dtype=op_dtype)
+            if out_index is None and rph == 1 and keys.shape[-1] % 8 == 0:
+                # x rows are the routes: the copy also writes the route -> padded
+                # row map the weighted combine reads.
+                xs, xpad, x_route_rows = ops.sort_rows_padded(x, sel_index, 1, sel, offsets, n_experts,
+                                                              dtype=op_dtype, route_rows=True)
+            else:
+                xs, xpad = ops.sort_rows_padded(x, sel_index, rph, sel, offsets, n_experts, dtype=op_dtype)
         a = x if xs is None else xs
         # fp32 op dtype (no autocast) over 16-bit x and keys (the reference's
         # bf16_params mode): every product of two 16-bit values is exact in
@@ -293,7 +299,8 @@ class CVMM(torch.autograd.Function):
                 # Route outputs stay in the padded sorted layout (dense TMA tile
                 # stores); the weighted combine gathers them per token.
                 out_pad = xpad
-                rows = ops.padded_route_rows(out_index if out_index is not None else sel_index, sel, offsets, xpad)
+                rows = x_route_rows if x_route_rows is not None else ops.padded_route_rows(
+                    out_index if out_index is not None else sel_index, sel, offsets, xpad)
             y = ops.forward(a, x_index, offsets, fwd_keys, oi, op_dtype, fwd_op, x_pad_start=xpad,
                             out_pad_start=out_pad)
             res = ops.weighted_combine(y, reduction_weight, op_dtype, y_rows=rows)
