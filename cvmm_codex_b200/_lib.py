@@ -59,6 +59,7 @@ SIGNATURES = {
     "cvmm_selftest_wait_timeout": (_I, [_L, _P]),
     "cvmm_weighted_token_backward": (_I, [_P, _I, _P, _I, _P, _I, _P, _I, _P, _L, _L, _L, _P]),
     "cvmm_cast": (_I, [_P, _I, _P, _I, _L, _P]),
+    "cvmm_cast_ahead": (_I, [_P, _I, _P, _I, _L, _P]),
     "cvmm_forward_gelu": (_I, [_P, _I, _L, _L, _P, _P, _P, _L, _P, _I, _L, _L, _L, _L, _L, _L,
                                _P, _P, _I, _L, _I, _P, _P, _S, _P]),
     "cvmm_gelu_backward": (_I, [_P, _P, _P, _I, _L, _P]),
@@ -90,7 +91,7 @@ def load():
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if lib.cvmm_abi_version() != 9:
+        if lib.cvmm_abi_version() != 10:
             raise CvmmLibraryError("libcvmm_sm100.so ABI version mismatch; rebuild it")
         _lib = lib
     return _lib

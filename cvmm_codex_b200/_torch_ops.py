@@ -309,10 +309,10 @@ class _Calls:
             return torch.ops.cvmm_b200.pad_starts(offsets, n_experts)
         return ops.pad_starts(offsets, n_experts)
 
-    def cast(self, src, dtype):
+    def cast(self, src, dtype, ahead=False):
         if self._tracing():
             return torch.ops.cvmm_b200.cast(src, dtype)
-        return ops.cast(src, dtype)
+        return ops.cast(src, dtype, ahead=ahead)
 
     def sort_rows_padded(self, src, index, div, sorted_sel, offsets, n_experts, dtype=None, scale=None,
                          route_rows=False, pad_start=None):

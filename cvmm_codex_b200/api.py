@@ -128,6 +128,9 @@ cvmm_forward_x_copy = os.environ.get("CVMM_B200_FORWARD_X_COPY", "1").lower() no
 # copy pass (warp-per-row gathers) and then reads it as dense tiles (True), instead
 # of writing it from its own cp.async gathers (False). Same results either way.
 cvmm_forward_sort_first = os.environ.get("CVMM_B200_FORWARD_SORT_FIRST", "0").lower() in ("1", "true", "yes", "on")
+# sm_100a engine knob: the keys cast loads the weights while the selector sort
+# queued before it still runs and writes after it (True), or starts after it (False).
+cvmm_cast_ahead = os.environ.get("CVMM_B200_CAST_AHEAD", "1").lower() not in ("0", "false", "no", "off")
 # sm_100a engine knob: in the bf16_params mode (bf16 x and keys, no autocast)
 # the unweighted backward runs on the bf16 tensor cores with the fp32 grad
 # split into two bf16 parts (True) instead of the fp32 SIMT GEMMs (False).
@@ -195,7 +198,9 @@ def _operand(keys: torch.Tensor, op_dtype: torch.dtype) -> torch.Tensor:
     forward (RNE, the same rounding) and reused by the backward."""
     if op_dtype == torch.float32 or keys.dtype == op_dtype:
         return keys
-    return ops.cast(keys, op_dtype)
+    # No kernel of this library writes the keys: the cast may overlap the
+    # selector kernels queued before it.
+    return ops.cast(keys, op_dtype, ahead=cvmm_cast_ahead)
 
 
 def _sortable(t: torch.Tensor, op_dtype: torch.dtype) -> bool:
@@ -243,8 +248,8 @@ class CVMM(torch.autograd.Function):
                 reduction_weight: Optional[torch.Tensor] = None):
         op_dtype = get_dtype()
         n_experts = keys.shape[0]
-        offsets = ops.expert_offsets(sel, n_experts)
         keys_op = _operand(keys, op_dtype)
+        offsets = ops.expert_offsets(sel, n_experts)
         # Routes per x row: 1, except for a route-indexed selector over an x
         # whose rows are shared by consecutive routes (SwitchHead: the 2 routes
         # of a head read that head's value row; see _routes_per_row).
@@ -521,8 +526,8 @@ class CVMMGelu(torch.autograd.Function):
     def forward(ctx, x, raw_sel, sel_index, sel, keys, out_index):
         op_dtype = get_dtype()
         n_experts = keys.shape[0]
-        offsets = ops.expert_offsets(sel, n_experts)
         keys_op = _operand(keys, op_dtype)
+        offsets = ops.expert_offsets(sel, n_experts)
         want_copy = _sortable(x, op_dtype)
         h, z, xs = ops.forward_gelu(x, sel_index, offsets, keys_op, out_index, op_dtype, x_copy=want_copy)
         ctx.save_for_backward(x, keys_op, raw_sel, sel, sel_index, out_index, None, offsets, xs, None, z)

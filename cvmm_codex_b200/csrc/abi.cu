@@ -394,6 +394,49 @@ __global__ void cast_f32_to_16_vec(const float4* __restrict__ src, uint4* __rest
   }
 }
 
+// The same cast with its first loads ahead of the previous kernel on the
+// stream: every thread loads its first kCastAhead groups of 8 fp32 values
+// into registers, then waits for the predecessor (pdl_wait) and only then
+// converts and stores. Reads of src may overlap the predecessor because no
+// kernel of this library writes src; writes wait, because dst may reuse
+// memory the predecessor still uses (stream-ordered allocation). Groups a
+// block touches are blockDim.x apart, so warp accesses stay coalesced.
+constexpr int kCastAhead = 4;
+__global__ void __launch_bounds__(256) cast_f32_to_16_ahead(const float4* __restrict__ src,
+                                                            uint4* __restrict__ dst, int d_dtype, int64_t n8) {
+  pdl_trigger();
+  const int64_t step = (int64_t)gridDim.x * blockDim.x * kCastAhead;
+  bool waited = false;
+  for (int64_t base = (int64_t)blockIdx.x * blockDim.x * kCastAhead + threadIdx.x; base < n8; base += step) {
+    float4 v[kCastAhead][2];
+#pragma unroll
+    for (int g = 0; g < kCastAhead; ++g) {
+      const int64_t i = base + (int64_t)g * blockDim.x;
+      if (i < n8) {
+        v[g][0] = src[2 * i];
+        v[g][1] = src[2 * i + 1];
+      }
+    }
+    if (!waited) {
+      pdl_wait();
+      waited = true;
+    }
+#pragma unroll
+    for (int g = 0; g < kCastAhead; ++g) {
+      const int64_t i = base + (int64_t)g * blockDim.x;
+      if (i < n8) {
+        uint4 o;
+        o.x = pack2(v[g][0].x, v[g][0].y, d_dtype);
+        o.y = pack2(v[g][0].z, v[g][0].w, d_dtype);
+        o.z = pack2(v[g][1].x, v[g][1].y, d_dtype);
+        o.w = pack2(v[g][1].z, v[g][1].w, d_dtype);
+        dst[i] = o;
+      }
+    }
+  }
+  if (!waited) pdl_wait();
+}
+
 static inline int grid_for(int64_t work, int threads) {
   int64_t g = (work + threads - 1) / threads;
   return (int)std::max<int64_t>(1, std::min<int64_t>(g, 148 * 16));
@@ -498,7 +541,7 @@ using namespace cvmm;
 // ================================================================== C ABI
 extern "C" {
 
-int cvmm_abi_version(void) { return 9; }
+int cvmm_abi_version(void) { return 10; }
 
 int cvmm_set_pdl(int enable) {
   const int prev = pdl_enabled() ? 1 : 0;
@@ -893,6 +936,18 @@ int cvmm_cast(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t 
     launch(cast_kernel, grid_for(n, 256), 256, 0, s, src, src_dtype, dst, dst_dtype, n);
   }
   return check_launch("cvmm_cast");
+}
+
+int cvmm_cast_ahead(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n, cvmm_stream_t stream) {
+  if (src_dtype == F32 && (dst_dtype == BF16 || dst_dtype == F16) && n > 0 && n % 8 == 0 && src && dst &&
+      al16(src) && al16(dst)) {
+    const int64_t per_block = 256 * kCastAhead;
+    const int grid = (int)std::min<int64_t>((n / 8 + per_block - 1) / per_block, 148 * 8);
+    launch(cast_f32_to_16_ahead, grid, 256, 0, reinterpret_cast<cudaStream_t>(stream),
+           static_cast<const float4*>(src), static_cast<uint4*>(dst), dst_dtype, n / 8);
+    return check_launch("cvmm_cast_ahead");
+  }
+  return cvmm_cast(src, src_dtype, dst, dst_dtype, n, stream);
 }
 
 }  // extern "C"

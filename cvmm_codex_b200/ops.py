@@ -408,14 +408,17 @@ def weighted_token_backward(route_grad: torch.Tensor, w: torch.Tensor, x: torch.
     return gx, gsel
 
 
-def cast(src: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
-    """Round-to-nearest-even dtype conversion on the device (e.g. fp32 keys -> bf16)."""
+def cast(src: torch.Tensor, dtype: torch.dtype, ahead: bool = False) -> torch.Tensor:
+    """Round-to-nearest-even dtype conversion on the device (e.g. fp32 keys -> bf16).
+    ahead: the cast's loads may overlap the previous kernel of this library on
+    the stream (cvmm_cast_ahead); only for a src none of this library's kernels write."""
     _require_cuda(src)
     lib = _lib.load()
     s = src.contiguous()
     out = torch.empty(s.shape, dtype=dtype, device=s.device)
+    fn = lib.cvmm_cast_ahead if ahead else lib.cvmm_cast
     with _Device(s.device) as stream:
-        rc = _invoke("cvmm_cast", lib.cvmm_cast, ptr(s), dtype_code(s.dtype), ptr(out), dtype_code(dtype), s.numel(), stream)
+        rc = _invoke("cvmm_cast", fn, ptr(s), dtype_code(s.dtype), ptr(out), dtype_code(dtype), s.numel(), stream)
     check(rc, "cvmm_cast")
     return out
 

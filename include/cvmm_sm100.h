@@ -52,7 +52,7 @@ typedef struct CUstream_st* cvmm_stream_t; /* == cudaStream_t */
 #define CVMM_DEV_BAD_INDEX 2
 
 /* ABI version of this header; bumped on any signature change. */
-int cvmm_abi_version(void);  /* 9 */
+int cvmm_abi_version(void);  /* 10 */
 
 /* Caps the number of SMs the persistent tensor-core GEMMs launched from now on
  * may occupy (one CTA per SM, nearly all of its shared memory); 0 removes the
@@ -338,6 +338,15 @@ int cvmm_weighted_token_backward(const void* route_grad, int rg_dtype, const voi
  * weights to a bf16 operand copy. Supports the float dtypes only. */
 int cvmm_cast(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n,
               cvmm_stream_t stream);
+/* cvmm_cast that may start while the previous kernel on the stream is still
+ * running (programmatic launch): it reads src at once, waits for that kernel,
+ * and only then writes dst, so every later kernel still sees the usual stream
+ * order. Use it only for a src that no kernel of this library enqueued
+ * earlier on the stream writes (expert weights updated by the caller's own
+ * kernels are fine: this library's kernels start only after those finish).
+ * It overlaps the reads of the keys cast with the selector sort. Same result as cvmm_cast
+ * (the reference's in-kernel weight cast, cvmm.py:202-204). */
+int cvmm_cast_ahead(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n, cvmm_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(lib, name), name
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
     assert set(_lib.SIGNATURES) == set(declared_functions())
-    assert lib.cvmm_abi_version() == 9
+    assert lib.cvmm_abi_version() == 10
 
 
 def test_workspace_queries_need_no_device():

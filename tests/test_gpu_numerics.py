@@ -335,3 +335,24 @@ def test_bf16_params_split_backward_matches_fp32_kernels(route_input, monkeypatc
     for name, a, e in (("out", out, eo), ("x_grad", gx, ex), ("keys_grad", gk, ek)):
         assert O.rel_max_err(_np(a), e) <= MAX_TOL["bfloat16"], name
         assert O.rel_rms_err(_np(a), e) <= RMS_TOL["bfloat16"], name
+
+
+@pytest.mark.parametrize("n", [8, 1000, 4104, 64 * 1024 * 128, 148 * 8 * 256 * 4 * 8 + 24])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_cast_ahead_matches_cast(n, dtype):
+    """cvmm_cast_ahead (loads overlap the previous kernel, stores wait for it) gives
+    cvmm_cast's result bit for bit, queued right behind a selector sort as in
+    CVMM.forward; sizes cover the single pass, the grid-stride loop and the
+    fallback for sizes that are not a multiple of 8."""
+    from cvmm_codex_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(3)
+    src = torch.randn(n, device="cuda", generator=g) * 3
+    sel = torch.randint(0, 64, (16384, 4), device="cuda", generator=g)
+    want = ops.cast(src, dtype)
+    for _ in range(2):
+        s = cvmm_prepare_sel2(sel)
+        got = ops.cast(src, dtype, ahead=True)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+        assert torch.equal(got, src.to(dtype))
+        del s
