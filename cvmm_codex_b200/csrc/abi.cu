@@ -581,8 +581,12 @@ int cvmm_sel_prepare(const void* sel, int sel_dtype, int64_t n_routes, int64_t t
                      int route_input, int32_t* raw_sel, int32_t* sorted_sel, int64_t* sel_index,
                      int64_t* out_index, void* workspace, size_t workspace_bytes,
                      cvmm_stream_t stream) {
+  // Tuning override (fewest routes per sort CTA) for measurements. It can
+  // only raise the default, so the workspace sized for the default suffices.
+  int64_t min_chunk = kSelMinChunk;
+  if (const char* ev = getenv("CVMM_B200_SEL_MIN_CHUNK")) min_chunk = std::max<int64_t>(kSelMinChunk, atoll(ev));
   return sel_prepare(sel, sel_dtype, n_routes, top_k, route_input, raw_sel, sorted_sel, sel_index,
-                     out_index, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+                     out_index, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), min_chunk);
 }
 
 int cvmm_expert_offsets(const int32_t* sorted_sel, int64_t n_routes, int64_t n_experts,
